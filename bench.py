@@ -1,0 +1,503 @@
+"""Benchmark of the paged-KV decode hot path on B200 (one JSON line on rank 0).
+
+Workload ("C3"): one decode step of a Qwen3-8B-shape model's KV
+path for a batch of 64 requests with ragged contexts uniform in [512, 8192]:
+for each of 36 layers, the slot-mapping index-copy of the step's 64 new K/V rows
+followed by paged GQA decode attention (32 query / 8 KV heads, head_dim 128, 16-token
+pages, bf16) over every request's whole context. Every layer has its own block
+tables of random, non-contiguous pages in one global pool (as the reference's engine
+lays out layers, src/plastic_infer/runtime/engine.py:501-507), so the ~41 GB of KV
+read per step is far larger than L2 and no flush is needed. The model's projections
+and MLP are outside the path and not run.
+
+  value      decode tokens/s of the whole job (64 tokens per step), device time
+  e2e        same through the public API with pinned host inputs/outputs: per step
+             the H2D copy of q / new K,V / slot mapping / lengths and the D2H read of
+             the attention outputs are inside the timed region
+  roofline   the attention kernel: algorithmic bytes (context K/V + q + out + block
+             table) / its CUDA-event time, against the measured HBM copy bandwidth
+  index_copy C2 microbench (65536-page pool): GB/s at B = 1, 64, 512 and a large-B sweep
+  cpu_baseline the oracle (numpy port of the reference path) on a bounded sample
+
+`--impl reference` times the CPU reference path instead (rank 0 only).
+Multi-GPU (torchrun, N = 2/4/8): KV heads and their pools are split across ranks;
+each rank attends its heads and the per-layer outputs are all-gathered (NCCL) before
+o_proj would run; time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (Qwen3-8B shape, paged KV); index-copy GB/s vs HBM peak"
+C3 = dict(layers=36, batch=64, hq=32, hkv=8, head_dim=128, page_size=16, ctx_lo=512,
+          ctx_hi=8192, seed=0)
+C2 = dict(pages=65536, page_size=16, hkv=8, head_dim=128, batches=(1, 64, 512, 4096, 65536))
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return dict(hbm_gbs=float(d["hbm_gbs"]), source="measured")
+    return dict(hbm_gbs=6650.0, source="fallback")
+
+
+def c3_contexts(cfg: dict) -> np.ndarray:
+    rng = np.random.default_rng(cfg["seed"])
+    return rng.integers(cfg["ctx_lo"], cfg["ctx_hi"] + 1, size=cfg["batch"]).astype(np.int64)
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                rows.append(parts)
+        if not rows:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["unsampled"], samples=0)
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
+        return dict(sm_mhz=statistics.median(sm) if sm else None,
+                    sm_max_mhz=float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None,
+                    reasons=reasons, samples=len(rows))
+
+
+# ---------------------------------------------------------------------------------
+# C3 decode step on the device
+# ---------------------------------------------------------------------------------
+
+
+class DecodeWorkload:
+    """Device state of one C3 decode step for this rank's KV-head shard."""
+
+    def __init__(self, cfg: dict, rank: int, world: int, dev: torch.device) -> None:
+        from plastic_infer_b200 import kernels
+
+        self.kernels = kernels
+        self.cfg = cfg
+        L, B, S, D = cfg["layers"], cfg["batch"], cfg["page_size"], cfg["head_dim"]
+        assert cfg["hkv"] % world == 0 and cfg["hq"] % world == 0
+        self.hkv = cfg["hkv"] // world
+        self.hq = cfg["hq"] // world
+        self.dev = dev
+        self.ctx = c3_contexts(cfg)
+        npg = (self.ctx + S - 1) // S
+        self.pages_per_layer = int(npg.sum())
+        self.total_pages = self.pages_per_layer * L
+        maxp = int(npg.max())
+        # Block tables: every layer draws its pages from one global random permutation
+        # (identical on every rank: page ids are replicated, pools are head-sharded).
+        rng = np.random.default_rng(cfg["seed"] + 1)
+        perm = rng.permutation(self.total_pages).astype(np.int32)
+        bt = np.zeros((L, B, maxp), np.int32)
+        cur = 0
+        for l in range(L):
+            for b in range(B):
+                bt[l, b, :npg[b]] = perm[cur:cur + npg[b]]
+                cur += npg[b]
+        self.block_tables = torch.from_numpy(bt).to(dev)
+        last = self.ctx - 1
+        slots = bt[np.arange(L)[:, None], np.arange(B)[None, :], last[None, :] // S] * S + last % S
+        self.slots_host = torch.from_numpy(slots.astype(np.int64)).pin_memory()
+        self.ctx_host = torch.from_numpy(self.ctx.astype(np.int32)).pin_memory()
+        self.slots = self.slots_host.to(dev)
+        self.ctx_lens = self.ctx_host.to(dev)
+        shape = (self.total_pages, self.hkv, S, D)
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        self.k_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        self.v_pool = torch.empty(shape, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        self.q = torch.randn((L, B, self.hq, D), dtype=torch.bfloat16, device=dev, generator=g)
+        self.k_new = torch.randn((L, B, self.hkv, D), dtype=torch.bfloat16, device=dev, generator=g)
+        self.v_new = torch.randn((L, B, self.hkv, D), dtype=torch.bfloat16, device=dev, generator=g)
+        self.out = torch.empty((L, B, self.hq, D), dtype=torch.bfloat16, device=dev)
+        self.ws = kernels.Workspace(dev)
+        self.world = world
+        self.gathered = None
+        if world > 1:
+            self.gathered = torch.empty((L, world, B, self.hq, D), dtype=torch.bfloat16, device=dev)
+
+    # algorithmic bytes of one attention launch (one layer) for this rank
+    def attn_bytes(self) -> float:
+        D, B = self.cfg["head_dim"], self.cfg["batch"]
+        kv = float(self.ctx.sum()) * self.hkv * D * 2 * 2
+        qo = 2.0 * B * self.hq * D * 2
+        tables = 4.0 * self.pages_per_layer + 4.0 * B
+        return kv + qo + tables
+
+    def copy_bytes(self) -> float:
+        # one index-copy launch: B tokens x (K+V) x (read + write) rows + slot ids
+        return float(self.cfg["batch"]) * (2 * 2 * self.hkv * self.cfg["head_dim"] * 2 + 8)
+
+    def layer(self, l: int, attention: bool = True, copy: bool = True) -> None:
+        k = self.kernels
+        if copy:
+            k.kv_index_copy(self.k_pool, self.v_pool, self.k_new[l], self.v_new[l], self.slots[l])
+        if attention:
+            k.paged_decode_attention(self.q[l], self.k_pool, self.v_pool, self.block_tables[l],
+                                     self.ctx_lens, out=self.out[l], workspace=self.ws)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.gathered[l], self.out[l])
+
+    def step(self, attention: bool = True, copy: bool = True) -> None:
+        for l in range(self.cfg["layers"]):
+            self.layer(l, attention, copy)
+
+
+def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
+    """Device ms for `steps` calls of fn, events on the launching stream."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
+def graph_of(fn, warm: int = 1) -> torch.cuda.CUDAGraph:
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def bench_index_copy(dev: torch.device, peak: float) -> dict:
+    """C2: scatter of B rows into a 65536-page bf16 pool; per-launch device time."""
+    from plastic_infer_b200 import kernels
+
+    P, S, H, D = C2["pages"], C2["page_size"], C2["hkv"], C2["head_dim"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    kp = torch.zeros((P, H, S, D), dtype=torch.bfloat16, device=dev)
+    vp = torch.zeros_like(kp)
+    res = {}
+    rng = np.random.default_rng(0)
+    perm = rng.permutation(P * S)
+    for B in C2["batches"]:
+        slots = torch.from_numpy(perm[:B].astype(np.int64)).to(dev)
+        kn = torch.randn((B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+        vn = torch.randn((B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+        reps = 200 if B <= 4096 else 20
+        fn = lambda: kernels.kv_index_copy(kp, vp, kn, vn, slots)  # noqa: E731
+        graph = graph_of(fn)
+        graph.replay()
+        ms = time_region(graph.replay, reps, torch.cuda.current_stream())
+        t = ms / reps * 1e-3
+        byts = 8200.0 * B
+        res[str(B)] = dict(us_per_launch=round(t * 1e6, 3), gbs=round(byts / t / 1e9, 1),
+                           frac_of_hbm=round(byts / t / 1e9 / peak, 3))
+    return res
+
+
+def cpu_baseline_sample(cfg: dict, layers_sample: int = 1, requests_sample: int = 4) -> dict:
+    """Oracle (numpy port of the reference path) on a bounded sample, scaled to a step."""
+    from oracle import paged_kv_oracle as orc
+
+    rng = np.random.default_rng(99)
+    ctx = c3_contexts(cfg)
+    S, D, Hq, Hkv = cfg["page_size"], cfg["head_dim"], cfg["hq"], cfg["hkv"]
+    idx = np.arange(requests_sample)
+    sub = ctx[idx]
+    npg = (sub + S - 1) // S
+    P = int(npg.sum())
+    kp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+    vp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+    perm = rng.permutation(P)
+    tables, cur = [], 0
+    for n in npg:
+        tables.append([int(x) for x in perm[cur:cur + n]])
+        cur += n
+    q = rng.standard_normal((len(sub), Hq, D), dtype=np.float32)
+    kn = rng.standard_normal((len(sub), Hkv, D), dtype=np.float32)
+    slots = np.array([orc.slot_of(t, int(c) - 1, S) for t, c in zip(tables, sub)])
+    t0 = time.perf_counter()
+    for _ in range(layers_sample):
+        orc.write_kv_slots(kp, vp, kn, kn, slots, S)
+        orc.paged_attention_decode(q, kp, vp, tables, sub, S)
+    dt = time.perf_counter() - t0
+    scale = (ctx.sum() / sub.sum()) * (cfg["layers"] / layers_sample)
+    step_s = dt * scale
+    return dict(value=round(cfg["batch"] / step_s, 3), unit="tok/s",
+                cores=_blas_threads(), kind="port",
+                sample=f"{layers_sample} layer x {requests_sample} of {cfg['batch']} requests "
+                       f"({int(sub.sum())} of {int(ctx.sum())} context tokens), fp32 numpy oracle, "
+                       f"scaled x{scale:.1f} to one {cfg['layers']}-layer step; {dt:.2f} s measured")
+
+
+def _blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    cfg = dict(C3)
+    for _ in range(args.warmup):
+        cpu_baseline_sample(cfg, 1, 2)
+    vals = [cpu_baseline_sample(cfg, 1, 4) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in vals)
+    cb = dict(vals[0])
+    cb["value"] = v
+    line = dict(metric=METRIC, value=v, unit="tok/s", impl="reference", n_gpus=world,
+                steps=args.steps, warmup=args.warmup, ms_per_step=round(cfg["batch"] / v * 1e3, 3),
+                higher_is_better=True, scaling="strong", vs_baseline=None, dtype="f32",
+                data="synthetic",
+                config=dict(workload="C3 qwen3-8b-shape paged decode KV path (36 layers x "
+                            "index-copy + paged attention), B=64, ctx U[512,8192]",
+                            global_batch=cfg["batch"], layers=cfg["layers"],
+                            parallelism="cpu reference (oracle port)"),
+                cpu_baseline=cb,
+                e2e=dict(value=v, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    peaks = measured_peaks()
+    cfg = dict(C3)
+    wl = DecodeWorkload(cfg, rank, world, dev)
+    stream = torch.cuda.current_stream()
+
+    # warm-up (also configures kernels before graph capture)
+    for _ in range(max(1, args.warmup)):
+        wl.step()
+    torch.cuda.synchronize()
+    use_graph = world == 1
+    step_fn = wl.step
+    if use_graph:
+        g_step = graph_of(wl.step)
+        step_fn = g_step.replay
+        for _ in range(args.warmup):
+            step_fn()
+
+    barrier(world)
+    with ClockSampler(local_rank) as clk:
+        ms = time_region(step_fn, args.steps, stream)
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+    ms_step = ms / args.steps
+    value = cfg["batch"] * args.steps / (ms * 1e-3)
+
+    # attention alone (dominant kernel), same stream, for the roofline
+    attn_fn = lambda: wl.step(attention=True, copy=False)  # noqa: E731
+    copy_fn = lambda: wl.step(attention=False, copy=True)  # noqa: E731
+    if use_graph:
+        ga, gc = graph_of(attn_fn), graph_of(copy_fn)
+        attn_fn, copy_fn = ga.replay, gc.replay
+    reps = max(2, args.steps)
+    attn_ms = time_region(attn_fn, reps, stream) / (reps * cfg["layers"])
+    copy_ms = time_region(copy_fn, reps, stream) / (reps * cfg["layers"])
+    attn_ms = max_over_ranks(attn_ms, world)
+    achieved = wl.attn_bytes() / (attn_ms * 1e-3) / 1e9
+
+    # e2e through the public API with pinned host buffers
+    e2e = None
+    if world == 1:
+        e2e = run_e2e(wl, args, stream)
+
+    idx = bench_index_copy(dev, peaks["hbm_gbs"]) if (world == 1 and not args.skip_c2) else None
+    cpu = cpu_baseline_sample(cfg) if (rank == 0 and world == 1 and not args.skip_cpu) else None
+
+    traffic = _profile_traffic()
+    if rank == 0:
+        line = dict(
+            metric=METRIC, value=round(value, 1), unit="tok/s", n_gpus=world, steps=args.steps,
+            warmup=args.warmup, ms_per_step=round(ms_step, 4), higher_is_better=True,
+            scaling="strong", vs_baseline=None, dtype="bf16", data="synthetic",
+            config=dict(workload="C3 qwen3-8b-shape paged decode KV path: 36 layers x "
+                        "(index-copy of 64 new K/V rows + paged GQA decode attention), "
+                        "B=64, ctx U[512,8192] seed 0, 32q/8kv heads, head_dim 128, page 16",
+                        global_batch=cfg["batch"], layers=cfg["layers"], seq_len="ragged 512-8192",
+                        parallelism=f"kv-head shard x{world}" if world > 1 else "single gpu",
+                        kv_bytes_per_step=round(wl.attn_bytes() * cfg["layers"] * world / 1e9, 3),
+                        l2="inputs larger than L2 (~41 GB KV per step), no flush",
+                        cuda_graph=use_graph),
+            roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm_gbs"],
+                          unit="GB/s", frac=round(achieved / peaks["hbm_gbs"], 4),
+                          traffic=traffic, kernel="paged_decode_attn_tma_kernel<bf16,128,16>",
+                          us_per_launch=round(attn_ms * 1e3, 2),
+                          algorithmic_bytes_per_launch=int(wl.attn_bytes()),
+                          peak_source=peaks["source"]),
+            index_copy_in_step=dict(us_per_launch=round(copy_ms * 1e3, 2),
+                                    gbs=round(wl.copy_bytes() / (copy_ms * 1e-3) / 1e9, 1)),
+            gpu_launches=args.steps * cfg["layers"] * 2,
+            clocks=clk.summary(),
+        )
+        if e2e is not None:
+            line["e2e"] = e2e
+        if idx is not None:
+            line["index_copy"] = dict(workload="C2: 65536-page bf16 pool x 16 x 8 x 128, "
+                                      "random distinct slots", bytes_per_row=8200,
+                                      per_batch=idx, peak=peaks["hbm_gbs"])
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
+    """Whole step through the public API, inputs from pinned host memory each step."""
+    from plastic_infer_b200 import kernels
+
+    dev = wl.dev
+    q_h = wl.q.cpu().pin_memory()
+    kn_h = wl.k_new.cpu().pin_memory()
+    vn_h = wl.v_new.cpu().pin_memory()
+    out_h = torch.empty(wl.out.shape, dtype=wl.out.dtype, pin_memory=True)
+    q_d, kn_d, vn_d = torch.empty_like(wl.q), torch.empty_like(wl.k_new), torch.empty_like(wl.v_new)
+    slots_d = torch.empty_like(wl.slots)
+    ctx_d = torch.empty_like(wl.ctx_lens)
+    L = wl.cfg["layers"]
+
+    def step():
+        q_d.copy_(q_h, non_blocking=True)
+        kn_d.copy_(kn_h, non_blocking=True)
+        vn_d.copy_(vn_h, non_blocking=True)
+        slots_d.copy_(wl.slots_host, non_blocking=True)
+        ctx_d.copy_(wl.ctx_host, non_blocking=True)
+        for l in range(L):
+            kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
+            kernels.paged_decode_attention(q_d[l], wl.k_pool, wl.v_pool, wl.block_tables[l], ctx_d,
+                                           out=wl.out[l], workspace=wl.ws)
+        out_h.copy_(wl.out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    ms = time_region(step, args.steps, stream)
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, kn_h, vn_h, wl.slots_host, wl.ctx_host))
+    d2h = out_h.numel() * out_h.element_size()
+    return dict(value=round(wl.cfg["batch"] * args.steps / (ms * 1e-3), 1), unit="tok/s",
+                h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
+                ms_per_step=round(ms / args.steps, 4), api="plastic_infer_b200.kernels")
+
+
+def _profile_traffic():
+    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        try:
+            with open(path) as f:
+                return json.load(f).get("paged_decode_attn_c3_bytes_per_launch")
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-c2", action="store_true", help="skip the index-copy microbench")
+    ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

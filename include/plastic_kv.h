@@ -1,0 +1,166 @@
+/*
+ * plastic_kv.h — C ABI of the B200 (sm_100a) paged-KV decode hot path.
+ *
+ * The library (libplastic_kv.so) replaces three pure-PyTorch pieces of
+ * plastic-infer's paged decode path:
+ *   - the slot-mapping KV write        (src/plastic_infer/exec/runner_paged.py:112-129,
+ *                                        src/plastic_infer/kv/kv_store.py:124-145)
+ *   - paged GQA decode attention        (src/plastic_infer/exec/attention.py:103-190)
+ *   - page moves between the device pool and the host chunk store
+ *                                       (src/plastic_infer/kv/kv_store.py:230-334)
+ *
+ * Conventions
+ *   - Plain pointers and sizes only; every device pointer is a CUDA device
+ *     address owned by the caller (the library allocates nothing and keeps no
+ *     pointer after a call returns).
+ *   - Every function returns an int status: PI_OK (0) or a PI_ERR_* code.
+ *     Arguments are validated on the host before any launch; a call that
+ *     returns non-zero has launched nothing. (The reference's C entry point,
+ *     src/plastic_infer/kernel/fast_index_copy.py:110-117, returns void.)
+ *   - Kernels run on the caller's stream (`stream`, last argument), like the
+ *     reference's ctypes launch on torch's current stream
+ *     (src/plastic_infer/kernel/fast_index_copy.py:175-186).
+ *   - `err` (optional, may be NULL) is a device int the kernels set to a
+ *     PI_ERR_* code when they meet a bad index at run time (slot or page id out
+ *     of range); the offending access is skipped, never faulted.
+ *
+ * Physical pool layout (the one thing that differs from the reference):
+ *   K and V pools are each [num_pages, kv_heads, page_size, head_dim], i.e. the
+ *   reference's logical [num_pages, kv_heads, head_dim, page_size]
+ *   (src/plastic_infer/kv/kv_store.py:86-88) with the last two axes swapped in
+ *   memory. A (page, kv-head) tile is one contiguous page_size*head_dim block and
+ *   one token's row for one head is head_dim contiguous elements.
+ */
+#ifndef PLASTIC_KV_H_
+#define PLASTIC_KV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define PI_OK 0
+#define PI_ERR_NULL_POINTER 1
+#define PI_ERR_BAD_SHAPE 2
+#define PI_ERR_MISALIGNED 3
+#define PI_ERR_UNSUPPORTED 4
+#define PI_ERR_CUDA 5
+#define PI_ERR_WORKSPACE 6
+#define PI_ERR_SLOT_RANGE 7   /* device-side: slot >= num_slots (write skipped)    */
+#define PI_ERR_PAGE_RANGE 8   /* device-side: page id outside the pool (zero read)  */
+#define PI_ERR_TIMEOUT 9      /* device-side: a bounded wait gave up                */
+
+/* element types */
+#define PI_DTYPE_F32 0
+#define PI_DTYPE_BF16 1
+#define PI_DTYPE_F16 2
+
+/* Version of this ABI (bumped on any signature change). */
+int pi_abi_version(void);
+
+/* Static description of a status code. Never NULL. */
+const char* pi_error_string(int code);
+
+/*
+ * Slot-mapping KV write: for i in [0, n_tokens) with s = slot_mapping[i] >= 0,
+ *   k_pool[s / page_size, h, s % page_size, :] = k_new[i, h, :]   (all h)
+ *   v_pool[...]                                = v_new[i, h, :]
+ * A negative slot is padding and is skipped. Bit-exact element copy.
+ *
+ * Replaces the per-token Python loop of _write_kv_layer
+ * (src/plastic_infer/exec/runner_paged.py:123-129) and the per-layer write of
+ * KVRequestCache.append_token (src/plastic_infer/kv/kv_store.py:140-143); slot
+ * addressing follows BlockTable.get_page (src/plastic_infer/kv/paged.py:54-59):
+ * slot = page_id * page_size + offset.
+ *
+ *   k_new, v_new   [n_tokens, kv_heads, head_dim] with token stride
+ *                  `src_token_stride` elements (heads are contiguous rows)
+ *   slot_mapping   [n_tokens] int64, device
+ *   num_slots      num_pages * page_size (bound for slots)
+ */
+int pi_kv_index_copy(void* k_pool, void* v_pool, const void* k_new, const void* v_new,
+                     const int64_t* slot_mapping, int64_t n_tokens, int kv_heads, int head_dim,
+                     int page_size, int64_t num_slots, int dtype, int64_t src_token_stride,
+                     int* err, cudaStream_t stream);
+
+/*
+ * Bytes of device workspace pi_paged_decode_attn needs for this batch shape on
+ * the current device. The first `pi_paged_decode_attn_ws_zero_bytes` bytes of
+ * the workspace must be zero before the first call; the kernel leaves them zero
+ * again on exit, so one zero-fill at allocation time suffices.
+ */
+size_t pi_paged_decode_attn_workspace_bytes(int batch, int num_q_heads, int num_kv_heads,
+                                            int head_dim);
+size_t pi_paged_decode_attn_ws_zero_bytes(int batch, int num_kv_heads);
+
+/*
+ * Batched paged GQA decode attention, one query token per request:
+ *   out[b, hq, :] = softmax(scale * q[b, hq, :] . K_b[hq / G]^T) V_b[hq / G]
+ * over the first ctx_lens[b] tokens of request b, whose pages are
+ * block_tables[b, 0 .. ceil(ctx_lens[b] / page_size)), G = num_q_heads / num_kv_heads.
+ * fp32 softmax and accumulation; a request with ctx_lens[b] == 0 gets zeros.
+ *
+ * Replaces gather_paged_kv + repeat_interleave + scaled_dot_product_attention of
+ * paged_attention_v1 (src/plastic_infer/exec/attention.py:103-190) for Sq == 1,
+ * batched over requests (the reference calls it once per request through
+ * _attn_paged, src/plastic_infer/exec/runner_paged.py:36-59). GQA mapping
+ * hq -> hq // G as at attention.py:183-187; default scale 1/sqrt(head_dim) as SDPA.
+ *
+ *   q, out         [batch, num_q_heads, head_dim], row stride q_stride / out_stride
+ *                  elements between consecutive requests (dtype of the pools)
+ *   block_tables   [batch, bt_stride] int32 page ids, device
+ *   ctx_lens       [batch] int32, device
+ *   workspace      >= pi_paged_decode_attn_workspace_bytes(...) bytes, 256-B aligned
+ */
+int pi_paged_decode_attn(void* out, const void* q, const void* k_pool, const void* v_pool,
+                         const int32_t* block_tables, int64_t bt_stride, const int32_t* ctx_lens,
+                         int batch, int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                         int64_t num_pages, float scale, int dtype, int64_t q_stride,
+                         int64_t out_stride, void* workspace, size_t workspace_bytes, int* err,
+                         cudaStream_t stream);
+
+/*
+ * Contiguous gather of a request's pages in the reference's gather layout:
+ *   out[t, h, :] = pool[block_table[t / page_size], h, t % page_size, :]
+ * for t in [0, num_tokens). out is [num_tokens, kv_heads, head_dim].
+ * Replaces gather_paged_kv's index_select + permute + reshape
+ * (src/plastic_infer/exec/attention.py:133-148) for one pool.
+ */
+int pi_paged_kv_gather(void* out, const void* pool, const int32_t* block_table, int64_t num_tokens,
+                       int kv_heads, int head_dim, int page_size, int64_t num_pages, int dtype,
+                       int* err, cudaStream_t stream);
+
+/*
+ * Page gather (pool -> contiguous staging) and scatter (staging -> pool).
+ * Page i of the list (page id page_ids[i]) holds kv_heads tiles of `tile_bytes`
+ * bytes (tile_bytes = page_size * head_dim * elem). In the staging buffer, pages
+ * are grouped `pages_per_group` at a time and laid out head-major inside a group:
+ *   staging offset of (page i, head h) =
+ *       ((i / ppg) * kv_heads + h) * ppg * tile_bytes + (i % ppg) * tile_bytes
+ * With ppg = pages_per_chunk and groups = layers this is the host chunk layout
+ * [n_layers, kv_heads, tokens_per_chunk, head_dim], i.e. the reference's chunk
+ * [n_layers, kv_heads, head_dim, tokens_per_chunk]
+ * (src/plastic_infer/kv/kv_store.py:252-269) with its last two axes swapped.
+ * With ppg = 1 pages are simply concatenated.
+ * Replaces the per-page .to("cpu") / .to(device) loops of
+ * KVStore.sink_completed_chunks (src/plastic_infer/kv/kv_store.py:258-269) and
+ * KVStore.load_prefix (src/plastic_infer/kv/kv_store.py:311-321); the host<->device
+ * leg is one cudaMemcpyAsync of the staging buffer issued by the caller.
+ * Page ids outside [0, num_pages) are skipped and reported through `err`.
+ */
+int pi_page_gather(void* staging, const void* pool, const int32_t* page_ids, int64_t n_pages,
+                   int kv_heads, int64_t tile_bytes, int pages_per_group, int64_t num_pages,
+                   int* err, cudaStream_t stream);
+int pi_page_scatter(void* pool, const void* staging, const int32_t* page_ids, int64_t n_pages,
+                    int kv_heads, int64_t tile_bytes, int pages_per_group, int64_t num_pages,
+                    int* err, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PLASTIC_KV_H_ */

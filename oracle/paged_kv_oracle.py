@@ -1,0 +1,209 @@
+"""CPU oracle of plastic-infer's paged-KV decode hot path (numpy restatement).
+
+TEST INFRASTRUCTURE ONLY. This module is the parity checker: only tests/,
+__graft_entry__.smoke() and bench.py's CPU baseline / reference arm may import it.
+The product path (plastic_infer_b200) never calls it and has no CPU fallback.
+
+Every function restates the reference algorithm in plain numpy and cites the
+reference line it follows (paths relative to the plastic-infer project). The
+restatement is pinned against golden vectors produced by running the reference
+itself (tests/golden/make_golden.py; checked by tests/test_oracle_golden.py).
+
+Layouts are the reference's *logical* ones:
+  page pool  [num_pages, kv_heads, head_dim, page_size]   (src/plastic_infer/kv/kv_store.py:86-88)
+  host chunk [n_layers, kv_heads, head_dim, tokens_per_chunk] (src/plastic_infer/kv/kv_store.py:252-256)
+bf16 data is carried as uint16 bit patterns (numpy has no bfloat16), so byte copies
+stay bit-exact and arithmetic widens to float32 first.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+# ---------------------------------------------------------------------------
+# bf16 bit helpers
+# ---------------------------------------------------------------------------
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round float32 to bf16 (round-to-nearest-even), returned as uint16 bits.
+
+    Same rounding as torch's float32 -> bfloat16 conversion for finite values.
+    """
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rounding = ((u >> 16) & 1) + np.uint32(0x7FFF)
+    out = ((u + rounding) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out = np.where(nan, np.uint16(0x7FC0), out)
+    return out
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# a1: slot-mapping KV write
+# ---------------------------------------------------------------------------
+
+
+def slot_of(block_table_layer: list[int], token: int, page_size: int) -> int:
+    """Flat slot of a token: page id * page_size + offset.
+
+    BlockTable.get_page / get_page_for_token (src/plastic_infer/kv/paged.py:54-59)
+    and the page_idx/page_off arithmetic of _write_kv_layer
+    (src/plastic_infer/exec/runner_paged.py:124-127).
+    """
+    return block_table_layer[token // page_size] * page_size + token % page_size
+
+
+def write_kv_slots(k_pages: np.ndarray, v_pages: np.ndarray, k_new: np.ndarray,
+                   v_new: np.ndarray, slots: np.ndarray, page_size: int) -> None:
+    """In place: pool[slot // S, :, :, slot % S] = new[i] for each slot >= 0.
+
+    The per-token assignment of _write_kv_layer (src/plastic_infer/exec/runner_paged.py:128-129)
+    and KVRequestCache.append_token (src/plastic_infer/kv/kv_store.py:142-143), applied in
+    token order so a repeated slot keeps the last write. Negative slots are padding.
+    """
+    for i, s in enumerate(np.asarray(slots, dtype=np.int64)):
+        if s < 0:
+            continue
+        page, off = divmod(int(s), page_size)
+        k_pages[page, :, :, off] = k_new[i]
+        v_pages[page, :, :, off] = v_new[i]
+
+
+# ---------------------------------------------------------------------------
+# a2: paged decode attention
+# ---------------------------------------------------------------------------
+
+
+def gather_paged_kv(k_pages: np.ndarray, v_pages: np.ndarray, block_table: list[int],
+                    page_size: int, num_tokens: int | None = None):
+    """Contiguous [T, kv_heads, head_dim] K and V of one request.
+
+    gather_paged_kv (src/plastic_infer/exec/attention.py:103-148): index_select the
+    pages, permute [n, H, D, S] -> [n, S, H, D], flatten, trim to num_tokens.
+    """
+    H, D = k_pages.shape[1], k_pages.shape[2]
+    if len(block_table) == 0:
+        e = np.zeros((0, H, D), dtype=k_pages.dtype)
+        return e, e.copy()
+    ids = np.asarray(block_table, dtype=np.int64)
+    k = k_pages[ids].transpose(0, 3, 1, 2).reshape(len(ids) * page_size, H, D)
+    v = v_pages[ids].transpose(0, 3, 1, 2).reshape(len(ids) * page_size, H, D)
+    if num_tokens is not None:
+        k, v = k[:num_tokens], v[:num_tokens]
+    return k, v
+
+
+def paged_attention_decode(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray,
+                           block_tables: list[list[int]], ctx_lens, page_size: int,
+                           scale: float | None = None) -> np.ndarray:
+    """Batched single-token paged attention, fp32 arithmetic.
+
+    For each request b: gather its first ctx_lens[b] tokens (attention.py:133-146),
+    expand KV heads with query head h reading KV head h // G (attention.py:180-187),
+    then softmax(q . K^T * scale) V with scale = 1/sqrt(D) (the SDPA default used at
+    attention.py:189; causal masking is a no-op for one query token at the end of the
+    context, as in decode, runner_paged.py:254-255). A request with no context
+    yields zeros (SDPA over zero keys).
+
+    q: [B, Hq, D]; pools logical fp32 (bf16 inputs widened by the caller).
+    """
+    q = np.asarray(q, dtype=np.float32)
+    B, Hq, D = q.shape
+    Hkv = k_pages.shape[1]
+    G = Hq // Hkv
+    if scale is None:
+        scale = 1.0 / np.sqrt(D)
+    out = np.zeros((B, Hq, D), dtype=np.float32)
+    for b in range(B):
+        n = int(ctx_lens[b])
+        if n <= 0:
+            continue
+        npg = -(-n // page_size)
+        k, v = gather_paged_kv(k_pages, v_pages, list(block_tables[b][:npg]), page_size, n)
+        k = k.astype(np.float32)
+        v = v.astype(np.float32)
+        for h in range(Hkv):
+            qg = q[b, h * G:(h + 1) * G]                 # [G, D]
+            s = (qg @ k[:, h, :].T) * np.float32(scale)  # [G, n]
+            s = s - s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(axis=1, keepdims=True)
+            out[b, h * G:(h + 1) * G] = p @ v[:, h, :]
+    return out
+
+
+# ---------------------------------------------------------------------------
+# a3: page moves between the pool and host chunks
+# ---------------------------------------------------------------------------
+
+
+def sink_chunk(k_pages: np.ndarray, v_pages: np.ndarray, block_table: list[list[int]],
+               chunk_idx: int, page_size: int, pages_per_chunk: int):
+    """Host copy of one completed chunk, [L, H, D, page_size * pages_per_chunk].
+
+    KVStore.sink_completed_chunks (src/plastic_infer/kv/kv_store.py:250-269): for each
+    layer and each page of the chunk, k_chunk[layer, :, :, t0:t1] = k_pages[phys].
+    Pages missing from a layer's table stay zero (kv_store.py:261-262).
+    """
+    L = len(block_table)
+    H, D = k_pages.shape[1], k_pages.shape[2]
+    T = page_size * pages_per_chunk
+    kc = np.zeros((L, H, D, T), dtype=k_pages.dtype)
+    vc = np.zeros((L, H, D, T), dtype=v_pages.dtype)
+    start = chunk_idx * pages_per_chunk
+    for layer in range(L):
+        for j in range(pages_per_chunk):
+            lp = start + j
+            if lp >= len(block_table[layer]):
+                continue
+            phys = block_table[layer][lp]
+            kc[layer, :, :, j * page_size:(j + 1) * page_size] = k_pages[phys]
+            vc[layer, :, :, j * page_size:(j + 1) * page_size] = v_pages[phys]
+    return kc, vc
+
+
+def load_chunk(k_pages: np.ndarray, v_pages: np.ndarray, k_chunk: np.ndarray,
+               v_chunk: np.ndarray, phys_pages: list[list[int]], page_size: int) -> None:
+    """In place: pool[phys_pages[l][j]] = chunk[l, :, :, j*S:(j+1)*S].
+
+    KVStore.load_prefix's copy loop (src/plastic_infer/kv/kv_store.py:311-321).
+    """
+    for layer, pages in enumerate(phys_pages):
+        for j, phys in enumerate(pages):
+            k_pages[phys] = k_chunk[layer, :, :, j * page_size:(j + 1) * page_size]
+            v_pages[phys] = v_chunk[layer, :, :, j * page_size:(j + 1) * page_size]
+
+
+# ---------------------------------------------------------------------------
+# chunk keys (host-store addressing)
+# ---------------------------------------------------------------------------
+
+INITIAL_SALT = b"plastic-infer-kv-v1"
+
+
+def chunk_keys(tokens: list[int], chunk_size: int) -> list[tuple[bytes, bytes]]:
+    """(prefix_key, cumulative_key) per chunk.
+
+    _compute_hashes (src/plastic_infer/kv/chunk.py:80-111): h0 = sha256(salt);
+    c_i = sha256 of the chunk's tokens as 4-byte little-endian unsigned ints;
+    h_{i+1} = sha256(h_i || c_i).
+    """
+    if len(tokens) % chunk_size:
+        raise ValueError("token count not aligned to chunk_size")
+    running = hashlib.sha256(INITIAL_SALT).digest()
+    keys = []
+    for c in range(len(tokens) // chunk_size):
+        ch = hashlib.sha256(
+            b"".join(int(t).to_bytes(4, "little", signed=False)
+                     for t in tokens[c * chunk_size:(c + 1) * chunk_size])).digest()
+        cum = hashlib.sha256(running + ch).digest()
+        keys.append((running, cum))
+        running = cum
+    return keys

@@ -1,0 +1,115 @@
+"""ctypes binding of libplastic_kv.so (declared in include/plastic_kv.h).
+
+Mirrors the reference's ctypes binding idiom (src/plastic_infer/kernel/jit.py:87-124,
+src/plastic_infer/kernel/fast_index_copy.py:88-186): plain pointers, sizes and the
+caller's CUDA stream handle. Unlike the reference, every entry point returns a
+status that is turned into an exception here.
+
+There is no fallback: if the library is missing or cannot be loaded, every kernel
+call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from . import _build
+
+PI_OK = 0
+PI_ERR_NULL_POINTER = 1
+PI_ERR_BAD_SHAPE = 2
+PI_ERR_MISALIGNED = 3
+PI_ERR_UNSUPPORTED = 4
+PI_ERR_CUDA = 5
+PI_ERR_WORKSPACE = 6
+PI_ERR_SLOT_RANGE = 7
+PI_ERR_PAGE_RANGE = 8
+PI_ERR_TIMEOUT = 9
+
+PI_DTYPE_F32 = 0
+PI_DTYPE_BF16 = 1
+PI_DTYPE_F16 = 2
+
+ABI_VERSION = 1
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_sz = ctypes.c_size_t
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); the one table of what the header declares.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "pi_abi_version": (_i32, []),
+    "pi_error_string": (ctypes.c_char_p, [_i32]),
+    "pi_kv_index_copy": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _i64, _vp, _vp],
+    ),
+    "pi_paged_decode_attn_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
+    "pi_paged_decode_attn_ws_zero_bytes": (_sz, [_i32, _i32]),
+    "pi_paged_decode_attn": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
+         _i64, _i64, _vp, _sz, _vp, _vp],
+    ),
+    "pi_paged_kv_gather": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _vp, _vp]),
+    "pi_page_gather": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _i32, _i64, _vp, _vp]),
+    "pi_page_scatter": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _i32, _i64, _vp, _vp]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class KernelError(RuntimeError):
+    """A libplastic_kv entry point returned a non-zero status."""
+
+    def __init__(self, func: str, code: int, msg: str) -> None:
+        super().__init__(f"{func} failed with status {code}: {msg}")
+        self.code = code
+        self.func = func
+
+
+def lib_path() -> str:
+    return str(_build.LIB_PATH)
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library; raise if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not _build.LIB_PATH.exists():
+            raise RuntimeError(
+                f"{_build.LIB_PATH} is not built; run `python -m plastic_infer_b200._build` "
+                "(the paged-KV path has no CPU or PyTorch fallback)"
+            )
+        lib = ctypes.CDLL(str(_build.LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        ver = lib.pi_abi_version()
+        if ver != ABI_VERSION:
+            raise RuntimeError(f"libplastic_kv ABI {ver} != expected {ABI_VERSION}; rebuild")
+        _lib = lib
+        return lib
+
+
+def error_string(code: int) -> str:
+    return load().pi_error_string(code).decode()
+
+
+def check(func: str, code: int) -> None:
+    if code != PI_OK:
+        raise KernelError(func, code, error_string(code))
+
+
+def call(func: str, *args) -> None:
+    """Call a status-returning entry point and raise on failure."""
+    check(func, getattr(load(), func)(*args))

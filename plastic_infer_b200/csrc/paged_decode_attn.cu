@@ -1,0 +1,876 @@
+// Batched paged GQA decode attention for B200 (sm_100a).
+//
+// Reference behaviour (src/plastic_infer/exec/attention.py:103-190): for one request,
+// gather the block table's pages into a contiguous [T, Hkv, D] copy, repeat each KV
+// head G = Hq/Hkv times, and run scaled_dot_product_attention (scale 1/sqrt(D),
+// softmax over the first kv_num_tokens tokens). Query head hq reads KV head hq // G.
+// The decode caller (_attn_paged, src/plastic_infer/exec/runner_paged.py:36-59) passes
+// one query token and causal=False.
+//
+// This file computes the same thing for a whole batch in one launch, reading each KV
+// byte of the pool exactly once and never materialising the gather.
+//
+// Fast path (bf16/f16 pools, head_dim 64/128/256, page_size 16/32, G <= 8):
+//   * Work = the flattened stream of (request b, kv head h, page p) over all requests,
+//     cut into equal contiguous ranges, one per resident warp (persistent grid of
+//     SM-count x occupancy CTAs). Every warp reads the same number of pages, so the
+//     ragged contexts cost no tail imbalance.
+//   * Each warp owns a kStages-deep ring of (K tile, V tile) stages in shared memory.
+//     Lane 0 fills a stage with four 2-D TMA loads (128-byte swizzled boxes of
+//     [page_size rows x 64 elements]) completing on that stage's mbarrier; the warp
+//     refills a stage as soon as it has consumed it, so kStages pages per warp are
+//     always in flight. Page ids for the next 64 stream positions are prefetched
+//     into registers one block of 32 ahead.
+//   * Math per page on the tensor cores (mma.sync m16n8k16, f32 accumulate):
+//       S^T[tokens, heads] = K[tokens, D] . Q^T[D, heads]   (A = K via ldmatrix)
+//       O^T[D, heads]     += V^T[D, tokens] . P^T[tokens, heads]
+//     The G query heads of a KV head ride in the n=8 dimension, so one K/V tile feeds
+//     all of its query heads. The S^T accumulator is turned into the P^T operand with
+//     movmatrix.trans; the online softmax (base-2, fp32) needs only three xor-shuffles
+//     per page.
+//   * A (b, h) segment cut across warps leaves fp32 partials (m, l, O) in the
+//     workspace; the last warp to finish it (atomic counter) merges them and resets
+//     the counter, so there is no second launch and no spin-wait anywhere.
+//
+// Generic path (everything else, e.g. fp32 pools or odd head_dim/page_size): one CTA
+// per (request, query head), SIMT fp32, same semantics.
+#include <mutex>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "pi_common.cuh"
+
+namespace pi {
+namespace attn {
+
+constexpr int kWarps = 4;            // warps per CTA (each an independent consumer)
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxBatch = 4096;      // prefix table lives in shared memory
+constexpr int kMaxCtasPerSm = 2;     // workspace is sized for this many
+constexpr int kHeadsPad = 8;         // n dimension of the MMAs (query heads per KV head)
+constexpr unsigned kFull = 0xffffffffu;
+
+struct FastParams {
+  void* out;
+  const void* q;
+  const int32_t* block_tables;
+  const int32_t* ctx_lens;
+  int64_t bt_stride;
+  int64_t q_stride;
+  int64_t out_stride;
+  int64_t num_pages;
+  int batch;
+  int hkv;
+  int group;
+  float scale_log2;
+  int* ws_cnt;   // [batch * hkv] arrival counters (zero between launches)
+  float* ws_ml;  // [n_warps * 2][kHeadsPad][2] partial (max, sum)
+  float* ws_o;   // [n_warps * 2][kHeadsPad][D] partial unnormalised outputs
+  int* err;
+};
+
+template <int D, int S>
+struct Cfg {
+  static constexpr int kBoxes = D / 64;           // 128-byte column boxes per row
+  static constexpr int kBoxBytes = S * 128;       // one box: S rows x 128 B
+  static constexpr int kTileBytes = kBoxes * kBoxBytes;
+  static constexpr int kStageBytes = 2 * kTileBytes;  // K + V
+  static constexpr int kSub = S / 16;             // 16-token MMA sub-tiles per page
+  static constexpr int kMT = D / 16;              // QK k-steps == PV m-tiles
+};
+
+// Pipeline depth per warp: as many (K, V) page stages as fit in ~200 KB of shared
+// memory next to the batch prefix table, capped at 4 (4 x 8 KB per warp already keeps
+// ~2x the bytes in flight that HBM latency needs at D = 128, 16-token pages).
+template <int D, int S>
+constexpr int stages_for() {
+  constexpr int budget = 200 * 1024 - (kMaxBatch + 1) * 4 - 1024;
+  constexpr int n = budget / (kWarps * Cfg<D, S>::kStageBytes);
+  return n < 1 ? 1 : (n > 4 ? 4 : n);
+}
+
+template <int D, int S, int NS>
+constexpr size_t fast_smem_bytes() {
+  return 1024 /* alignment slack */ + static_cast<size_t>(kWarps) * NS * Cfg<D, S>::kStageBytes +
+         static_cast<size_t>(kWarps) * NS * 8 /* mbarriers */ + (kMaxBatch + 1) * 4;
+}
+
+// Byte offset of element (t, d) inside a swizzled [boxes][S][128 B] tile.
+template <int S>
+__device__ __forceinline__ uint32_t tile_off(int t, int d) {
+  return static_cast<uint32_t>((d >> 6) * (S * 128) + t * 128 + ((((d & 63) >> 3) ^ (t & 7)) << 4));
+}
+
+__device__ __forceinline__ int clamp_pages(int ctx, int S, int64_t bt_stride) {
+  const int c = ctx > 0 ? ctx : 0;
+  int64_t n = (static_cast<int64_t>(c) + S - 1) / S;
+  if (n > bt_stride) n = bt_stride;
+  return static_cast<int>(n);
+}
+
+template <typename T, int D, int S, int NS>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_decode_attn_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                                 const __grid_constant__ CUtensorMap tmap_v, const FastParams p) {
+  using C = Cfg<D, S>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + kWarps * NS * C::kStageBytes);
+  int* s_poff = reinterpret_cast<int*>(bars + kWarps * NS);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int B = p.batch;
+  const int Hkv = p.hkv;
+  const int G = p.group;
+
+  // ---- per-CTA exclusive prefix of page counts over the batch --------------------
+  {
+    const int per = (B + kThreads - 1) / kThreads;
+    const int beg = tid * per;
+    const int end = min(beg + per, B);
+    int local = 0;
+    for (int i = beg; i < end; ++i) local += clamp_pages(__ldg(p.ctx_lens + i), S, p.bt_stride);
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    __shared__ int warp_tot[kWarps];
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int base = 0;
+    for (int w = 0; w < warp; ++w) base += warp_tot[w];
+    int run = base + incl - local;
+    for (int i = beg; i < end; ++i) {
+      s_poff[i] = run;
+      run += clamp_pages(__ldg(p.ctx_lens + i), S, p.bt_stride);
+    }
+    if (tid == 0) {
+      int tot = 0;
+      for (int w = 0; w < kWarps; ++w) tot += warp_tot[w];
+      s_poff[B] = tot;
+    }
+  }
+  const uint32_t bar0 = smem_u32(bars + warp * NS);
+  if (lane == 0) {
+    for (int s = 0; s < NS; ++s) mbar_init(bar0 + 8 * s, 1);
+    fence_mbar_init();
+  }
+  if (tid == 0) {
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_v);
+  }
+  __syncthreads();
+
+  const int NW = gridDim.x * kWarps;
+  const int gw = blockIdx.x * kWarps + warp;
+  const int64_t total = static_cast<int64_t>(s_poff[B]) * Hkv;
+  const int hq = Hkv * G;
+
+  // Requests with no context produce zeros (SDPA over zero keys).
+  for (int b = gw; b < B; b += NW) {
+    if (s_poff[b + 1] == s_poff[b]) {
+      T* o = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride;
+      for (int i = lane; i < hq * D; i += 32) o[i] = from_f32<T>(0.f);
+    }
+  }
+
+  // Partition over at most `total` warps so every active warp owns >= 1 page: a
+  // segment's pieces are then exactly the warps [first, last] that overlap it.
+  const int NWe = static_cast<int>(total < NW ? total : NW);
+  if (gw >= NWe) return;
+  const int64_t lo = total * gw / NWe;
+  const int64_t hi = total * (gw + 1) / NWe;
+
+  // (b, h, page) of a stream position: largest b with s_poff[b] * Hkv <= pos.
+  auto locate = [&](int64_t pos, int& b, int& h, int& pg) {
+    int l = 0, r = B - 1;
+    while (l < r) {
+      const int mid = (l + r + 1) >> 1;
+      if (static_cast<int64_t>(s_poff[mid]) * Hkv <= pos) l = mid; else r = mid - 1;
+    }
+    b = l;
+    const int n = s_poff[l + 1] - s_poff[l];
+    const int64_t rem = pos - static_cast<int64_t>(s_poff[l]) * Hkv;
+    h = static_cast<int>(rem / n);
+    pg = static_cast<int>(rem - static_cast<int64_t>(h) * n);
+  };
+
+  // Tile index (page_id * Hkv + h) for stream position base + lane.
+  auto load_ids = [&](int64_t base) -> int {
+    const int64_t pos = base + lane;
+    if (pos >= hi) return 0;
+    int b, h, pg;
+    locate(pos, b, h, pg);
+    int pid = __ldg(p.block_tables + static_cast<int64_t>(b) * p.bt_stride + pg);
+    if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
+      record_error(p.err, PI_ERR_PAGE_RANGE);
+      pid = 0;
+    }
+    return pid * Hkv + h;
+  };
+
+  const uint32_t tiles_u32 = smem_u32(tiles) + warp * NS * C::kStageBytes;
+  int64_t pbase = lo;
+  int id_cur = load_ids(lo);
+  int id_nxt = load_ids(lo + 32);
+
+  auto issue = [&](int64_t pos, int stage) {
+    if (pos - pbase >= 32) {
+      pbase += 32;
+      id_cur = id_nxt;
+      id_nxt = load_ids(pbase + 32);
+    }
+    const int tile = __shfl_sync(kFull, id_cur, static_cast<int>(pos - pbase));
+    if (lane == 0) {
+      const uint32_t bar = bar0 + 8 * stage;
+      const uint32_t kdst = tiles_u32 + stage * C::kStageBytes;
+      const uint32_t vdst = kdst + C::kTileBytes;
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(bar, C::kStageBytes);
+#pragma unroll
+      for (int j = 0; j < C::kBoxes; ++j) {
+        tma_load_2d(kdst + j * C::kBoxBytes, &tmap_k, bar, 64 * j, tile * S);
+        tma_load_2d(vdst + j * C::kBoxBytes, &tmap_v, bar, 64 * j, tile * S);
+      }
+    }
+  };
+
+  int64_t issued = lo;
+  for (int s = 0; s < NS && issued < hi; ++s, ++issued) issue(issued, s);
+
+  // Lane-constant pieces of the fragment addressing.
+  const int gid = lane >> 2;   // row group (token for S^T, d for O^T)
+  const int tig = lane & 3;    // thread in group (head pair)
+  const int mi = lane >> 3;    // ldmatrix matrix this lane addresses
+  const int mr = lane & 7;     // row inside that matrix
+  // QK: A = K[t][d], t = mr + 8*(mi&1), d = 16*kk + 8*(mi>>1)
+  const int qk_t = mr + 8 * (mi & 1);
+  const int qk_d = 8 * (mi >> 1);
+  // PV: A = V^T, ldmatrix.trans over V[t][d], t = mr + 8*(mi>>1), d = 16*mt + 8*(mi&1)
+  const int pv_t = mr + 8 * (mi >> 1);
+  const int pv_d = 8 * (mi & 1);
+
+  using Mma = MmaOp<T>;
+  uint32_t qf[C::kMT][2];
+  float o[C::kMT][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  int cb, ch, cp;
+  locate(lo, cb, ch, cp);
+  int cn = s_poff[cb + 1] - s_poff[cb];
+  int cctx = min(max(__ldg(p.ctx_lens + cb), 0), cn * S);
+  int64_t piece_start = lo;
+  bool fresh = true;
+  bool failed = false;
+  int64_t pos = lo;
+  int k = 0;
+
+  auto first_warp_of = [&](int64_t s) -> int {
+    return static_cast<int>(((s + 1) * NWe - 1) / total);
+  };
+
+  auto finalize = [&](int64_t piece_end) {
+    float lt0 = l0, lt1 = l1;
+#pragma unroll
+    for (int x = 4; x < 32; x <<= 1) {
+      lt0 += __shfl_xor_sync(kFull, lt0, x);
+      lt1 += __shfl_xor_sync(kFull, lt1, x);
+    }
+    const int64_t seg_start = static_cast<int64_t>(s_poff[cb]) * Hkv + static_cast<int64_t>(ch) * cn;
+    const int64_t seg_end = seg_start + cn;
+    const int g0 = 2 * tig, g1 = 2 * tig + 1;
+    if (piece_start == seg_start && piece_end == seg_end) {
+      T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(cb) * p.out_stride +
+              static_cast<int64_t>(ch) * G * D;
+      const float i0 = lt0 > 0.f ? 1.f / lt0 : 0.f;
+      const float i1 = lt1 > 0.f ? 1.f / lt1 : 0.f;
+#pragma unroll
+      for (int mt = 0; mt < C::kMT; ++mt) {
+        const int d = 16 * mt + gid;
+        if (g0 < G) {
+          ob[g0 * D + d] = from_f32<T>(o[mt][0] * i0);
+          ob[g0 * D + d + 8] = from_f32<T>(o[mt][2] * i0);
+        }
+        if (g1 < G) {
+          ob[g1 * D + d] = from_f32<T>(o[mt][1] * i1);
+          ob[g1 * D + d + 8] = from_f32<T>(o[mt][3] * i1);
+        }
+      }
+      return;
+    }
+    // Partial piece: publish (m, l, O) and let the last arriving warp merge.
+    const int role = (piece_start == lo) ? 0 : 1;
+    const int64_t slot = static_cast<int64_t>(gw) * 2 + role;
+    float* wo = p.ws_o + slot * kHeadsPad * D;
+#pragma unroll
+    for (int mt = 0; mt < C::kMT; ++mt) {
+      const int d = 16 * mt + gid;
+      wo[g0 * D + d] = o[mt][0];
+      wo[g1 * D + d] = o[mt][1];
+      wo[g0 * D + d + 8] = o[mt][2];
+      wo[g1 * D + d + 8] = o[mt][3];
+    }
+    if (gid == 0) {
+      float* wml = p.ws_ml + slot * kHeadsPad * 2;
+      wml[g0 * 2 + 0] = m0;
+      wml[g0 * 2 + 1] = lt0;
+      wml[g1 * 2 + 0] = m1;
+      wml[g1 * 2 + 1] = lt1;
+    }
+    __threadfence();
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(p.ws_cnt + cb * Hkv + ch, 1);
+    old = __shfl_sync(kFull, old, 0);
+    const int wa = first_warp_of(seg_start);
+    const int wb = static_cast<int>((seg_end * NWe - 1) / total);
+    const int npieces = wb - wa + 1;
+    if (old != npieces - 1) return;
+    __threadfence();
+    const int role_a = (total * wa / NWe == seg_start) ? 0 : 1;
+    T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(cb) * p.out_stride +
+            static_cast<int64_t>(ch) * G * D;
+    for (int g = 0; g < G; ++g) {
+      float M = -INFINITY;
+      for (int j = 0; j < npieces; ++j) {
+        const int64_t sl = static_cast<int64_t>(wa + j) * 2 + (j == 0 ? role_a : 0);
+        M = fmaxf(M, __ldcg(p.ws_ml + sl * kHeadsPad * 2 + g * 2));
+      }
+      float L = 0.f;
+      float acc[D / 32];
+#pragma unroll
+      for (int e = 0; e < D / 32; ++e) acc[e] = 0.f;
+      for (int j = 0; j < npieces; ++j) {
+        const int64_t sl = static_cast<int64_t>(wa + j) * 2 + (j == 0 ? role_a : 0);
+        const float mj = __ldcg(p.ws_ml + sl * kHeadsPad * 2 + g * 2);
+        const float lj = __ldcg(p.ws_ml + sl * kHeadsPad * 2 + g * 2 + 1);
+        const float w = fast_exp2(mj - M);
+        L += w * lj;
+        const float* src = p.ws_o + sl * kHeadsPad * D + g * D;
+#pragma unroll
+        for (int e = 0; e < D / 32; ++e) acc[e] += w * __ldcg(src + lane + 32 * e);
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+      for (int e = 0; e < D / 32; ++e) ob[g * D + lane + 32 * e] = from_f32<T>(acc[e] * inv);
+    }
+    if (lane == 0) p.ws_cnt[cb * Hkv + ch] = 0;
+  };
+
+  while (pos < hi) {
+    if (fresh) {
+      // New (b, h) piece: load this KV head's G query rows as the MMA B operand.
+      const T* qb = static_cast<const T*>(p.q) + static_cast<int64_t>(cb) * p.q_stride +
+                    static_cast<int64_t>(ch) * G * D;
+#pragma unroll
+      for (int kk = 0; kk < C::kMT; ++kk) {
+        if (gid < G) {
+          const uint32_t* qr = reinterpret_cast<const uint32_t*>(qb + gid * D + 16 * kk + 2 * tig);
+          qf[kk][0] = __ldg(qr);
+          qf[kk][1] = __ldg(qr + 4);
+        } else {
+          qf[kk][0] = 0u;
+          qf[kk][1] = 0u;
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < C::kMT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+      piece_start = pos;
+      fresh = false;
+    }
+
+    const int stage = k % NS;
+    if (!mbar_wait_bounded(bar0 + 8 * stage, static_cast<uint32_t>((k / NS) & 1))) {
+      if (lane == 0) record_error(p.err, PI_ERR_TIMEOUT);
+      failed = true;
+      break;
+    }
+    const uint32_t ktile = tiles_u32 + stage * C::kStageBytes;
+    const uint32_t vtile = ktile + C::kTileBytes;
+    const int valid = min(S, cctx - cp * S);
+    if (valid < S) {
+      // Rows past the context may hold anything (even NaN); P is 0 there, and
+      // 0 * NaN would still poison O, so clear those V rows.
+      uint8_t* vt = tiles + (warp * NS + stage) * C::kStageBytes + C::kTileBytes;
+      const int nrow = S - valid;
+      for (int i = lane; i < C::kBoxes * nrow * 8; i += 32) {
+        const int j = i / (nrow * 8);
+        const int rem = i - j * nrow * 8;
+        const int row = valid + rem / 8;
+        const int c16 = rem & 7;
+        *reinterpret_cast<uint4*>(vt + j * C::kBoxBytes + row * 128 + c16 * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+
+    // S^T = K Q^T for each 16-token sub-tile.
+    float s[C::kSub][4];
+#pragma unroll
+    for (int u = 0; u < C::kSub; ++u) {
+      float ce[4] = {0.f, 0.f, 0.f, 0.f};
+      float co[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kk = 0; kk < C::kMT; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(ktile + tile_off<S>(16 * u + qk_t, 16 * kk + qk_d), a0, a1, a2, a3);
+        if (kk & 1) Mma::run(co, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+        else Mma::run(ce, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+      }
+      const int t0 = 16 * u + gid;
+      const int t1 = t0 + 8;
+      s[u][0] = t0 < valid ? (ce[0] + co[0]) * p.scale_log2 : -INFINITY;
+      s[u][1] = t0 < valid ? (ce[1] + co[1]) * p.scale_log2 : -INFINITY;
+      s[u][2] = t1 < valid ? (ce[2] + co[2]) * p.scale_log2 : -INFINITY;
+      s[u][3] = t1 < valid ? (ce[3] + co[3]) * p.scale_log2 : -INFINITY;
+    }
+
+    // Online softmax (base 2) for heads g0 = 2*tig and g1 = 2*tig + 1.
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < C::kSub; ++u) {
+      mx0 = fmaxf(mx0, fmaxf(s[u][0], s[u][2]));
+      mx1 = fmaxf(mx1, fmaxf(s[u][1], s[u][3]));
+    }
+#pragma unroll
+    for (int x = 4; x < 32; x <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, x));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, x));
+    }
+    const float mn0 = fmaxf(m0, mx0);
+    const float mn1 = fmaxf(m1, mx1);
+    const float al0 = fast_exp2(m0 - mn0);
+    const float al1 = fast_exp2(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    uint32_t pb[C::kSub][2];
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int u = 0; u < C::kSub; ++u) {
+      const float p0 = fast_exp2(s[u][0] - mn0);
+      const float p1 = fast_exp2(s[u][1] - mn1);
+      const float p2 = fast_exp2(s[u][2] - mn0);
+      const float p3 = fast_exp2(s[u][3] - mn1);
+      ps0 += p0 + p2;
+      ps1 += p1 + p3;
+      pb[u][0] = movmatrix_trans(Mma::pack(p0, p1));
+      pb[u][1] = movmatrix_trans(Mma::pack(p2, p3));
+    }
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+
+    // O^T = O^T * alpha + V^T P^T.
+#pragma unroll
+    for (int mt = 0; mt < C::kMT; ++mt) {
+      o[mt][0] *= al0;
+      o[mt][1] *= al1;
+      o[mt][2] *= al0;
+      o[mt][3] *= al1;
+#pragma unroll
+      for (int u = 0; u < C::kSub; ++u) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4_trans(vtile + tile_off<S>(16 * u + pv_t, 16 * mt + pv_d), a0, a1, a2, a3);
+        Mma::run(o[mt], a0, a1, a2, a3, pb[u][0], pb[u][1]);
+      }
+    }
+    __syncwarp();
+
+    // Refill the stage just consumed with the page NS positions ahead.
+    if (issued < hi) {
+      issue(issued, stage);
+      ++issued;
+    }
+    ++k;
+    ++pos;
+    if (++cp == cn) {
+      finalize(pos);
+      if (pos < hi) {
+        cp = 0;
+        if (++ch == Hkv) {
+          ch = 0;
+          do { ++cb; } while (cb < B && s_poff[cb + 1] == s_poff[cb]);
+        }
+        cn = s_poff[cb + 1] - s_poff[cb];
+        cctx = min(max(__ldg(p.ctx_lens + cb), 0), cn * S);
+        fresh = true;
+      }
+    } else if (pos == hi) {
+      finalize(pos);
+    }
+  }
+
+  if (failed) {
+    // Drain every load still in flight before the CTA's shared memory is released.
+    for (int64_t j = k; j < issued - lo; ++j) {
+      mbar_wait_bounded(bar0 + 8 * static_cast<int>(j % NS), static_cast<uint32_t>((j / NS) & 1));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Generic SIMT path: one CTA per (request, query head); 4 warps split the pages.
+// ---------------------------------------------------------------------------------
+
+struct SimtParams {
+  void* out;
+  const void* q;
+  const void* k_pool;
+  const void* v_pool;
+  const int32_t* block_tables;
+  const int32_t* ctx_lens;
+  int64_t bt_stride;
+  int64_t q_stride;
+  int64_t out_stride;
+  int64_t num_pages;
+  int hkv;
+  int group;
+  int head_dim;
+  int page_size;
+  float scale_log2;
+  int* err;
+};
+
+constexpr int kSimtMaxD = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(128) paged_decode_attn_simt_kernel(const SimtParams p) {
+  const int b = blockIdx.x;
+  const int hq = blockIdx.y;
+  const int h = hq / p.group;
+  const int D = p.head_dim;
+  const int S = p.page_size;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  __shared__ float q_s[kSimtMaxD];
+  __shared__ float w_m[4], w_l[4];
+  __shared__ float w_acc[4][kSimtMaxD];
+
+  const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.q_stride +
+                  static_cast<int64_t>(hq) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) q_s[d] = to_f32(qrow[d]) * p.scale_log2;
+  __syncthreads();
+
+  const int n_pages = clamp_pages(__ldg(p.ctx_lens + b), S, p.bt_stride);
+  const int ctx = min(max(__ldg(p.ctx_lens + b), 0), n_pages * S);
+  const T* K = static_cast<const T*>(p.k_pool);
+  const T* V = static_cast<const T*>(p.v_pool);
+
+  float m = -INFINITY, l = 0.f;
+  float acc[kSimtMaxD / 32];
+#pragma unroll
+  for (int e = 0; e < kSimtMaxD / 32; ++e) acc[e] = 0.f;
+
+  for (int pg = warp; pg < n_pages; pg += 4) {
+    int pid = __ldg(p.block_tables + static_cast<int64_t>(b) * p.bt_stride + pg);
+    if (pid < 0 || pid >= p.num_pages) {
+      if (lane == 0) record_error(p.err, PI_ERR_PAGE_RANGE);
+      continue;
+    }
+    const int64_t tile = (static_cast<int64_t>(pid) * p.hkv + h) * S * D;
+    for (int t0 = 0; t0 < S; t0 += 32) {
+      const int t = t0 + lane;
+      const bool ok = t < S && pg * S + t < ctx;
+      float sc = -INFINITY;
+      if (ok) {
+        const T* kr = K + tile + static_cast<int64_t>(t) * D;
+        float dot = 0.f;
+        for (int d = 0; d < D; ++d) dot += q_s[d] * to_f32(kr[d]);
+        sc = dot;
+      }
+      float mx = sc;
+#pragma unroll
+      for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, x));
+      const float mn = fmaxf(m, mx);
+      if (mn == -INFINITY) continue;  // whole chunk masked
+      const float al = fast_exp2(m - mn);
+      const float pt = ok ? fast_exp2(sc - mn) : 0.f;
+      float ps = pt;
+#pragma unroll
+      for (int x = 16; x > 0; x >>= 1) ps += __shfl_xor_sync(kFull, ps, x);
+      l = l * al + ps;
+      m = mn;
+#pragma unroll
+      for (int e = 0; e < kSimtMaxD / 32; ++e) acc[e] *= al;
+      const int nt = min(32, S - t0);
+      for (int tt = 0; tt < nt; ++tt) {
+        const float pv = __shfl_sync(kFull, pt, tt);
+        if (pg * S + t0 + tt >= ctx) break;
+        const T* vr = V + tile + static_cast<int64_t>(t0 + tt) * D;
+#pragma unroll
+        for (int e = 0; e < kSimtMaxD / 32; ++e) {
+          const int d = lane + 32 * e;
+          if (d < D) acc[e] += pv * to_f32(vr[d]);
+        }
+      }
+    }
+  }
+  if (lane == 0) {
+    w_m[warp] = m;
+    w_l[warp] = l;
+  }
+#pragma unroll
+  for (int e = 0; e < kSimtMaxD / 32; ++e) {
+    const int d = lane + 32 * e;
+    if (d < D) w_acc[warp][d] = acc[e];
+  }
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < 4; ++w) M = fmaxf(M, w_m[w]);
+  float L = 0.f;
+  float wt[4];
+  for (int w = 0; w < 4; ++w) {
+    wt[w] = (w_m[w] == -INFINITY) ? 0.f : fast_exp2(w_m[w] - M);
+    L += wt[w] * w_l[w];
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride +
+            static_cast<int64_t>(hq) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float v = 0.f;
+    for (int w = 0; w < 4; ++w) v += wt[w] * w_acc[w][d];
+    orow[d] = from_f32<T>(v * inv);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Host side: tensor-map cache, launch configuration, workspace layout.
+// ---------------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  uint64_t rows;
+  int d;
+  int s;
+  int dtype;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && d == o.d && s == o.s && dtype == o.dtype;
+  }
+};
+
+// Encoding a tensor map costs a driver call; decode steps reuse the same pools, so
+// keep a small cache keyed on (base, rows, head_dim, page_size, dtype).
+bool pool_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, int D, int S, int dtype) {
+  constexpr int kCache = 32;
+  static std::mutex mu;
+  static MapKey keys[kCache];
+  static CUtensorMap maps[kCache];
+  static int used = 0, next = 0;
+  const MapKey key{base, rows, D, S, dtype};
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i) {
+    if (keys[i] == key) {
+      *out = maps[i];
+      return true;
+    }
+  }
+  auto encode = get_encode();
+  if (!encode) return false;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(S)};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUtensorMapDataType dt =
+      dtype == PI_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = encode(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  const int slot = used < kCache ? used++ : (next++ % kCache);
+  keys[slot] = key;
+  maps[slot] = m;
+  *out = m;
+  return true;
+}
+
+struct Layout {
+  size_t cnt_off, ml_off, o_off, total;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+Layout ws_layout(int batch, int hkv, int head_dim, int sms) {
+  Layout L;
+  const size_t slots = static_cast<size_t>(sms) * kMaxCtasPerSm * kWarps * 2;
+  L.cnt_off = 0;
+  L.ml_off = align256(static_cast<size_t>(batch) * hkv * sizeof(int));
+  L.o_off = L.ml_off + align256(slots * kHeadsPad * 2 * sizeof(float));
+  L.total = L.o_off + align256(slots * kHeadsPad * static_cast<size_t>(head_dim) * sizeof(float));
+  return L;
+}
+
+template <typename T, int D, int S>
+int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, int64_t rows,
+                int dtype, cudaStream_t stream) {
+  constexpr int NS = stages_for<D, S>();
+  static_assert(fast_smem_bytes<D, S, NS>() <= 227 * 1024, "shared memory budget");
+  auto kern = paged_decode_attn_tma_kernel<T, D, S, NS>;
+  constexpr size_t smem = fast_smem_bytes<D, S, NS>();
+  static int configured_ctas[64] = {0};  // per device: CTAs per SM (0 = not yet)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PI_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return PI_ERR_UNSUPPORTED;
+  if (configured_ctas[dev] == 0) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return PI_ERR_CUDA;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess)
+      return PI_ERR_CUDA;
+    if (occ < 1) return PI_ERR_UNSUPPORTED;
+    configured_ctas[dev] = occ < kMaxCtasPerSm ? occ : kMaxCtasPerSm;
+  }
+  CUtensorMap tk, tv;
+  if (!pool_tensor_map(&tk, k_pool, static_cast<uint64_t>(rows), D, S, dtype) ||
+      !pool_tensor_map(&tv, v_pool, static_cast<uint64_t>(rows), D, S, dtype))
+    return PI_ERR_CUDA;
+  const unsigned grid = static_cast<unsigned>(device_sm_count() * configured_ctas[dev]);
+  kern<<<grid, kThreads, smem, stream>>>(tk, tv, fp);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace attn
+}  // namespace pi
+
+extern "C" size_t pi_paged_decode_attn_workspace_bytes(int batch, int num_q_heads,
+                                                       int num_kv_heads, int head_dim) {
+  (void)num_q_heads;
+  if (batch <= 0 || num_kv_heads <= 0 || head_dim <= 0) return 0;
+  return pi::attn::ws_layout(batch, num_kv_heads, head_dim, pi::device_sm_count()).total;
+}
+
+extern "C" size_t pi_paged_decode_attn_ws_zero_bytes(int batch, int num_kv_heads) {
+  if (batch <= 0 || num_kv_heads <= 0) return 0;
+  return pi::attn::align256(static_cast<size_t>(batch) * num_kv_heads * sizeof(int));
+}
+
+extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool,
+                                    const void* v_pool, const int32_t* block_tables,
+                                    int64_t bt_stride, const int32_t* ctx_lens, int batch,
+                                    int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                    int64_t num_pages, float scale, int dtype, int64_t q_stride,
+                                    int64_t out_stride, void* workspace, size_t workspace_bytes,
+                                    int* err, cudaStream_t stream) {
+  using namespace pi;
+  using namespace pi::attn;
+  const int eb = elem_bytes_of(dtype);
+  if (eb == 0) return PI_ERR_UNSUPPORTED;
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || page_size <= 0 ||
+      num_pages < 0 || bt_stride < 0)
+    return PI_ERR_BAD_SHAPE;
+  if (num_q_heads % num_kv_heads != 0) return PI_ERR_BAD_SHAPE;
+  const int64_t row = static_cast<int64_t>(num_q_heads) * head_dim;
+  if (q_stride < row || out_stride < row) return PI_ERR_BAD_SHAPE;
+  if (batch == 0) return PI_OK;
+  if (!out || !q || !k_pool || !v_pool || !block_tables || !ctx_lens) return PI_ERR_NULL_POINTER;
+  if (!aligned(block_tables, 4) || !aligned(ctx_lens, 4)) return PI_ERR_MISALIGNED;
+  const int group = num_q_heads / num_kv_heads;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const int64_t rows = num_pages * num_kv_heads * page_size;
+
+  const bool half_type = dtype == PI_DTYPE_BF16 || dtype == PI_DTYPE_F16;
+  const bool fast = half_type && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
+                    (page_size == 16 || page_size == 32) && group <= kHeadsPad &&
+                    batch <= kMaxBatch && rows > 0 && rows < (int64_t{1} << 31) &&
+                    static_cast<int64_t>(batch) * bt_stride < (int64_t{1} << 31) &&
+                    aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(q, 4) &&
+                    q_stride % 2 == 0 && aligned(out, 2);
+  if (fast) {
+    const Layout L = ws_layout(batch, num_kv_heads, head_dim, device_sm_count());
+    if (workspace == nullptr || workspace_bytes < L.total) return PI_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return PI_ERR_MISALIGNED;
+    FastParams fp;
+    fp.out = out;
+    fp.q = q;
+    fp.block_tables = block_tables;
+    fp.ctx_lens = ctx_lens;
+    fp.bt_stride = bt_stride;
+    fp.q_stride = q_stride;
+    fp.out_stride = out_stride;
+    fp.num_pages = num_pages;
+    fp.batch = batch;
+    fp.hkv = num_kv_heads;
+    fp.group = group;
+    fp.scale_log2 = scale_log2;
+    char* ws = static_cast<char*>(workspace);
+    fp.ws_cnt = reinterpret_cast<int*>(ws + L.cnt_off);
+    fp.ws_ml = reinterpret_cast<float*>(ws + L.ml_off);
+    fp.ws_o = reinterpret_cast<float*>(ws + L.o_off);
+    fp.err = err;
+#define PI_FAST(T, D, S)                                                                  \
+  if (head_dim == D && page_size == S)                                                    \
+    return launch_fast<T, D, S>(fp, k_pool, v_pool, rows, dtype, stream);
+    if (dtype == PI_DTYPE_BF16) {
+      PI_FAST(__nv_bfloat16, 64, 16)
+      PI_FAST(__nv_bfloat16, 128, 16)
+      PI_FAST(__nv_bfloat16, 256, 16)
+      PI_FAST(__nv_bfloat16, 64, 32)
+      PI_FAST(__nv_bfloat16, 128, 32)
+      PI_FAST(__nv_bfloat16, 256, 32)
+    } else {
+      PI_FAST(__half, 64, 16)
+      PI_FAST(__half, 128, 16)
+      PI_FAST(__half, 256, 16)
+      PI_FAST(__half, 64, 32)
+      PI_FAST(__half, 128, 32)
+      PI_FAST(__half, 256, 32)
+    }
+#undef PI_FAST
+    return PI_ERR_UNSUPPORTED;
+  }
+
+  // Generic SIMT path.
+  if (head_dim > kSimtMaxD) return PI_ERR_UNSUPPORTED;
+  if (batch > 65535 * 1024 || num_q_heads > 65535) return PI_ERR_UNSUPPORTED;
+  if (!aligned(q, eb) || !aligned(out, eb) || !aligned(k_pool, eb) || !aligned(v_pool, eb))
+    return PI_ERR_MISALIGNED;
+  SimtParams sp;
+  sp.out = out;
+  sp.q = q;
+  sp.k_pool = k_pool;
+  sp.v_pool = v_pool;
+  sp.block_tables = block_tables;
+  sp.ctx_lens = ctx_lens;
+  sp.bt_stride = bt_stride;
+  sp.q_stride = q_stride;
+  sp.out_stride = out_stride;
+  sp.num_pages = num_pages;
+  sp.hkv = num_kv_heads;
+  sp.group = group;
+  sp.head_dim = head_dim;
+  sp.page_size = page_size;
+  sp.scale_log2 = scale_log2;
+  sp.err = err;
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(num_q_heads));
+  if (dtype == PI_DTYPE_F32)
+    paged_decode_attn_simt_kernel<float><<<grid, 128, 0, stream>>>(sp);
+  else if (dtype == PI_DTYPE_BF16)
+    paged_decode_attn_simt_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(sp);
+  else
+    paged_decode_attn_simt_kernel<__half><<<grid, 128, 0, stream>>>(sp);
+  return cuda_status(cudaGetLastError());
+}

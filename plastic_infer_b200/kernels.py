@@ -1,0 +1,276 @@
+"""Tensor-level wrappers over the C ABI (the batched entry points of the hot path).
+
+These are the batched additions behind the reference's single-request API:
+
+  kv_index_copy          one launch writes a whole step's new K/V rows
+                         (reference: _write_kv_layer, src/plastic_infer/exec/runner_paged.py:112-129)
+  paged_decode_attention one launch attends every request of the batch
+                         (reference: paged_attention_v1, src/plastic_infer/exec/attention.py:151-190)
+  paged_kv_gather        contiguous gather of one request
+                         (reference: gather_paged_kv, src/plastic_infer/exec/attention.py:103-148)
+  page_gather / page_scatter
+                         pool <-> staging moves for the host store
+                         (reference: src/plastic_infer/kv/kv_store.py:258-269, 311-321)
+
+Pools are the *physical* tensors [num_pages, kv_heads, page_size, head_dim]. Every
+function launches on torch's current stream, as the reference's ctypes launch does
+(src/plastic_infer/kernel/fast_index_copy.py:185), and raises `KernelError` on a
+non-zero status. Inputs must be CUDA tensors; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import _capi
+
+_DTYPES = {
+    torch.float32: _capi.PI_DTYPE_F32,
+    torch.bfloat16: _capi.PI_DTYPE_BF16,
+    torch.float16: _capi.PI_DTYPE_F16,
+}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPES[dt]
+    except KeyError:
+        raise TypeError(f"unsupported KV dtype {dt}; expected float32, bfloat16 or float16")
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError(
+                "plastic_infer_b200 kernels need CUDA tensors (no CPU fallback); got "
+                f"{t.device}"
+            )
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _err_ptr(err: torch.Tensor | None) -> int | None:
+    if err is None:
+        return None
+    if err.dtype != torch.int32 or not err.is_cuda or err.numel() < 1:
+        raise ValueError("err must be a CUDA int32 tensor with at least one element")
+    return err.data_ptr()
+
+
+def _check_pool(pool: torch.Tensor, name: str) -> tuple[int, int, int, int]:
+    if pool.dim() != 4 or not pool.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous [num_pages, kv_heads, page_size, head_dim] tensor")
+    return tuple(pool.shape)  # type: ignore[return-value]
+
+
+# ---------------------------------------------------------------------------
+# a1: slot-mapping index-copy
+# ---------------------------------------------------------------------------
+
+
+def kv_index_copy(
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    err: torch.Tensor | None = None,
+) -> None:
+    """pool[slot // S, :, slot % S, :] = new[i] for every i with slot_mapping[i] >= 0.
+
+    k_new / v_new: [n, kv_heads, head_dim] (any token stride, heads contiguous) or
+    [1, n, kv_heads, head_dim] as produced by the reference runner.
+    slot_mapping: int64 [n] on the pool's device; slot = page_id * page_size + offset.
+    """
+    P, H, S, D = _check_pool(k_pool, "k_pool")
+    if v_pool.shape != k_pool.shape or v_pool.dtype != k_pool.dtype:
+        raise ValueError("k_pool and v_pool must have the same shape and dtype")
+    if k_new.dim() == 4:
+        k_new = k_new.reshape(-1, k_new.shape[-2], k_new.shape[-1])
+        v_new = v_new.reshape(-1, v_new.shape[-2], v_new.shape[-1])
+    if k_new.shape != v_new.shape or tuple(k_new.shape[1:]) != (H, D):
+        raise ValueError(f"k_new/v_new must be [n, {H}, {D}], got {tuple(k_new.shape)}")
+    if k_new.dtype != k_pool.dtype or v_new.dtype != k_pool.dtype:
+        raise TypeError("new K/V rows must have the pool dtype")
+    n = k_new.shape[0]
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (n,):
+        raise ValueError("slot_mapping must be int64 of shape [n]")
+    _require_cuda(k_pool, v_pool, k_new, v_new, slot_mapping)
+    if n == 0:
+        return
+    # Rows of one token must be [H, D] contiguous and K/V must share one token
+    # stride; tokens themselves may be strided (e.g. slices of a fused QKV output).
+    if not (k_new.stride(2) == 1 and k_new.stride(1) == D and v_new.stride() == k_new.stride()):
+        k_new = k_new.contiguous()
+        v_new = v_new.contiguous()
+    slot_mapping = slot_mapping.contiguous()
+    _capi.call(
+        "pi_kv_index_copy",
+        k_pool.data_ptr(), v_pool.data_ptr(), k_new.data_ptr(), v_new.data_ptr(),
+        slot_mapping.data_ptr(), n, H, D, S, P * S, dtype_code(k_pool.dtype), k_new.stride(0),
+        _err_ptr(err), _stream(),
+    )
+
+
+# ---------------------------------------------------------------------------
+# a2: paged decode attention
+# ---------------------------------------------------------------------------
+
+
+class Workspace:
+    """Zero-initialised device scratch for pi_paged_decode_attn, grown on demand.
+
+    The kernel leaves its counter region zero on exit, so the buffer is zeroed once
+    at allocation. Launches that share one Workspace must be ordered (same stream);
+    give concurrent streams their own Workspace.
+    """
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = torch.device(device)
+        self.buf: torch.Tensor | None = None
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes:
+            n = max(nbytes, 1 << 20)
+            self.buf = torch.zeros(n, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+_ws_lock = threading.Lock()
+_default_ws: dict[int, Workspace] = {}
+
+
+def default_workspace(device: torch.device) -> Workspace:
+    idx = torch.device(device).index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    with _ws_lock:
+        ws = _default_ws.get(idx)
+        if ws is None:
+            ws = _default_ws[idx] = Workspace(torch.device("cuda", idx))
+        return ws
+
+
+def workspace_bytes(batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int) -> int:
+    return int(_capi.load().pi_paged_decode_attn_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim))
+
+
+def paged_decode_attention(
+    q: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_tables: torch.Tensor,
+    ctx_lens: torch.Tensor,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    workspace: Workspace | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Decode attention of q [B, Hq, D] over each request's first ctx_lens[b] tokens.
+
+    block_tables: int32 [B, max_pages] page ids; ctx_lens: int32 [B]. Returns
+    out [B, Hq, D] in the pool dtype (fp32 softmax/accumulation inside).
+    """
+    P, Hkv, S, D = _check_pool(k_pool, "k_pool")
+    if v_pool.shape != k_pool.shape or v_pool.dtype != k_pool.dtype:
+        raise ValueError("k_pool and v_pool must have the same shape and dtype")
+    if q.dim() != 3 or q.shape[2] != D:
+        raise ValueError(f"q must be [B, Hq, {D}], got {tuple(q.shape)}")
+    B, Hq, _ = q.shape
+    if Hq % Hkv != 0:
+        raise ValueError(f"num_q_heads {Hq} not a multiple of num_kv_heads {Hkv}")
+    if q.dtype != k_pool.dtype:
+        raise TypeError("q must have the pool dtype")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.shape[0] != B:
+        raise ValueError("block_tables must be int32 [B, max_pages]")
+    if ctx_lens.dtype != torch.int32 or ctx_lens.shape != (B,):
+        raise ValueError("ctx_lens must be int32 [B]")
+    _require_cuda(q, k_pool, v_pool, block_tables, ctx_lens)
+    if q.stride(2) != 1 or q.stride(1) != D:
+        q = q.contiguous()
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    ctx_lens = ctx_lens.contiguous()
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
+    elif out.shape != (B, Hq, D) or out.dtype != q.dtype or out.stride(2) != 1 or out.stride(1) != D:
+        raise ValueError("out must be [B, Hq, D] with contiguous heads, pool dtype")
+    if B == 0:
+        return out
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    nbytes = workspace_bytes(B, Hq, Hkv, D)
+    ws = (workspace or default_workspace(q.device)).get(nbytes)
+    _capi.call(
+        "pi_paged_decode_attn",
+        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        block_tables.data_ptr(), block_tables.stride(0), ctx_lens.data_ptr(),
+        B, Hq, Hkv, D, S, P, float(scale), dtype_code(q.dtype), q.stride(0), out.stride(0),
+        ws.data_ptr(), ws.numel(), _err_ptr(err), _stream(),
+    )
+    return out
+
+
+# ---------------------------------------------------------------------------
+# gather_paged_kv and a3: page moves
+# ---------------------------------------------------------------------------
+
+
+def paged_kv_gather(pool: torch.Tensor, block_table: torch.Tensor, num_tokens: int,
+                    err: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t, h, :] = pool[block_table[t // S], h, t % S, :] -> [num_tokens, H, D]."""
+    P, H, S, D = _check_pool(pool, "pool")
+    if block_table.dtype != torch.int32 or block_table.dim() != 1:
+        raise ValueError("block_table must be int32 [n_pages]")
+    if num_tokens > block_table.numel() * S:
+        raise ValueError("num_tokens exceeds the block table's pages")
+    _require_cuda(pool, block_table)
+    out = torch.empty((num_tokens, H, D), dtype=pool.dtype, device=pool.device)
+    if num_tokens == 0:
+        return out
+    _capi.call(
+        "pi_paged_kv_gather",
+        out.data_ptr(), pool.data_ptr(), block_table.contiguous().data_ptr(), num_tokens, H, D, S,
+        P, dtype_code(pool.dtype), _err_ptr(err), _stream(),
+    )
+    return out
+
+
+def _page_move(func: str, pool: torch.Tensor, staging: torch.Tensor, page_ids: torch.Tensor,
+               pages_per_group: int, err: torch.Tensor | None) -> None:
+    P, H, S, D = _check_pool(pool, "pool")
+    if page_ids.dtype != torch.int32 or page_ids.dim() != 1:
+        raise ValueError("page_ids must be int32 [n]")
+    n = page_ids.numel()
+    tile_bytes = S * D * pool.element_size()
+    if not staging.is_contiguous() or staging.numel() * staging.element_size() < n * H * tile_bytes:
+        raise ValueError("staging must be contiguous and hold n * kv_heads * page_size * head_dim elements")
+    if pages_per_group <= 0 or n % pages_per_group != 0:
+        raise ValueError("page count must be a multiple of pages_per_group")
+    _require_cuda(pool, staging, page_ids)
+    if n == 0:
+        return
+    page_ids = page_ids.contiguous()
+    if func == "pi_page_gather":
+        args = (staging.data_ptr(), pool.data_ptr())
+    else:
+        args = (pool.data_ptr(), staging.data_ptr())
+    _capi.call(func, *args, page_ids.data_ptr(), n, H, tile_bytes, pages_per_group, P,
+               _err_ptr(err), _stream())
+
+
+def page_gather(pool: torch.Tensor, page_ids: torch.Tensor, staging: torch.Tensor,
+                pages_per_group: int = 1, err: torch.Tensor | None = None) -> None:
+    """staging <- pool pages, grouped head-major (see include/plastic_kv.h)."""
+    _page_move("pi_page_gather", pool, staging, page_ids, pages_per_group, err)
+
+
+def page_scatter(staging: torch.Tensor, page_ids: torch.Tensor, pool: torch.Tensor,
+                 pages_per_group: int = 1, err: torch.Tensor | None = None) -> None:
+    """pool pages <- staging (inverse of page_gather)."""
+    _page_move("pi_page_scatter", pool, staging, page_ids, pages_per_group, err)

@@ -1,0 +1,120 @@
+"""Deterministic synthetic inputs shared by the golden-vector generator and the tests.
+
+Golden files (tests/golden/*.npz) hold the reference's *outputs*; large inputs are
+regenerated here from their seed with numpy's PCG64 (stable across machines) and
+their checksum is stored beside the outputs so a generator change is caught.
+
+bf16 tensors are carried as uint16 bit patterns (see oracle.paged_kv_oracle).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from oracle.paged_kv_oracle import bf16_bits_to_f32, f32_to_bf16_bits
+
+# Attention parity cases: (name, seed, B, Hq, Hkv, D, S, num_pages, ctx_lens, dtype)
+ATTENTION_CASES = [
+    # C1 tiny shape (fp32): 4 ragged requests
+    dict(name="att_c1_f32", seed=101, B=4, Hq=4, Hkv=2, D=64, S=16, P=24,
+         ctx=[8, 23, 48, 64], dtype="f32"),
+    # Qwen3-8B head shape (bf16): single token, partial page, several pages
+    dict(name="att_8b_bf16", seed=102, B=3, Hq=32, Hkv=8, D=128, S=16, P=16,
+         ctx=[1, 17, 100], dtype="bf16"),
+    # Qwen3-30B-A3B head shape (bf16, G = 8)
+    dict(name="att_moe_bf16", seed=103, B=2, Hq=32, Hkv=4, D=128, S=16, P=12,
+         ctx=[33, 64], dtype="bf16"),
+    # head_dim 64 with 32-token pages
+    dict(name="att_d64_s32_bf16", seed=104, B=2, Hq=8, Hkv=2, D=64, S=32, P=8,
+         ctx=[40, 64], dtype="bf16"),
+    # the reference unit-test geometry: tiny head_dim, 3-token pages, MHA
+    dict(name="att_small_f32", seed=105, B=2, Hq=2, Hkv=2, D=8, S=3, P=5,
+         ctx=[9, 4], dtype="f32"),
+    # an empty request next to a non-empty one
+    dict(name="att_empty_bf16", seed=106, B=2, Hq=8, Hkv=2, D=128, S=16, P=4,
+         ctx=[0, 5], dtype="bf16"),
+]
+
+
+def attention_inputs(case: dict) -> dict:
+    """q [B,Hq,D], logical pools [P,Hkv,D,S] (float32 values; bf16-representable for
+    bf16 cases, plus their bit patterns) and block tables of distinct random pages."""
+    rng = np.random.default_rng(case["seed"])
+    B, Hq, Hkv, D, S, P = (case[k] for k in ("B", "Hq", "Hkv", "D", "S", "P"))
+    q = rng.standard_normal((B, Hq, D), dtype=np.float32)
+    k = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+    v = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+    perm = rng.permutation(P)
+    tables, cur = [], 0
+    for n in case["ctx"]:
+        npg = -(-n // S)
+        tables.append([int(x) for x in perm[cur:cur + npg]])
+        cur += npg
+    assert cur <= P, "pool too small for the case"
+    out = dict(q=q, k=k, v=v, tables=tables, ctx=list(case["ctx"]))
+    if case["dtype"] == "bf16":
+        for name in ("q", "k", "v"):
+            bits = f32_to_bf16_bits(out[name])
+            out[name + "_bits"] = bits
+            out[name] = bf16_bits_to_f32(bits)
+    return out
+
+
+def checksum(*arrays: np.ndarray) -> float:
+    return float(sum(np.asarray(a, dtype=np.float64).sum() for a in arrays))
+
+
+# C1: tiny Qwen3-architecture dense decoder
+C1_MODEL = dict(n_layers=2, n_heads=4, n_kv_heads=2, head_dim=64, hidden_dim=256,
+                intermediate_dim=512, vocab_size=1024, max_seq_len=128, rope_base=1e6)
+C1_SEED = 7
+C1_DECODE_STEPS = 32
+C1_LOGIT_STEPS = (0, 1, 2, 8, 16, 32)   # steps whose full logits are stored
+
+
+def c1_weights() -> dict[str, np.ndarray]:
+    """fp32 weights ~N(0, 0.02) from a seed; RMSNorm weights are 1."""
+    m = C1_MODEL
+    rng = np.random.default_rng(C1_SEED)
+    hid, inter, voc = m["hidden_dim"], m["intermediate_dim"], m["vocab_size"]
+    qd = m["n_heads"] * m["head_dim"]
+    kvd = m["n_kv_heads"] * m["head_dim"]
+
+    def w(*shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+
+    ws = {"embed_tokens.weight": w(voc, hid)}
+    for i in range(m["n_layers"]):
+        p = f"layers.{i}."
+        ws[p + "input_layernorm.weight"] = np.ones(hid, np.float32)
+        ws[p + "self_attn.q_proj.weight"] = w(qd, hid)
+        ws[p + "self_attn.k_proj.weight"] = w(kvd, hid)
+        ws[p + "self_attn.v_proj.weight"] = w(kvd, hid)
+        ws[p + "self_attn.o_proj.weight"] = w(hid, qd)
+        ws[p + "post_attention_layernorm.weight"] = np.ones(hid, np.float32)
+        ws[p + "mlp.gate_proj.weight"] = w(inter, hid)
+        ws[p + "mlp.up_proj.weight"] = w(inter, hid)
+        ws[p + "mlp.down_proj.weight"] = w(hid, inter)
+    ws["norm.weight"] = np.ones(hid, np.float32)
+    ws["lm_head.weight"] = w(voc, hid)
+    return ws
+
+
+def c1_prompts() -> list[list[int]]:
+    """4 prompts with lengths uniform in [8, 64], token ids uniform in [0, vocab)."""
+    rng = np.random.default_rng(C1_SEED + 1)
+    lens = rng.integers(8, 65, size=4)
+    return [[int(t) for t in rng.integers(0, C1_MODEL["vocab_size"], size=int(n))] for n in lens]
+
+
+# Index-copy / host-store scenario inputs
+def token_kv(seed: int, n_tokens: int, n_layers: int, n_heads: int, head_dim: int,
+             dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """Per-token K/V [n_tokens, L, H, D]; float32 values (bf16-representable for bf16)."""
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((n_tokens, n_layers, n_heads, head_dim), dtype=np.float32)
+    v = rng.standard_normal((n_tokens, n_layers, n_heads, head_dim), dtype=np.float32)
+    if dtype == "bf16":
+        k = bf16_bits_to_f32(f32_to_bf16_bits(k))
+        v = bf16_bits_to_f32(f32_to_bf16_bits(v))
+    return k, v

@@ -1,0 +1,83 @@
+"""The C-ABI library builds, loads, and exports exactly what include/plastic_kv.h declares.
+
+No kernel is launched here (no GPU needed): only symbol presence, the ABI version,
+status strings, and host-side argument validation, which returns before any CUDA
+call.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+from plastic_infer_b200 import _build, _capi
+
+HEADER = pathlib.Path(__file__).resolve().parent.parent / "include" / "plastic_kv.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pi_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib() -> ctypes.CDLL:
+    _build.build()
+    return _capi.load()
+
+
+def test_header_and_binding_agree() -> None:
+    assert declared_functions() == sorted(_capi.SIGNATURES)
+
+
+def test_every_declared_symbol_is_exported(lib: ctypes.CDLL) -> None:
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_strings(lib: ctypes.CDLL) -> None:
+    assert lib.pi_abi_version() == _capi.ABI_VERSION
+    for code in range(0, 10):
+        s = _capi.error_string(code)
+        assert s and s != "unknown status code"
+    assert _capi.error_string(1234) == "unknown status code"
+
+
+def test_host_validation_rejects_before_launch(lib: ctypes.CDLL) -> None:
+    # zero tokens is a no-op
+    assert lib.pi_kv_index_copy(None, None, None, None, None, 0, 8, 128, 16, 1024,
+                                _capi.PI_DTYPE_BF16, 1024, None, None) == _capi.PI_OK
+    # null pointers with work to do
+    assert lib.pi_kv_index_copy(None, None, None, None, None, 4, 8, 128, 16, 1024,
+                                _capi.PI_DTYPE_BF16, 1024, None, None) == _capi.PI_ERR_NULL_POINTER
+    # unknown dtype
+    assert lib.pi_kv_index_copy(None, None, None, None, None, 4, 8, 128, 16, 1024, 7, 1024,
+                                None, None) == _capi.PI_ERR_UNSUPPORTED
+    # token stride shorter than a row
+    assert lib.pi_kv_index_copy(None, None, None, None, None, 4, 8, 128, 16, 1024,
+                                _capi.PI_DTYPE_BF16, 100, None, None) == _capi.PI_ERR_BAD_SHAPE
+    # Hq not a multiple of Hkv
+    assert lib.pi_paged_decode_attn(None, None, None, None, None, 4, None, 2, 6, 4, 128, 16, 64,
+                                    1.0, _capi.PI_DTYPE_BF16, 768, 768, None, 0, None,
+                                    None) == _capi.PI_ERR_BAD_SHAPE
+    # page moves: tile size not a multiple of 16 bytes
+    fake = ctypes.c_void_p(256)
+    assert lib.pi_page_gather(fake, fake, fake, 1, 2, 24, 1, 4, None,
+                              None) == _capi.PI_ERR_MISALIGNED
+    assert lib.pi_page_scatter(None, None, None, 0, 2, 4096, 1, 4, None, None) == _capi.PI_OK
+    assert lib.pi_paged_decode_attn_ws_zero_bytes(64, 8) == 2048
+
+
+def test_kernels_refuse_cpu_tensors() -> None:
+    import torch
+
+    from plastic_infer_b200 import kernels
+
+    pool = torch.zeros(4, 2, 16, 64, dtype=torch.bfloat16)
+    new = torch.zeros(1, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        kernels.kv_index_copy(pool, pool, new, new, torch.zeros(1, dtype=torch.int64))

@@ -1,0 +1,160 @@
+"""Host-side logic of the drop-in API, checked on CPU against the reference's behaviour.
+
+Allocator traces and chunk keys are pinned by golden files produced by the
+reference (tests/golden/allocator.json, chunk_keys.json). The store's bookkeeping
+(page reservation, free, eviction, host LRU) runs on a CPU-device pool; data moves
+on such a pool must raise (no CPU path).
+"""
+
+from __future__ import annotations
+
+import json
+import pathlib
+
+import pytest
+import torch
+
+from plastic_infer_b200.kv import (BlockTable, KVConfig, KVStore, PageAllocator,
+                                   compute_prefix_hashes, longest_prefix_hits)
+from plastic_infer_b200.kv.chunk import compute_prefix_hashes_and_final
+
+GOLD = pathlib.Path(__file__).resolve().parent / "golden"
+
+
+def test_allocator_trace_matches_reference() -> None:
+    trace = json.loads((GOLD / "allocator.json").read_text())
+    a = PageAllocator(10)
+    for step in trace:
+        op = step["op"]
+        if op[0] == "alloc":
+            r = a.alloc()
+        elif op[0] == "alloc_many":
+            r = a.alloc_many(op[1])
+        elif op[0] == "free":
+            r = a.free(op[1])
+        else:
+            r = a.free_many(op[1])
+        assert r == step["result"], step
+        assert (a.free_pages, a.used_pages) == (step["free"], step["used"]), step
+
+
+def test_allocator_errors_match_reference() -> None:
+    a = PageAllocator(3)
+    for _ in range(3):
+        a.alloc()
+    with pytest.raises(IndexError):
+        a.alloc()
+    with pytest.raises(IndexError):
+        PageAllocator(5).alloc_many(10)
+    b = PageAllocator(4)
+    with pytest.raises(AssertionError):
+        b.free(2)  # double free / never allocated
+    with pytest.raises(AssertionError):
+        PageAllocator(0)
+
+
+def test_allocator_no_leak_random() -> None:
+    # tests/test_paged.py:89-107 of the reference: seeded alloc/free never leaks.
+    import random
+
+    rng = random.Random(0)
+    a = PageAllocator(64)
+    live: list[int] = []
+    for _ in range(2000):
+        if live and (rng.random() < 0.5 or a.free_pages == 0):
+            a.free(live.pop(rng.randrange(len(live))))
+        else:
+            live.append(a.alloc())
+        assert a.used_pages == len(live)
+        assert len(set(live)) == len(live)
+
+
+def test_block_table_slots() -> None:
+    bt = BlockTable(n_layers=2, page_size=4)
+    for pid in (7, 2, 9):
+        bt.append_page(0, pid)
+    bt.append_page(1, 5)
+    assert bt.slot(0, 0) == 28 and bt.slot(0, 5) == 9 and bt.slot(0, 11) == 39
+    assert bt.slots_for(0, 3, 3) == [31, 8, 9]
+    assert bt.chunk_page_ids(0, 2) == [7, 2, 5]
+    assert bt.is_chunk_complete(0, 1) and not bt.is_chunk_complete(1, 1)
+    assert bt.all_page_ids() == {2, 5, 7, 9}
+
+
+def test_chunk_keys_match_reference() -> None:
+    gold = json.loads((GOLD / "chunk_keys.json").read_text())
+    for name, case in gold.items():
+        keys = compute_prefix_hashes(case["tokens"], chunk_size=case["chunk_size"])
+        assert [k.prefix_key.hex() for k in keys] == case["prefix"], name
+        assert [k.cumulative_key.hex() for k in keys] == case["cumulative"], name
+    with pytest.raises(ValueError):
+        compute_prefix_hashes(list(range(5)), chunk_size=4)
+
+
+def test_longest_prefix_hits() -> None:
+    toks = list(range(40))
+    keys, _ = compute_prefix_hashes_and_final(toks[:32], chunk_size=8)
+    index = {k.full_key: k for k in keys[:3]}
+    matched, tail = longest_prefix_hits(index, toks, chunk_size=8)
+    assert len(matched) == 3 and tail == 24
+    other = toks[:8] + [999] * 8 + toks[16:]
+    matched, tail = longest_prefix_hits(index, other, chunk_size=8)
+    assert len(matched) == 1 and tail == 8
+    assert longest_prefix_hits({}, toks, chunk_size=8) == ([], 0)
+
+
+def _cpu_store(**kw) -> KVStore:
+    cfg = dict(n_layers=2, n_kv_heads=2, head_dim=4, page_size=4, pages_per_chunk=2,
+               max_pages=64, max_host_chunks=8, dtype=torch.float32, device=torch.device("cpu"))
+    cfg.update(kw)
+    return KVStore(KVConfig(**cfg))
+
+
+def test_store_bookkeeping_on_cpu_pool() -> None:
+    store = _cpu_store()
+    assert store.config.bytes_per_page == 2 * 4 * 4 * 2 * 4
+    assert store.config.tokens_per_chunk == 8
+    # logical views keep the reference's shape
+    assert store.gpu.k_pages.shape == (64, 2, 4, 4)
+    assert store.gpu.get_page_k(3).shape == (2, 4, 4)
+    cache = store.new_request()
+    cache.reserve_tokens(5)   # 5 tokens -> 2 pages per layer
+    assert cache.length == 5
+    assert cache.block_table.num_logical_pages(0) == 2
+    assert store.gpu.allocator.used_pages == 4
+    # reference page order: layer 0 and 1 alternate per new page
+    assert cache.get_block_table_for_layer(0) == [0, 2]
+    assert cache.get_block_table_for_layer(1) == [1, 3]
+    store.free_request(cache)
+    assert store.gpu.allocator.used_pages == 0
+
+
+def test_store_eviction_policy_matches_reference() -> None:
+    # tests/test_kv_store.py:268-284 of the reference, on the bookkeeping only.
+    store = _cpu_store()
+    cache = store.new_request()
+    cache.reserve_tokens(8 * 4)           # 4 full chunks
+    cache.set_token_ids(list(range(32)))
+    assert cache.num_complete_chunks() == 4 and len(cache.chunk_keys) == 4
+    used = store.gpu.allocator.used_pages
+    freed = store.evict_chunks(need_pages=1, protected_request=cache)
+    assert freed == 4                      # one chunk = 2 layers x 2 pages
+    assert store.gpu.allocator.used_pages == used - freed
+    assert store.evict_chunks(need_pages=1) == 0  # no protected request -> no-op
+    # The reference leaves freed pages in the block table (kv_store.py:380-383), so
+    # a second eviction walks chunk 0 again and trips the double-free assertion;
+    # the reference raises the same AssertionError("page 0 not in use").
+    with pytest.raises(AssertionError, match="page 0 not in use"):
+        store.evict_chunks(need_pages=100, protected_request=cache)
+
+
+def test_data_moves_need_cuda() -> None:
+    store = _cpu_store()
+    cache = store.new_request()
+    k = torch.zeros(2, 2, 4)
+    with pytest.raises((ValueError, RuntimeError)):
+        cache.append_token(k, k)
+    cache.reserve_tokens(8)
+    cache.set_token_ids(list(range(8)))
+    with pytest.raises(RuntimeError):
+        store.sink_completed_chunks(cache)

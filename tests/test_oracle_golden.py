@@ -1,0 +1,108 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself.
+
+tests/golden/make_golden.py ran the reference's own functions (append_token,
+_write_kv_layer, paged_attention_v1, sink_completed_chunks, load_prefix,
+compute_prefix_hashes) on seeded inputs; here the numpy restatement must reproduce
+every one of those results (bit-exact for copies, 1e-5 for fp32 attention).
+"""
+
+from __future__ import annotations
+
+import json
+import pathlib
+
+import numpy as np
+import pytest
+
+from oracle import paged_kv_oracle as orc
+from tests.golden.inputs import ATTENTION_CASES, attention_inputs, checksum
+
+GOLD = pathlib.Path(__file__).resolve().parent / "golden"
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_index_copy_matches_reference(dtype: str) -> None:
+    g = np.load(GOLD / f"index_copy_{dtype}.npz")
+    k = np.zeros_like(g["k_pages"])
+    v = np.zeros_like(g["v_pages"])
+    orc.write_kv_slots(k, v, g["k_new"], g["v_new"], g["slots"], int(g["page_size"]))
+    assert np.array_equal(k, g["k_pages"])
+    assert np.array_equal(v, g["v_pages"])
+
+
+@pytest.mark.parametrize("case", ATTENTION_CASES, ids=[c["name"] for c in ATTENTION_CASES])
+def test_attention_matches_reference(case: dict) -> None:
+    g = np.load(GOLD / "attention.npz")
+    x = attention_inputs(case)
+    assert checksum(x["q"], x["k"], x["v"]) == pytest.approx(float(g[case["name"] + "/checksum"]),
+                                                            rel=1e-12)
+    out = orc.paged_attention_decode(x["q"], x["k"], x["v"], x["tables"], x["ctx"], case["S"])
+    ref = g[case["name"] + "/out"]
+    np.testing.assert_allclose(out, ref, atol=2e-5, rtol=1e-5)
+
+
+def test_gather_matches_reference_layout() -> None:
+    # gather_paged_kv of a non-contiguous table [4, 1, 3] with a partial last page
+    # (tests/test_ops.py:227-266 geometry) == page-by-page permute + concat.
+    rng = np.random.default_rng(0)
+    kp = rng.standard_normal((5, 2, 8, 3)).astype(np.float32)
+    vp = rng.standard_normal((5, 2, 8, 3)).astype(np.float32)
+    k, v = orc.gather_paged_kv(kp, vp, [4, 1, 3], 3, num_tokens=8)
+    ref = np.concatenate([kp[p].transpose(2, 0, 1) for p in [4, 1, 3]])[:8]
+    assert np.array_equal(k, ref)
+    e, _ = orc.gather_paged_kv(kp, vp, [], 3)
+    assert e.shape == (0, 2, 8)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_sink_and_load_match_reference(dtype: str) -> None:
+    g = np.load(GOLD / f"store_{dtype}.npz")
+    L, H, D, S, ppc, P = (int(g[k]) for k in ("L", "H", "D", "S", "ppc", "P"))
+    from tests.golden.inputs import token_kv
+    from oracle.paged_kv_oracle import f32_to_bf16_bits
+
+    ntok = len(g["tokens"])
+    k, v = token_kv(21 if dtype == "f32" else 22, ntok, L, H, D, dtype)
+    if dtype == "bf16":
+        k, v = f32_to_bf16_bits(k), f32_to_bf16_bits(v)
+    # Replay the appends into a logical pool with the recorded tables.
+    pool_dt = np.uint16 if dtype == "bf16" else np.float32
+    kp = np.zeros((P, H, D, S), pool_dt)
+    vp = np.zeros((P, H, D, S), pool_dt)
+    tables = [list(map(int, r)) for r in g["c1_tables"]]
+    for layer in range(L):
+        slots = [orc.slot_of(tables[layer], t, S) for t in range(ntok)]
+        orc.write_kv_slots(kp, vp, k[:, layer], v[:, layer], np.asarray(slots), S)
+    n_chunks = int(g["sunk"])
+    for c in range(n_chunks):
+        kc, vc = orc.sink_chunk(kp, vp, tables, c, S, ppc)
+        assert np.array_equal(kc, g["host_k"][c])
+        assert np.array_equal(vc, g["host_v"][c])
+    # Load into the recorded fresh pages and compare the pool contents.
+    kp2 = np.zeros_like(kp)
+    vp2 = np.zeros_like(vp)
+    c2 = [list(map(int, r)) for r in g["c2_tables"]]
+    for c in range(int(g["matched"]) // (S * ppc)):
+        orc.load_chunk(kp2, vp2, g["host_k"][c], g["host_v"][c],
+                       [row[c * ppc:(c + 1) * ppc] for row in c2], S)
+    for layer in range(L):
+        assert np.array_equal(kp2[c2[layer]], g["loaded_k"][layer])
+        assert np.array_equal(vp2[c2[layer]], g["loaded_v"][layer])
+
+
+def test_chunk_keys_match_reference() -> None:
+    gold = json.loads((GOLD / "chunk_keys.json").read_text())
+    for name, case in gold.items():
+        keys = orc.chunk_keys(case["tokens"], case["chunk_size"])
+        assert [p.hex() for p, _ in keys] == case["prefix"], name
+        assert [c.hex() for _, c in keys] == case["cumulative"], name
+
+
+def test_bf16_rounding_is_round_to_nearest_even() -> None:
+    import torch
+
+    x = np.random.default_rng(1).standard_normal(4096).astype(np.float32) * 100
+    x[:4] = [1.00390625, 1.01171875, -2.0078125, 3.0e38]  # exact ties and a large value
+    bits = orc.f32_to_bf16_bits(x)
+    ref = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(bits, ref)
