@@ -161,7 +161,8 @@ class DecodeWorkload:
         self.world = world
         self.gathered = None
         if world > 1:
-            self.gathered = torch.empty((L, world, B, self.hq, D), dtype=torch.bfloat16, device=dev)
+            # rank-major [world * B, Hq/N, D] per layer (what o_proj would consume)
+            self.gathered = torch.empty((L, world * B, self.hq, D), dtype=torch.bfloat16, device=dev)
 
     # algorithmic bytes of one attention launch (one layer) for this rank
     def attn_bytes(self) -> float:

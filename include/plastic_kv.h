@@ -88,14 +88,17 @@ int pi_kv_index_copy(void* k_pool, void* v_pool, const void* k_new, const void* 
                      int* err, cudaStream_t stream);
 
 /*
- * Bytes of device workspace pi_paged_decode_attn needs for this batch shape on
- * the current device. The first `pi_paged_decode_attn_ws_zero_bytes` bytes of
- * the workspace must be zero before the first call; the kernel leaves them zero
- * again on exit, so one zero-fill at allocation time suffices.
+ * Bytes of device workspace pi_paged_decode_attn needs for this shape on the
+ * current device (it depends on head_dim and the SM count only). The first
+ * pi_paged_decode_attn_ws_zero_bytes() bytes hold arrival counters at a fixed
+ * place for every shape: they must be zero before the first call and every
+ * completed call leaves them zero again, so one zero-fill when the workspace is
+ * allocated suffices. After a call that reported PI_ERR_TIMEOUT through `err`,
+ * zero them again. Calls sharing one workspace must be ordered (one stream).
  */
 size_t pi_paged_decode_attn_workspace_bytes(int batch, int num_q_heads, int num_kv_heads,
                                             int head_dim);
-size_t pi_paged_decode_attn_ws_zero_bytes(int batch, int num_kv_heads);
+size_t pi_paged_decode_attn_ws_zero_bytes(void);
 
 /*
  * Batched paged GQA decode attention, one query token per request:

@@ -48,7 +48,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _i64, _vp, _vp],
     ),
     "pi_paged_decode_attn_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
-    "pi_paged_decode_attn_ws_zero_bytes": (_sz, [_i32, _i32]),
+    "pi_paged_decode_attn_ws_zero_bytes": (_sz, []),
     "pi_paged_decode_attn": (
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,

@@ -47,6 +47,7 @@ namespace attn {
 constexpr int kWarps = 4;            // warps per CTA (each an independent consumer)
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxBatch = 4096;      // prefix table lives in shared memory
+constexpr int kMaxKvHeads = 64;      // arrival counters: kMaxBatch x kMaxKvHeads
 constexpr int kMaxCtasPerSm = 2;     // workspace is sized for this many
 constexpr int kHeadsPad = 8;         // n dimension of the MMAs (query heads per KV head)
 constexpr unsigned kFull = 0xffffffffu;
@@ -713,11 +714,17 @@ struct Layout {
 
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-Layout ws_layout(int batch, int hkv, int head_dim, int sms) {
+// Workspace = [arrival counters | partial (m, l) | partial O]. The counter block has
+// a fixed size and position whatever the batch shape, so a launch of one shape can
+// never find partials of an earlier launch of another shape where its counters are:
+// zeroed once, it stays zero because every launch resets the counters it used.
+constexpr size_t kCounterBytes = static_cast<size_t>(kMaxBatch) * kMaxKvHeads * sizeof(int);
+
+Layout ws_layout(int head_dim, int sms) {
   Layout L;
   const size_t slots = static_cast<size_t>(sms) * kMaxCtasPerSm * kWarps * 2;
   L.cnt_off = 0;
-  L.ml_off = align256(static_cast<size_t>(batch) * hkv * sizeof(int));
+  L.ml_off = align256(kCounterBytes);
   L.o_off = L.ml_off + align256(slots * kHeadsPad * 2 * sizeof(float));
   L.total = L.o_off + align256(slots * kHeadsPad * static_cast<size_t>(head_dim) * sizeof(float));
   return L;
@@ -760,12 +767,11 @@ extern "C" size_t pi_paged_decode_attn_workspace_bytes(int batch, int num_q_head
                                                        int num_kv_heads, int head_dim) {
   (void)num_q_heads;
   if (batch <= 0 || num_kv_heads <= 0 || head_dim <= 0) return 0;
-  return pi::attn::ws_layout(batch, num_kv_heads, head_dim, pi::device_sm_count()).total;
+  return pi::attn::ws_layout(head_dim, pi::device_sm_count()).total;
 }
 
-extern "C" size_t pi_paged_decode_attn_ws_zero_bytes(int batch, int num_kv_heads) {
-  if (batch <= 0 || num_kv_heads <= 0) return 0;
-  return pi::attn::align256(static_cast<size_t>(batch) * num_kv_heads * sizeof(int));
+extern "C" size_t pi_paged_decode_attn_ws_zero_bytes(void) {
+  return pi::attn::align256(pi::attn::kCounterBytes);
 }
 
 extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool,
@@ -795,12 +801,12 @@ extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool
   const bool half_type = dtype == PI_DTYPE_BF16 || dtype == PI_DTYPE_F16;
   const bool fast = half_type && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
                     (page_size == 16 || page_size == 32) && group <= kHeadsPad &&
-                    batch <= kMaxBatch && rows > 0 && rows < (int64_t{1} << 31) &&
+                    batch <= kMaxBatch && num_kv_heads <= kMaxKvHeads && rows > 0 && rows < (int64_t{1} << 31) &&
                     static_cast<int64_t>(batch) * bt_stride < (int64_t{1} << 31) &&
                     aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(q, 4) &&
                     q_stride % 2 == 0 && aligned(out, 2);
   if (fast) {
-    const Layout L = ws_layout(batch, num_kv_heads, head_dim, device_sm_count());
+    const Layout L = ws_layout(head_dim, device_sm_count());
     if (workspace == nullptr || workspace_bytes < L.total) return PI_ERR_WORKSPACE;
     if (!aligned(workspace, 256)) return PI_ERR_MISALIGNED;
     FastParams fp;
