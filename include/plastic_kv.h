@@ -53,6 +53,7 @@ extern "C" {
 #define PI_ERR_SLOT_RANGE 7   /* device-side: slot >= num_slots (write skipped)    */
 #define PI_ERR_PAGE_RANGE 8   /* device-side: page id outside the pool (zero read)  */
 #define PI_ERR_TIMEOUT 9      /* device-side: a bounded wait gave up                */
+#define PI_ERR_SCRATCH_LIMIT 10 /* request needs more than the built-in scratch     */
 
 /* element types */
 #define PI_DTYPE_F32 0
@@ -125,6 +126,38 @@ int pi_paged_decode_attn(void* out, const void* q, const void* k_pool, const voi
                          int64_t num_pages, float scale, int dtype, int64_t q_stride,
                          int64_t out_stride, void* workspace, size_t workspace_bytes, int* err,
                          cudaStream_t stream);
+
+/*
+ * Allocation-free pi_paged_decode_attn (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory when they attend: a host loop
+ * that reaches this library only through this C ABI and owns no CUDA allocator,
+ * or an engine whose memory planner has already given every free byte to the
+ * page pool and the weights, so that a cudaMalloc during decoding would fail or
+ * stall the device. Same arguments and results as pi_paged_decode_attn, minus the
+ * workspace: the split-KV scratch is one array of PI_NOALLOC_SCRATCH_BYTES
+ * compiled into the library, which every GPU that loads the library holds until
+ * the process exits. The function calls no cudaMalloc / cudaFree and no
+ * allocating library routine.
+ *
+ *   - A request whose scratch need (pi_paged_decode_attn_workspace_bytes) exceeds
+ *     PI_NOALLOC_SCRATCH_BYTES is rejected with PI_ERR_SCRATCH_LIMIT before any
+ *     launch (e.g. head_dim 256, or head_dim 128 on a GPU with more than 148 SMs).
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current and caches it; make that
+ *     first call before any stream capture on the device.
+ *   - All calls share the one array and it keeps the last call's contents; each
+ *     call clears the part that must start at zero (a cudaMemsetAsync on `stream`).
+ *     Calls that overlap on the GPU (other streams, other threads) race on it:
+ *     order them on one stream.
+ */
+#define PI_NOALLOC_SCRATCH_BYTES ((size_t)12 << 20)
+int pi_paged_decode_attn_noalloc(void* out, const void* q, const void* k_pool,
+                                 const void* v_pool, const int32_t* block_tables,
+                                 int64_t bt_stride, const int32_t* ctx_lens, int batch,
+                                 int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                 int64_t num_pages, float scale, int dtype, int64_t q_stride,
+                                 int64_t out_stride, int* err, cudaStream_t stream);
 
 /*
  * Contiguous gather of a request's pages in the reference's gather layout:

@@ -26,6 +26,8 @@ PI_ERR_WORKSPACE = 6
 PI_ERR_SLOT_RANGE = 7
 PI_ERR_PAGE_RANGE = 8
 PI_ERR_TIMEOUT = 9
+PI_ERR_SCRATCH_LIMIT = 10
+NOALLOC_SCRATCH_BYTES = 12 << 20  # PI_NOALLOC_SCRATCH_BYTES in include/plastic_kv.h
 
 PI_DTYPE_F32 = 0
 PI_DTYPE_BF16 = 1
@@ -53,6 +55,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
          _i64, _i64, _vp, _sz, _vp, _vp],
+    ),
+    # allocation-free variant: scratch is the library's built-in array (no workspace)
+    "pi_paged_decode_attn_noalloc": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
+         _i64, _i64, _vp, _vp],
     ),
     "pi_paged_kv_gather": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _vp, _vp]),
     "pi_page_gather": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _i32, _i64, _vp, _vp]),

@@ -34,6 +34,9 @@ extern "C" const char* pi_error_string(int code) {
     case PI_ERR_SLOT_RANGE: return "slot index outside the page pool (write skipped)";
     case PI_ERR_PAGE_RANGE: return "page id outside the page pool (read skipped)";
     case PI_ERR_TIMEOUT: return "bounded device wait expired";
+    case PI_ERR_SCRATCH_LIMIT:
+      return "request needs more scratch than the allocation-free entry point's built-in "
+             "array (PI_NOALLOC_SCRATCH_BYTES); use pi_paged_decode_attn with a workspace";
     default: return "unknown status code";
   }
 }

@@ -880,3 +880,79 @@ extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool
     paged_decode_attn_simt_kernel<__half><<<grid, 128, 0, stream>>>(sp);
   return cuda_status(cudaGetLastError());
 }
+
+// ---------------------------------------------------------------------------------
+// Allocation-free variant of pi_paged_decode_attn.
+//
+// Some callers cannot allocate device memory when they run attention: a host loop
+// that reaches this library only through the C ABI and owns no CUDA allocator, or
+// an engine whose memory planner has already handed every free byte to the page
+// pool and the weights, where a cudaMalloc in the middle of decoding would fail or
+// stall the device. For them the split-KV scratch (arrival counters and per-warp
+// partial results) lives in one fixed array compiled into this library. Every GPU
+// that loads the library reserves it until the process exits.
+// ---------------------------------------------------------------------------------
+
+namespace pi {
+namespace attn {
+
+// Capacity of the built-in scratch: counters (1 MiB) plus partials for
+// head_dim <= 128 on a GPU with up to 148 SMs (about 10.9 MB at head_dim 128).
+constexpr size_t kStaticScratchBytes = PI_NOALLOC_SCRATCH_BYTES;
+static_assert(PI_NOALLOC_SCRATCH_BYTES == (size_t{12} << 20), "header and library agree");
+
+static __device__ __align__(256) unsigned char g_attn_scratch[kStaticScratchBytes];
+
+// Device address of g_attn_scratch on the current device. On the host the symbol
+// name is only a handle for the runtime, never an address a kernel may use, so the
+// address is looked up once per device (with that device current) and cached.
+int static_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PI_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return PI_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess || p == nullptr)
+      return PI_ERR_CUDA;
+    cached[dev] = p;
+  }
+  *out = cached[dev];
+  return PI_OK;
+}
+
+}  // namespace attn
+}  // namespace pi
+
+extern "C" int pi_paged_decode_attn_noalloc(void* out, const void* q, const void* k_pool,
+                                            const void* v_pool, const int32_t* block_tables,
+                                            int64_t bt_stride, const int32_t* ctx_lens, int batch,
+                                            int num_q_heads, int num_kv_heads, int head_dim,
+                                            int page_size, int64_t num_pages, float scale,
+                                            int dtype, int64_t q_stride, int64_t out_stride,
+                                            int* err, cudaStream_t stream) {
+  using namespace pi;
+  using namespace pi::attn;
+  if (batch <= 0 || num_kv_heads <= 0 || head_dim <= 0) {
+    // Nothing that needs scratch; let the regular entry point validate and return.
+    return pi_paged_decode_attn(out, q, k_pool, v_pool, block_tables, bt_stride, ctx_lens, batch,
+                                num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
+                                dtype, q_stride, out_stride, nullptr, 0, err, stream);
+  }
+  const size_t need =
+      pi_paged_decode_attn_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim);
+  if (need > kStaticScratchBytes) return PI_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int st = static_scratch_address(&scratch);
+  if (st != PI_OK) return st;
+  // The scratch keeps whatever the previous call left; the arrival counters must
+  // start at zero, so clear them on the caller's stream (a memset, not an allocation).
+  if (cudaMemsetAsync(scratch, 0, pi_paged_decode_attn_ws_zero_bytes(), stream) != cudaSuccess)
+    return PI_ERR_CUDA;
+  return pi_paged_decode_attn(out, q, k_pool, v_pool, block_tables, bt_stride, ctx_lens, batch,
+                              num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
+                              dtype, q_stride, out_stride, scratch, kStaticScratchBytes, err,
+                              stream);
+}
