@@ -69,22 +69,26 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int) -> None:
+    def __init__(self, index: int, interval_ms: int = 20) -> None:
         self.index = index
+        self.interval_ms = interval_ms
         self.proc = None
+        self.out = ""
+        self.first = ""
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # nvidia-smi needs a moment to start; the first line marks it sampling
+            self.first = self.proc.stdout.readline()
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *exc) -> None:
-        self.out = ""
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -176,21 +180,21 @@ class DecodeWorkload:
         # one index-copy launch: B tokens x (K+V) x (read + write) rows + slot ids
         return float(self.cfg["batch"]) * (2 * 2 * self.hkv * self.cfg["head_dim"] * 2 + 8)
 
-    def layer(self, l: int, attention: bool = True, copy: bool = True) -> None:
+    def layer(self, l: int, attention: bool = True, copy: bool = True, gather: bool = True) -> None:
         k = self.kernels
         if copy:
             k.kv_index_copy(self.k_pool, self.v_pool, self.k_new[l], self.v_new[l], self.slots[l])
         if attention:
             k.paged_decode_attention(self.q[l], self.k_pool, self.v_pool, self.block_tables[l],
                                      self.ctx_lens, out=self.out[l], workspace=self.ws)
-        if self.world > 1:
+        if self.world > 1 and gather:
             import torch.distributed as dist
 
             dist.all_gather_into_tensor(self.gathered[l], self.out[l])
 
-    def step(self, attention: bool = True, copy: bool = True) -> None:
+    def step(self, attention: bool = True, copy: bool = True, gather: bool = True) -> None:
         for l in range(self.cfg["layers"]):
-            self.layer(l, attention, copy)
+            self.layer(l, attention, copy, gather)
 
 
 def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
@@ -334,11 +338,37 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_c2_only(args, dev: torch.device) -> None:
+    """C2 index-copy microbench alone (with --profile: plain launches for ncu)."""
+    from plastic_infer_b200 import kernels
+
+    peaks = measured_peaks()
+    if not args.profile:
+        print(json.dumps(dict(index_copy=bench_index_copy(dev, peaks["hbm_gbs"]))), flush=True)
+        return
+    P, S, H, D = C2["pages"], C2["page_size"], C2["hkv"], C2["head_dim"]
+    kp = torch.zeros((P, H, S, D), dtype=torch.bfloat16, device=dev)
+    vp = torch.zeros_like(kp)
+    perm = np.random.default_rng(0).permutation(P * S)
+    for B in C2["batches"]:
+        slots = torch.from_numpy(perm[:B].astype(np.int64)).to(dev)
+        kn = torch.randn((B, H, D), dtype=torch.bfloat16, device=dev)
+        vn = torch.randn((B, H, D), dtype=torch.bfloat16, device=dev)
+        for _ in range(args.warmup + args.steps):
+            kernels.kv_index_copy(kp, vp, kn, vn, slots)
+    torch.cuda.synchronize()
+    print(json.dumps(dict(profile=True, c2_batches=list(C2["batches"]))), flush=True)
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    if args.c2_only:
+        run_c2_only(args, dev)
+        return
     peaks = measured_peaks()
     cfg = dict(C3)
+    cfg["layers"] = args.layers
     wl = DecodeWorkload(cfg, rank, world, dev)
     stream = torch.cuda.current_stream()
 
@@ -346,6 +376,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for _ in range(max(1, args.warmup)):
         wl.step()
     torch.cuda.synchronize()
+    if args.profile:
+        # Profiling mode (ncu): plain launches, nothing but the timed steps.
+        for _ in range(args.steps):
+            wl.step()
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps(dict(profile=True, layers=cfg["layers"], steps=args.steps,
+                                  attn_bytes_per_launch=int(wl.attn_bytes()))), flush=True)
+        return
     use_graph = world == 1
     step_fn = wl.step
     if use_graph:
@@ -363,8 +402,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     value = cfg["batch"] * args.steps / (ms * 1e-3)
 
     # attention alone (dominant kernel), same stream, for the roofline
-    attn_fn = lambda: wl.step(attention=True, copy=False)  # noqa: E731
-    copy_fn = lambda: wl.step(attention=False, copy=True)  # noqa: E731
+    attn_fn = lambda: wl.step(attention=True, copy=False, gather=False)  # noqa: E731
+    copy_fn = lambda: wl.step(attention=False, copy=True, gather=False)  # noqa: E731
     if use_graph:
         ga, gc = graph_of(attn_fn), graph_of(copy_fn)
         attn_fn, copy_fn = ga.replay, gc.replay
@@ -376,7 +415,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     # e2e through the public API with pinned host buffers
     e2e = None
-    if world == 1:
+    if world == 1 and not args.skip_e2e:
         e2e = run_e2e(wl, args, stream)
 
     idx = bench_index_copy(dev, peaks["hbm_gbs"]) if (world == 1 and not args.skip_c2) else None
@@ -419,10 +458,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
 
 def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
-    """Whole step through the public API, inputs from pinned host memory each step."""
+    """Whole step through the public API, inputs from pinned host memory each step.
+
+    Layer l's inputs are copied host->device on one copy stream and its attention
+    output device->host on another, so the copies of layer l+1 / l-1 overlap the
+    kernels of layer l; the step ends when the last output is on the host.
+    """
     from plastic_infer_b200 import kernels
 
-    dev = wl.dev
     q_h = wl.q.cpu().pin_memory()
     kn_h = wl.k_new.cpu().pin_memory()
     vn_h = wl.v_new.cpu().pin_memory()
@@ -431,18 +474,31 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
     slots_d = torch.empty_like(wl.slots)
     ctx_d = torch.empty_like(wl.ctx_lens)
     L = wl.cfg["layers"]
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(L)]
+    ev_out = [torch.cuda.Event() for _ in range(L)]
 
     def step():
-        q_d.copy_(q_h, non_blocking=True)
-        kn_d.copy_(kn_h, non_blocking=True)
-        vn_d.copy_(vn_h, non_blocking=True)
-        slots_d.copy_(wl.slots_host, non_blocking=True)
-        ctx_d.copy_(wl.ctx_host, non_blocking=True)
+        h2d.wait_stream(stream)  # device inputs of the previous step are no longer read
+        with torch.cuda.stream(h2d):
+            ctx_d.copy_(wl.ctx_host, non_blocking=True)
+            for l in range(L):
+                q_d[l].copy_(q_h[l], non_blocking=True)
+                kn_d[l].copy_(kn_h[l], non_blocking=True)
+                vn_d[l].copy_(vn_h[l], non_blocking=True)
+                slots_d[l].copy_(wl.slots_host[l], non_blocking=True)
+                ev_in[l].record(h2d)
         for l in range(L):
+            stream.wait_event(ev_in[l])
             kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
             kernels.paged_decode_attention(q_d[l], wl.k_pool, wl.v_pool, wl.block_tables[l], ctx_d,
                                            out=wl.out[l], workspace=wl.ws)
-        out_h.copy_(wl.out, non_blocking=True)
+            ev_out[l].record(stream)
+        with torch.cuda.stream(d2h):
+            for l in range(L):
+                d2h.wait_event(ev_out[l])
+                out_h[l].copy_(wl.out[l], non_blocking=True)
+        stream.wait_stream(d2h)
 
     for _ in range(args.warmup):
         step()
@@ -474,6 +530,12 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-c2", action="store_true", help="skip the index-copy microbench")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--skip-e2e", action="store_true", help="skip the host-buffer e2e run")
+    ap.add_argument("--layers", type=int, default=C3["layers"],
+                    help="decoder layers per step (36 = Qwen3-8B; fewer only for profiling)")
+    ap.add_argument("--profile", action="store_true",
+                    help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
+    ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -126,16 +126,19 @@ def paged_attention_decode(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarr
         if n <= 0:
             continue
         npg = -(-n // page_size)
-        k, v = gather_paged_kv(k_pages, v_pages, list(block_tables[b][:npg]), page_size, n)
-        k = k.astype(np.float32)
-        v = v.astype(np.float32)
-        for h in range(Hkv):
-            qg = q[b, h * G:(h + 1) * G]                 # [G, D]
-            s = (qg @ k[:, h, :].T) * np.float32(scale)  # [G, n]
-            s = s - s.max(axis=1, keepdims=True)
-            p = np.exp(s)
-            p /= p.sum(axis=1, keepdims=True)
-            out[b, h * G:(h + 1) * G] = p @ v[:, h, :]
+        ids = np.asarray(block_tables[b][:npg], dtype=np.int64)
+        # Gathered pages [npg, Hkv, D, S] -> per-head K^T / V^T [Hkv, D, T] (the same
+        # token order as gather_paged_kv's permute + reshape), trimmed to n tokens.
+        kt = k_pages[ids].astype(np.float32, copy=False).transpose(1, 2, 0, 3)
+        vt = v_pages[ids].astype(np.float32, copy=False).transpose(1, 2, 0, 3)
+        kt = kt.reshape(Hkv, D, npg * page_size)[:, :, :n]
+        vt = vt.reshape(Hkv, D, npg * page_size)[:, :, :n]
+        qg = q[b].reshape(Hkv, G, D)                          # query head h*G+g -> KV head h
+        s = np.matmul(qg, kt) * np.float32(scale)             # [Hkv, G, n]
+        s -= s.max(axis=2, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=2, keepdims=True)
+        out[b] = np.matmul(p, vt.transpose(0, 2, 1)).reshape(Hq, D)
     return out
 
 

@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(256) kv_index_copy_kernel(
     int kv_heads, int row_bytes, int page_size, int64_t num_slots, int64_t src_token_stride_bytes,
     int* err) {
   using V = typename VecT<VEC>::type;
+  constexpr int kPerLane = VEC == 16 ? 8 : 16;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -67,29 +68,54 @@ __global__ void __launch_bounds__(256) kv_index_copy_kernel(
   const int64_t head_stride = static_cast<int64_t>(page_size) * row_bytes;  // pool bytes per head
   const int64_t page_stride = head_stride * kv_heads;
 
-  for (int64_t t = warp; t < n_tokens; t += nwarps) {
-    const int64_t slot = __ldg(slot_mapping + t);
-    if (slot < 0) continue;  // padding
-    if (slot >= num_slots) {
+  const int total = 2 * vec_per_tensor;  // vectors of one token (K then V)
+  int64_t t = warp;
+  int64_t slot = t < n_tokens ? __ldg(slot_mapping + t) : -1;
+  for (; t < n_tokens; t += nwarps) {
+    // Prefetch the next token's slot so its load overlaps this token's copy.
+    const int64_t tn = t + nwarps;
+    const int64_t next_slot = tn < n_tokens ? __ldg(slot_mapping + tn) : -1;
+    const int64_t s = slot;
+    slot = next_slot;
+    if (s < 0) continue;  // padding
+    if (s >= num_slots) {
       if (lane == 0) record_error(err, PI_ERR_SLOT_RANGE);
       continue;
     }
-    const int64_t page = slot / page_size;
-    const int64_t off = slot - page * page_size;
+    const int64_t page = s / page_size;
+    const int64_t off = s - page * page_size;
     const int64_t dst_base = page * page_stride + off * row_bytes;
     const char* ks = k_new + t * src_token_stride_bytes;
     const char* vs = v_new + t * src_token_stride_bytes;
 
-    // K and V in one pass so each lane has several independent loads in flight.
-    for (int c = lane; c < 2 * vec_per_tensor; c += 32) {
-      const bool is_v = c >= vec_per_tensor;
-      const int cc = is_v ? c - vec_per_tensor : c;
-      const int h = cc / vec_per_row;
-      const int w = cc - h * vec_per_row;
-      const int64_t src_off = static_cast<int64_t>(h) * row_bytes + static_cast<int64_t>(w) * VEC;
-      const int64_t dst_off = dst_base + h * head_stride + static_cast<int64_t>(w) * VEC;
-      const V val = load_stream<VEC>((is_v ? vs : ks) + src_off);
-      *reinterpret_cast<V*>((is_v ? v_pool : k_pool) + dst_off) = val;
+    // All loads of a batch of kPerLane vectors per lane are issued before any store,
+    // so a warp keeps up to 32 * kPerLane * VEC bytes (4 KiB at 16 B) in flight.
+    for (int base = 0; base < total; base += 32 * kPerLane) {
+      V vals[kPerLane];
+#pragma unroll
+      for (int j = 0; j < kPerLane; ++j) {
+        const int c = base + j * 32 + lane;
+        if (c < total) {
+          const bool is_v = c >= vec_per_tensor;
+          const int cc = is_v ? c - vec_per_tensor : c;
+          const int h = cc / vec_per_row;
+          const int w = cc - h * vec_per_row;
+          vals[j] = load_stream<VEC>((is_v ? vs : ks) + static_cast<int64_t>(h) * row_bytes +
+                                     static_cast<int64_t>(w) * VEC);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kPerLane; ++j) {
+        const int c = base + j * 32 + lane;
+        if (c < total) {
+          const bool is_v = c >= vec_per_tensor;
+          const int cc = is_v ? c - vec_per_tensor : c;
+          const int h = cc / vec_per_row;
+          const int w = cc - h * vec_per_row;
+          *reinterpret_cast<V*>((is_v ? v_pool : k_pool) + dst_base + h * head_stride +
+                                static_cast<int64_t>(w) * VEC) = vals[j];
+        }
+      }
     }
   }
 }
