@@ -163,6 +163,7 @@ class DecodeWorkload:
         self.out = torch.empty((L, B, self.hq, D), dtype=torch.bfloat16, device=dev)
         self.ws = kernels.Workspace(dev)
         self.world = world
+        self.fused = True
         self.gathered = None
         if world > 1:
             # rank-major [world * B, Hq/N, D] per layer (what o_proj would consume)
@@ -182,11 +183,19 @@ class DecodeWorkload:
 
     def layer(self, l: int, attention: bool = True, copy: bool = True, gather: bool = True) -> None:
         k = self.kernels
-        if copy:
-            k.kv_index_copy(self.k_pool, self.v_pool, self.k_new[l], self.v_new[l], self.slots[l])
-        if attention:
+        if attention and copy and self.fused:
+            # one launch: write the 64 new K/V rows, then attend
             k.paged_decode_attention(self.q[l], self.k_pool, self.v_pool, self.block_tables[l],
-                                     self.ctx_lens, out=self.out[l], workspace=self.ws)
+                                     self.ctx_lens, out=self.out[l], workspace=self.ws,
+                                     k_new=self.k_new[l], v_new=self.v_new[l],
+                                     slot_mapping=self.slots[l])
+        else:
+            if copy:
+                k.kv_index_copy(self.k_pool, self.v_pool, self.k_new[l], self.v_new[l],
+                                self.slots[l])
+            if attention:
+                k.paged_decode_attention(self.q[l], self.k_pool, self.v_pool, self.block_tables[l],
+                                         self.ctx_lens, out=self.out[l], workspace=self.ws)
         if self.world > 1 and gather:
             import torch.distributed as dist
 
@@ -370,6 +379,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     cfg = dict(C3)
     cfg["layers"] = args.layers
     wl = DecodeWorkload(cfg, rank, world, dev)
+    wl.fused = not args.unfused
     stream = torch.cuda.current_stream()
 
     # warm-up (also configures kernels before graph capture)
@@ -443,7 +453,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                           peak_source=peaks["source"]),
             index_copy_in_step=dict(us_per_launch=round(copy_ms * 1e3, 2),
                                     gbs=round(wl.copy_bytes() / (copy_ms * 1e-3) / 1e9, 1)),
-            gpu_launches=args.steps * cfg["layers"] * 2,
+            gpu_launches=args.steps * cfg["layers"] * (1 if wl.fused else 2),
             clocks=clk.summary(),
         )
         if e2e is not None:
@@ -490,9 +500,9 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                 ev_in[l].record(h2d)
         for l in range(L):
             stream.wait_event(ev_in[l])
-            kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
             kernels.paged_decode_attention(q_d[l], wl.k_pool, wl.v_pool, wl.block_tables[l], ctx_d,
-                                           out=wl.out[l], workspace=wl.ws)
+                                           out=wl.out[l], workspace=wl.ws, k_new=kn_d[l],
+                                           v_new=vn_d[l], slot_mapping=slots_d[l])
             ev_out[l].record(stream)
         with torch.cuda.stream(d2h):
             for l in range(L):
@@ -536,6 +546,8 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
     ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
+    ap.add_argument("--unfused", action="store_true",
+                    help="separate index-copy and attention launches per layer (default: fused)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

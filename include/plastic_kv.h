@@ -128,6 +128,29 @@ int pi_paged_decode_attn(void* out, const void* q, const void* k_pool, const voi
                          cudaStream_t stream);
 
 /*
+ * Decode step of one layer in one launch: the slot-mapping write of the step's new
+ * K/V rows followed by paged decode attention. Same result as
+ *   pi_kv_index_copy(k_pool, v_pool, k_new, v_new, slot_mapping, batch, ...)
+ *   pi_paged_decode_attn(out, q, k_pool, v_pool, ...)
+ * with one new row per request (k_new, v_new: [batch, kv_heads, head_dim], request
+ * stride new_stride elements; slot_mapping[b] < 0 = no new row for request b).
+ * The page holding request b's new slot must be read only by request b (the
+ * reference never shares pages between requests, src/plastic_infer/kv/paged.py:12).
+ * Replaces the per-layer pair _write_kv_layer + _attn_paged of the decode loop
+ * (src/plastic_infer/exec/runner_paged.py:250-255). Shapes the fused kernel does
+ * not cover run the two kernels back to back.
+ */
+int pi_paged_decode_attn_append(void* out, const void* q, void* k_pool, void* v_pool,
+                                const void* k_new, const void* v_new,
+                                const int64_t* slot_mapping, int64_t new_stride,
+                                const int32_t* block_tables, int64_t bt_stride,
+                                const int32_t* ctx_lens, int batch, int num_q_heads,
+                                int num_kv_heads, int head_dim, int page_size, int64_t num_pages,
+                                float scale, int dtype, int64_t q_stride, int64_t out_stride,
+                                void* workspace, size_t workspace_bytes, int* err,
+                                cudaStream_t stream);
+
+/*
  * Allocation-free pi_paged_decode_attn (no counterpart in the reference).
  *
  * For callers that cannot allocate device memory when they attend: a host loop

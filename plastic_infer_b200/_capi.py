@@ -56,6 +56,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
          _i64, _i64, _vp, _sz, _vp, _vp],
     ),
+    "pi_paged_decode_attn_append": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32,
+         _i64, _f32, _i32, _i64, _i64, _vp, _sz, _vp, _vp],
+    ),
     # allocation-free variant: scratch is the library's built-in array (no workspace)
     "pi_paged_decode_attn_noalloc": (
         _i32,

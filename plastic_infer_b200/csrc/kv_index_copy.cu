@@ -52,7 +52,7 @@ __device__ __forceinline__ typename VecT<VEC>::type load_stream(const void* p) {
   }
 }
 
-template <int VEC>
+template <int VEC, bool kFixedLanes>
 __global__ void __launch_bounds__(256) kv_index_copy_kernel(
     char* __restrict__ k_pool, char* __restrict__ v_pool, const char* __restrict__ k_new,
     const char* __restrict__ v_new, const int64_t* __restrict__ slot_mapping, int64_t n_tokens,
@@ -69,6 +69,9 @@ __global__ void __launch_bounds__(256) kv_index_copy_kernel(
   const int64_t page_stride = head_stride * kv_heads;
 
   const int total = 2 * vec_per_tensor;  // vectors of one token (K then V)
+  const int rows_per_pass = kFixedLanes ? 32 / vec_per_row : 0;
+  const int r0 = kFixedLanes ? lane / vec_per_row : 0;
+  const int64_t w0 = kFixedLanes ? static_cast<int64_t>(lane % vec_per_row) * VEC : 0;
   int64_t t = warp;
   int64_t slot = t < n_tokens ? __ldg(slot_mapping + t) : -1;
   for (; t < n_tokens; t += nwarps) {
@@ -88,8 +91,38 @@ __global__ void __launch_bounds__(256) kv_index_copy_kernel(
     const char* ks = k_new + t * src_token_stride_bytes;
     const char* vs = v_new + t * src_token_stride_bytes;
 
-    // All loads of a batch of kPerLane vectors per lane are issued before any store,
-    // so a warp keeps up to 32 * kPerLane * VEC bytes (4 KiB at 16 B) in flight.
+    if constexpr (kFixedLanes) {
+      // 32 % vec_per_row == 0: lane `lane` always copies vector w of rows r0, r0 +
+      // rows_per_pass, ... over the token's 2*kv_heads rows (K rows, then V rows), so
+      // the per-vector address math has no division. All loads go out before any store.
+      constexpr int kMaxRows = kPerLane;  // rows per lane handled per pass
+      for (int rbase = 0; rbase < 2 * kv_heads; rbase += rows_per_pass * kMaxRows) {
+        V vals[kMaxRows];
+#pragma unroll
+        for (int j = 0; j < kMaxRows; ++j) {
+          const int r = rbase + r0 + j * rows_per_pass;
+          if (r < 2 * kv_heads) {
+            const bool is_v = r >= kv_heads;
+            const int h = is_v ? r - kv_heads : r;
+            vals[j] = load_stream<VEC>((is_v ? vs : ks) + static_cast<int64_t>(h) * row_bytes + w0);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kMaxRows; ++j) {
+          const int r = rbase + r0 + j * rows_per_pass;
+          if (r < 2 * kv_heads) {
+            const bool is_v = r >= kv_heads;
+            const int h = is_v ? r - kv_heads : r;
+            *reinterpret_cast<V*>((is_v ? v_pool : k_pool) + dst_base + h * head_stride + w0) =
+                vals[j];
+          }
+        }
+      }
+      continue;
+    }
+
+    // General shapes: all loads of a batch of kPerLane vectors per lane are issued
+    // before any store, so a warp keeps up to 32 * kPerLane * VEC bytes in flight.
     for (int base = 0; base < total; base += 32 * kPerLane) {
       V vals[kPerLane];
 #pragma unroll
@@ -132,10 +165,18 @@ int launch_index_copy(void* k_pool, void* v_pool, const void* k_new, const void*
   const int64_t cap = static_cast<int64_t>(sms) * 16;  // grid-stride beyond 16 CTAs per SM
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  kv_index_copy_kernel<VEC><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-      static_cast<char*>(k_pool), static_cast<char*>(v_pool), static_cast<const char*>(k_new),
-      static_cast<const char*>(v_new), slot_mapping, n_tokens, kv_heads, row_bytes, page_size,
-      num_slots, src_stride_bytes, err);
+  const bool fixed = (32 % (row_bytes / VEC)) == 0;
+  if (fixed) {
+    kv_index_copy_kernel<VEC, true><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
+        static_cast<char*>(k_pool), static_cast<char*>(v_pool), static_cast<const char*>(k_new),
+        static_cast<const char*>(v_new), slot_mapping, n_tokens, kv_heads, row_bytes, page_size,
+        num_slots, src_stride_bytes, err);
+  } else {
+    kv_index_copy_kernel<VEC, false><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
+        static_cast<char*>(k_pool), static_cast<char*>(v_pool), static_cast<const char*>(k_new),
+        static_cast<const char*>(v_new), slot_mapping, n_tokens, kv_heads, row_bytes, page_size,
+        num_slots, src_stride_bytes, err);
+  }
   return cuda_status(cudaGetLastError());
 }
 

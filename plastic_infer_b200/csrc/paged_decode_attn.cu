@@ -69,6 +69,15 @@ struct FastParams {
   float* ws_ml;  // [n_warps * 2][kHeadsPad][2] partial (max, sum)
   float* ws_o;   // [n_warps * 2][kHeadsPad][D] partial unnormalised outputs
   int* err;
+  // Fused append (all null for plain attention): before attending, request b's new
+  // K/V rows k_new[b], v_new[b] ([hkv, D], row stride new_stride elements) are
+  // written at slot slot_mapping[b] (< 0: none) of the pools k_pool_w / v_pool_w.
+  const void* k_new;
+  const void* v_new;
+  const int64_t* slot_mapping;
+  int64_t new_stride;
+  void* k_pool_w;
+  void* v_pool_w;
 };
 
 template <int D, int S>
@@ -94,7 +103,8 @@ constexpr int stages_for() {
 template <int D, int S, int NS>
 constexpr size_t fast_smem_bytes() {
   return 1024 /* alignment slack */ + static_cast<size_t>(kWarps) * NS * Cfg<D, S>::kStageBytes +
-         static_cast<size_t>(kWarps) * NS * 8 /* mbarriers */ + (kMaxBatch + 1) * 4;
+         static_cast<size_t>(kWarps) * NS * 8 /* mbarriers */ + (kMaxBatch + 1) * 4 +
+         static_cast<size_t>(kWarps) * NS * 4 /* tile held by each stage */;
 }
 
 // Byte offset of element (t, d) inside a swizzled [boxes][S][128 B] tile.
@@ -121,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* tiles = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + kWarps * NS * C::kStageBytes);
   int* s_poff = reinterpret_cast<int*>(bars + kWarps * NS);
+  int* s_tile = s_poff + kMaxBatch + 1;  // [kWarps][NS] tile index loaded into each stage
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -182,6 +193,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // Fused append: store the step's new K/V rows in the pools (one warp per
+  // (request, head) row pair). A TMA load of the same page may see the row before or
+  // after this store; the warp that consumes that page patches the row in shared
+  // memory from the source instead, so the result never depends on the order.
+  constexpr int kRowChunks = D / 8;  // 16-byte chunks per head row
+  if (p.slot_mapping != nullptr) {
+    for (int i = gw; i < B * Hkv; i += NW) {
+      const int b = i / Hkv;
+      const int h = i - b * Hkv;
+      const int64_t s = __ldg(p.slot_mapping + b);
+      if (s < 0) continue;
+      if (s >= p.num_pages * S) {
+        if (lane == 0) record_error(p.err, PI_ERR_SLOT_RANGE);
+        continue;
+      }
+      const int64_t page = s / S;
+      const int64_t dst = ((page * Hkv + h) * S + (s - page * S)) * D;
+      const int64_t src = static_cast<int64_t>(b) * p.new_stride + static_cast<int64_t>(h) * D;
+      for (int c = lane; c < 2 * kRowChunks; c += 32) {
+        const bool is_v = c >= kRowChunks;
+        const int cc = is_v ? c - kRowChunks : c;
+        const uint4 val =
+            *reinterpret_cast<const uint4*>(static_cast<const T*>(is_v ? p.v_new : p.k_new) + src + cc * 8);
+        *reinterpret_cast<uint4*>(static_cast<T*>(is_v ? p.v_pool_w : p.k_pool_w) + dst + cc * 8) = val;
+      }
+    }
+  }
+
   // Partition over at most `total` warps so every active warp owns >= 1 page: a
   // segment's pieces are then exactly the warps [first, last] that overlap it.
   const int NWe = static_cast<int>(total < NW ? total : NW);
@@ -230,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int tile = __shfl_sync(kFull, id_cur, static_cast<int>(pos - pbase));
     if (lane == 0) {
+      s_tile[warp * NS + stage] = tile;
       const uint32_t bar = bar0 + 8 * stage;
       const uint32_t kdst = tiles_u32 + stage * C::kStageBytes;
       const uint32_t vdst = kdst + C::kTileBytes;
@@ -272,6 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool failed = false;
   int64_t pos = lo;
   int k = 0;
+  // Fused append: the tile (page_id * Hkv + h) holding the current segment's new
+  // slot (-1: none), the row inside it, and this lane's share of the new K/V row.
+  constexpr int kPatch = (2 * kRowChunks + 31) / 32;
+  int patch_tile = -1;
+  int patch_row = 0;
+  uint4 patch_val[kPatch];
 
   auto first_warp_of = [&](int64_t s) -> int {
     return static_cast<int>(((s + 1) * NWe - 1) / total);
@@ -387,6 +433,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       l0 = l1 = 0.f;
       piece_start = pos;
       fresh = false;
+      if (p.slot_mapping != nullptr) {
+        // Fused append: fetch this head's new K/V row now (lane c holds 16-byte chunk
+        // c of [K row | V row]) so the patch below never waits on memory.
+        const int64_t s = __ldg(p.slot_mapping + cb);
+        patch_tile = (s >= 0 && s < p.num_pages * S) ? static_cast<int>(s / S) * Hkv + ch : -1;
+        patch_row = static_cast<int>(s % S);
+        const int64_t src = static_cast<int64_t>(cb) * p.new_stride + static_cast<int64_t>(ch) * D;
+#pragma unroll
+        for (int e = 0; e < kPatch; ++e) {
+          const int c = lane + 32 * e;
+          if (patch_tile >= 0 && c < 2 * kRowChunks) {
+            const bool is_v = c >= kRowChunks;
+            const int cc = is_v ? c - kRowChunks : c;
+            patch_val[e] = *reinterpret_cast<const uint4*>(
+                static_cast<const T*>(is_v ? p.v_new : p.k_new) + src + cc * 8);
+          }
+        }
+      }
     }
 
     const int stage = k % NS;
@@ -410,6 +474,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c16 = rem & 7;
         *reinterpret_cast<uint4*>(vt + j * C::kBoxBytes + row * 128 + c16 * 16) =
             make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+    if (patch_tile >= 0 && s_tile[warp * NS + stage] == patch_tile) {
+      // This stage holds the page of the request's new slot: overwrite that row of
+      // the K and V tiles with the new values (swizzled like the TMA box).
+      uint8_t* kt = tiles + (warp * NS + stage) * C::kStageBytes;
+#pragma unroll
+      for (int e = 0; e < kPatch; ++e) {
+        const int c = lane + 32 * e;
+        if (c < 2 * kRowChunks) {
+          const bool is_v = c >= kRowChunks;
+          const int cc = is_v ? c - kRowChunks : c;  // chunk along D: box cc / 8, column cc % 8
+          uint8_t* base = kt + (is_v ? C::kTileBytes : 0) + (cc >> 3) * C::kBoxBytes +
+                          patch_row * 128 + (((cc & 7) ^ (patch_row & 7)) << 4);
+          *reinterpret_cast<uint4*>(base) = patch_val[e];
+        }
       }
       __syncwarp();
     }
@@ -774,15 +855,23 @@ extern "C" size_t pi_paged_decode_attn_ws_zero_bytes(void) {
   return pi::attn::align256(pi::attn::kCounterBytes);
 }
 
-extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool,
-                                    const void* v_pool, const int32_t* block_tables,
-                                    int64_t bt_stride, const int32_t* ctx_lens, int batch,
-                                    int num_q_heads, int num_kv_heads, int head_dim, int page_size,
-                                    int64_t num_pages, float scale, int dtype, int64_t q_stride,
-                                    int64_t out_stride, void* workspace, size_t workspace_bytes,
-                                    int* err, cudaStream_t stream) {
-  using namespace pi;
-  using namespace pi::attn;
+namespace pi {
+namespace attn {
+
+// New K/V rows to store before attending (fused append); see FastParams.
+struct AppendArgs {
+  const void* k_new;
+  const void* v_new;
+  const int64_t* slot_mapping;
+  int64_t new_stride;
+};
+
+int attn_dispatch(void* out, const void* q, const void* k_pool, const void* v_pool,
+                  const int32_t* block_tables, int64_t bt_stride, const int32_t* ctx_lens,
+                  int batch, int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                  int64_t num_pages, float scale, int dtype, int64_t q_stride, int64_t out_stride,
+                  void* workspace, size_t workspace_bytes, int* err, cudaStream_t stream,
+                  const AppendArgs* app) {
   const int eb = elem_bytes_of(dtype);
   if (eb == 0) return PI_ERR_UNSUPPORTED;
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || page_size <= 0 ||
@@ -805,6 +894,17 @@ extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool
                     static_cast<int64_t>(batch) * bt_stride < (int64_t{1} << 31) &&
                     aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(q, 4) &&
                     q_stride % 2 == 0 && aligned(out, 2);
+  // The fused append stores whole 16-byte chunks of the new rows.
+  const bool fuse = app != nullptr && fast && aligned(app->k_new, 16) &&
+                    aligned(app->v_new, 16) && (app->new_stride * eb) % 16 == 0;
+  if (app != nullptr && !fuse) {
+    // Not fusable: store the rows with the index-copy kernel, then attend.
+    const int rc = pi_kv_index_copy(const_cast<void*>(k_pool), const_cast<void*>(v_pool),
+                                    app->k_new, app->v_new, app->slot_mapping, batch,
+                                    num_kv_heads, head_dim, page_size, num_pages * page_size,
+                                    dtype, app->new_stride, err, stream);
+    if (rc != PI_OK) return rc;
+  }
   if (fast) {
     const Layout L = ws_layout(head_dim, device_sm_count());
     if (workspace == nullptr || workspace_bytes < L.total) return PI_ERR_WORKSPACE;
@@ -827,6 +927,12 @@ extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool
     fp.ws_ml = reinterpret_cast<float*>(ws + L.ml_off);
     fp.ws_o = reinterpret_cast<float*>(ws + L.o_off);
     fp.err = err;
+    fp.k_new = fuse ? app->k_new : nullptr;
+    fp.v_new = fuse ? app->v_new : nullptr;
+    fp.slot_mapping = fuse ? app->slot_mapping : nullptr;
+    fp.new_stride = fuse ? app->new_stride : 0;
+    fp.k_pool_w = const_cast<void*>(k_pool);
+    fp.v_pool_w = const_cast<void*>(v_pool);
 #define PI_FAST(T, D, S)                                                                  \
   if (head_dim == D && page_size == S)                                                    \
     return launch_fast<T, D, S>(fp, k_pool, v_pool, rows, dtype, stream);
@@ -879,6 +985,39 @@ extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool
   else
     paged_decode_attn_simt_kernel<__half><<<grid, 128, 0, stream>>>(sp);
   return cuda_status(cudaGetLastError());
+}
+
+}  // namespace attn
+}  // namespace pi
+
+extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool,
+                                    const void* v_pool, const int32_t* block_tables,
+                                    int64_t bt_stride, const int32_t* ctx_lens, int batch,
+                                    int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                    int64_t num_pages, float scale, int dtype, int64_t q_stride,
+                                    int64_t out_stride, void* workspace, size_t workspace_bytes,
+                                    int* err, cudaStream_t stream) {
+  return pi::attn::attn_dispatch(out, q, k_pool, v_pool, block_tables, bt_stride, ctx_lens, batch,
+                                 num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
+                                 dtype, q_stride, out_stride, workspace, workspace_bytes, err,
+                                 stream, nullptr);
+}
+
+extern "C" int pi_paged_decode_attn_append(
+    void* out, const void* q, void* k_pool, void* v_pool, const void* k_new, const void* v_new,
+    const int64_t* slot_mapping, int64_t new_stride, const int32_t* block_tables,
+    int64_t bt_stride, const int32_t* ctx_lens, int batch, int num_q_heads, int num_kv_heads,
+    int head_dim, int page_size, int64_t num_pages, float scale, int dtype, int64_t q_stride,
+    int64_t out_stride, void* workspace, size_t workspace_bytes, int* err, cudaStream_t stream) {
+  using namespace pi;
+  if (batch > 0 && (!k_new || !v_new || !slot_mapping)) return PI_ERR_NULL_POINTER;
+  if (new_stride < static_cast<int64_t>(num_kv_heads) * head_dim) return PI_ERR_BAD_SHAPE;
+  if (slot_mapping && !aligned(slot_mapping, 8)) return PI_ERR_MISALIGNED;
+  const attn::AppendArgs app{k_new, v_new, slot_mapping, new_stride};
+  return attn::attn_dispatch(out, q, k_pool, v_pool, block_tables, bt_stride, ctx_lens, batch,
+                             num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
+                             dtype, q_stride, out_stride, workspace, workspace_bytes, err, stream,
+                             &app);
 }
 
 // ---------------------------------------------------------------------------------

@@ -94,10 +94,11 @@ def decode_step_paged_batched(weights: DenseWeights, config: ModelConfig, store:
         # request has its own position, so apply it per row via the seq axis.
         q = rope_positions(cos, sin, pos_t, q.transpose(0, 1)).transpose(0, 1)
         k = rope_positions(cos, sin, pos_t, k.transpose(0, 1)).transpose(0, 1)
-        kernels.kv_index_copy(gpu.k_phys, gpu.v_phys, k[:, 0].to(gpu.dtype), v[:, 0].to(gpu.dtype),
-                              slots[l])
+        # one launch per layer: write the new K/V rows, then attend
         attn = kernels.paged_decode_attention(q[:, 0].contiguous().to(gpu.dtype), gpu.k_phys,
-                                              gpu.v_phys, tables.tables[l], ctx)
+                                              gpu.v_phys, tables.tables[l], ctx,
+                                              k_new=k[:, 0].to(gpu.dtype), v_new=v[:, 0].to(gpu.dtype),
+                                              slot_mapping=slots[l])
         attn = attn.to(dt).view(B, 1, cfg.n_heads * cfg.head_dim)
         x = x + linear(attn, weights[p + "self_attn.o_proj.weight"])
         h = rms_norm(x, weights[p + "post_attention_layernorm.weight"])

@@ -170,11 +170,18 @@ def paged_decode_attention(
     out: torch.Tensor | None = None,
     workspace: Workspace | None = None,
     err: torch.Tensor | None = None,
+    k_new: torch.Tensor | None = None,
+    v_new: torch.Tensor | None = None,
+    slot_mapping: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Decode attention of q [B, Hq, D] over each request's first ctx_lens[b] tokens.
 
     block_tables: int32 [B, max_pages] page ids; ctx_lens: int32 [B]. Returns
     out [B, Hq, D] in the pool dtype (fp32 softmax/accumulation inside).
+
+    With k_new / v_new [B, Hkv, D] and slot_mapping int64 [B], the step's new rows
+    are first written at their slots (the kv_index_copy semantics) in the same
+    launch: a whole decode layer's KV path is then one kernel.
     """
     P, Hkv, S, D = _check_pool(k_pool, "k_pool")
     if v_pool.shape != k_pool.shape or v_pool.dtype != k_pool.dtype:
@@ -206,9 +213,33 @@ def paged_decode_attention(
         scale = 1.0 / math.sqrt(D)
     nbytes = workspace_bytes(B, Hq, Hkv, D)
     ws = (workspace or default_workspace(q.device)).get(nbytes)
+    if k_new is None and v_new is None and slot_mapping is None:
+        _capi.call(
+            "pi_paged_decode_attn",
+            out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+            block_tables.data_ptr(), block_tables.stride(0), ctx_lens.data_ptr(),
+            B, Hq, Hkv, D, S, P, float(scale), dtype_code(q.dtype), q.stride(0), out.stride(0),
+            ws.data_ptr(), ws.numel(), _err_ptr(err), _stream(),
+        )
+        return out
+    # Fused append: write one new K/V row per request, then attend (one launch).
+    if k_new is None or v_new is None or slot_mapping is None:
+        raise ValueError("k_new, v_new and slot_mapping go together")
+    if k_new.shape != (B, Hkv, D) or v_new.shape != (B, Hkv, D):
+        raise ValueError(f"k_new/v_new must be [{B}, {Hkv}, {D}]")
+    if k_new.dtype != k_pool.dtype or v_new.dtype != k_pool.dtype:
+        raise TypeError("new K/V rows must have the pool dtype")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (B,):
+        raise ValueError("slot_mapping must be int64 [B]")
+    _require_cuda(k_new, v_new, slot_mapping)
+    if not (k_new.stride(2) == 1 and k_new.stride(1) == D and v_new.stride() == k_new.stride()):
+        k_new = k_new.contiguous()
+        v_new = v_new.contiguous()
+    slot_mapping = slot_mapping.contiguous()
     _capi.call(
-        "pi_paged_decode_attn",
-        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        "pi_paged_decode_attn_append",
+        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_new.data_ptr(),
+        v_new.data_ptr(), slot_mapping.data_ptr(), k_new.stride(0),
         block_tables.data_ptr(), block_tables.stride(0), ctx_lens.data_ptr(),
         B, Hq, Hkv, D, S, P, float(scale), dtype_code(q.dtype), q.stride(0), out.stride(0),
         ws.data_ptr(), ws.numel(), _err_ptr(err), _stream(),

@@ -175,3 +175,29 @@ def test_paged_attention_v1_decode_semantics(causal: bool) -> None:
     ref = _oracle(q, kp, vp, tables, eff, 16)
     assert out.shape == (1, 1, 8, 128)
     assert_close(out[0].float().cpu().numpy(), ref, ATOL, RTOL)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_append_equals_copy_then_attend(dtype: torch.dtype) -> None:
+    # One decode layer: write each request's new row at position ctx-1, then attend.
+    ctx = [1, 17, 100, 513, 2048, 33, 16, 4000]
+    S, Hq, Hkv, D = 16, 32, 8, 128
+    q, kp, vp, tables = _random_batch(12, len(ctx), Hq, Hkv, D, S, ctx, dtype)
+    g = torch.Generator().manual_seed(3)
+    k_new = torch.randn((len(ctx), Hkv, D), generator=g).to(dtype).to(DEV)
+    v_new = torch.randn((len(ctx), Hkv, D), generator=g).to(dtype).to(DEV)
+    slots = [orc.slot_of(t, c - 1, S) for t, c in zip(tables, ctx)]
+    slots[2] = -1  # a request without a new row this step
+    slot_t = torch.tensor(slots, dtype=torch.int64, device=DEV)
+    bt = _tables_tensor(tables)
+    ctx_t = torch.tensor(ctx, dtype=torch.int32, device=DEV)
+    kp2, vp2 = kp.clone(), vp.clone()
+    kernels.kv_index_copy(kp, vp, k_new, v_new, slot_t)
+    ref = kernels.paged_decode_attention(q, kp, vp, bt, ctx_t)
+    out = kernels.paged_decode_attention(q, kp2, vp2, bt, ctx_t, k_new=k_new, v_new=v_new,
+                                         slot_mapping=slot_t)
+    torch.cuda.synchronize()
+    assert torch.equal(kp2, kp) and torch.equal(vp2, vp)
+    assert torch.equal(out, ref)
+    # and against the oracle on the updated pool
+    assert_close(out.float().cpu().numpy(), _oracle(q, kp, vp, tables, ctx, S), *_tol(dtype))
