@@ -120,7 +120,7 @@ __device__ __forceinline__ int clamp_pages(int ctx, int S, int64_t bt_stride) {
   return static_cast<int>(n);
 }
 
-template <typename T, int D, int S, int NS>
+template <typename T, int D, int S, int NS, bool kAppend>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_attn_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                  const __grid_constant__ CUtensorMap tmap_v, const FastParams p) {
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // after this store; the warp that consumes that page patches the row in shared
   // memory from the source instead, so the result never depends on the order.
   constexpr int kRowChunks = D / 8;  // 16-byte chunks per head row
-  if (p.slot_mapping != nullptr) {
+  if constexpr (kAppend) {
     for (int i = gw; i < B * Hkv; i += NW) {
       const int b = i / Hkv;
       const int h = i - b * Hkv;
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int tile = __shfl_sync(kFull, id_cur, static_cast<int>(pos - pbase));
     if (lane == 0) {
-      s_tile[warp * NS + stage] = tile;
+      if constexpr (kAppend) s_tile[warp * NS + stage] = tile;
       const uint32_t bar = bar0 + 8 * stage;
       const uint32_t kdst = tiles_u32 + stage * C::kStageBytes;
       const uint32_t vdst = kdst + C::kTileBytes;
@@ -433,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       l0 = l1 = 0.f;
       piece_start = pos;
       fresh = false;
-      if (p.slot_mapping != nullptr) {
+      if constexpr (kAppend) {
         // Fused append: fetch this head's new K/V row now (lane c holds 16-byte chunk
         // c of [K row | V row]) so the patch below never waits on memory.
         const int64_t s = __ldg(p.slot_mapping + cb);
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     }
-    if (patch_tile >= 0 && s_tile[warp * NS + stage] == patch_tile) {
+    if (kAppend && patch_tile >= 0 && s_tile[warp * NS + stage] == patch_tile) {
       // This stage holds the page of the request's new slot: overwrite that row of
       // the K and V tiles with the new values (swizzled like the TMA box).
       uint8_t* kt = tiles + (warp * NS + stage) * C::kStageBytes;
@@ -816,13 +816,16 @@ int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, in
                 int dtype, cudaStream_t stream) {
   constexpr int NS = stages_for<D, S>();
   static_assert(fast_smem_bytes<D, S, NS>() <= 227 * 1024, "shared memory budget");
-  auto kern = paged_decode_attn_tma_kernel<T, D, S, NS>;
+  const bool append = fp.slot_mapping != nullptr;
+  auto kern = append ? paged_decode_attn_tma_kernel<T, D, S, NS, true>
+                     : paged_decode_attn_tma_kernel<T, D, S, NS, false>;
   constexpr size_t smem = fast_smem_bytes<D, S, NS>();
-  static int configured_ctas[64] = {0};  // per device: CTAs per SM (0 = not yet)
+  static int configured_ctas[2][64] = {{0}};  // per variant and device: CTAs per SM (0 = unset)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return PI_ERR_CUDA;
   if (dev < 0 || dev >= 64) return PI_ERR_UNSUPPORTED;
-  if (configured_ctas[dev] == 0) {
+  int* configured = &configured_ctas[append ? 1 : 0][dev];
+  if (*configured == 0) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return PI_ERR_CUDA;
@@ -830,13 +833,13 @@ int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, in
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess)
       return PI_ERR_CUDA;
     if (occ < 1) return PI_ERR_UNSUPPORTED;
-    configured_ctas[dev] = occ < kMaxCtasPerSm ? occ : kMaxCtasPerSm;
+    *configured = occ < kMaxCtasPerSm ? occ : kMaxCtasPerSm;
   }
   CUtensorMap tk, tv;
   if (!pool_tensor_map(&tk, k_pool, static_cast<uint64_t>(rows), D, S, dtype) ||
       !pool_tensor_map(&tv, v_pool, static_cast<uint64_t>(rows), D, S, dtype))
     return PI_ERR_CUDA;
-  const unsigned grid = static_cast<unsigned>(device_sm_count() * configured_ctas[dev]);
+  const unsigned grid = static_cast<unsigned>(device_sm_count() * *configured);
   kern<<<grid, kThreads, smem, stream>>>(tk, tv, fp);
   return cuda_status(cudaGetLastError());
 }
