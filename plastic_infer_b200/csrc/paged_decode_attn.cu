@@ -103,8 +103,7 @@ constexpr int stages_for() {
 template <int D, int S, int NS>
 constexpr size_t fast_smem_bytes() {
   return 1024 /* alignment slack */ + static_cast<size_t>(kWarps) * NS * Cfg<D, S>::kStageBytes +
-         static_cast<size_t>(kWarps) * NS * 8 /* mbarriers */ + (kMaxBatch + 1) * 4 +
-         static_cast<size_t>(kWarps) * NS * 4 /* tile held by each stage */;
+         static_cast<size_t>(kWarps) * NS * 8 /* mbarriers */ + (kMaxBatch + 1) * 4;
 }
 
 // Byte offset of element (t, d) inside a swizzled [boxes][S][128 B] tile.
@@ -131,7 +130,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* tiles = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + kWarps * NS * C::kStageBytes);
   int* s_poff = reinterpret_cast<int*>(bars + kWarps * NS);
-  int* s_tile = s_poff + kMaxBatch + 1;  // [kWarps][NS] tile index loaded into each stage
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -198,7 +196,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // after this store; the warp that consumes that page patches the row in shared
   // memory from the source instead, so the result never depends on the order.
   constexpr int kRowChunks = D / 8;  // 16-byte chunks per head row
-  if constexpr (kAppend) {
+  auto append_rows = [&]() {
+    if constexpr (!kAppend) return;
     for (int i = gw; i < B * Hkv; i += NW) {
       const int b = i / Hkv;
       const int h = i - b * Hkv;
@@ -219,12 +218,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint4*>(static_cast<T*>(is_v ? p.v_pool_w : p.k_pool_w) + dst + cc * 8) = val;
       }
     }
-  }
+  };
 
   // Partition over at most `total` warps so every active warp owns >= 1 page: a
   // segment's pieces are then exactly the warps [first, last] that overlap it.
   const int NWe = static_cast<int>(total < NW ? total : NW);
-  if (gw >= NWe) return;
+  if (gw >= NWe) {
+    append_rows();
+    return;
+  }
   const int64_t lo = total * gw / NWe;
   const int64_t hi = total * (gw + 1) / NWe;
 
@@ -269,7 +271,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int tile = __shfl_sync(kFull, id_cur, static_cast<int>(pos - pbase));
     if (lane == 0) {
-      if constexpr (kAppend) s_tile[warp * NS + stage] = tile;
       const uint32_t bar = bar0 + 8 * stage;
       const uint32_t kdst = tiles_u32 + stage * C::kStageBytes;
       const uint32_t vdst = kdst + C::kTileBytes;
@@ -285,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int64_t issued = lo;
   for (int s = 0; s < NS && issued < hi; ++s, ++issued) issue(issued, s);
+  append_rows();  // while the first pages are in flight
 
   // Lane-constant pieces of the fragment addressing.
   const int gid = lane >> 2;   // row group (token for S^T, d for O^T)
@@ -312,10 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool failed = false;
   int64_t pos = lo;
   int k = 0;
-  // Fused append: the tile (page_id * Hkv + h) holding the current segment's new
-  // slot (-1: none), the row inside it, and this lane's share of the new K/V row.
+  // Fused append: the index (in the request's block table) of the page holding the
+  // current segment's new slot (-1: none), the row inside it, and this lane's share
+  // of the new K/V row.
   constexpr int kPatch = (2 * kRowChunks + 31) / 32;
-  int patch_tile = -1;
+  int patch_idx = -1;
   int patch_row = 0;
   uint4 patch_val[kPatch];
 
@@ -434,16 +437,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       piece_start = pos;
       fresh = false;
       if constexpr (kAppend) {
-        // Fused append: fetch this head's new K/V row now (lane c holds 16-byte chunk
-        // c of [K row | V row]) so the patch below never waits on memory.
+        // Fused append: find which of this request's pages holds its new slot and
+        // fetch this head's new K/V row now (lane c holds 16-byte chunk c of
+        // [K row | V row]) so the per-page check is a register compare.
         const int64_t s = __ldg(p.slot_mapping + cb);
-        patch_tile = (s >= 0 && s < p.num_pages * S) ? static_cast<int>(s / S) * Hkv + ch : -1;
+        patch_idx = -1;
         patch_row = static_cast<int>(s % S);
+        if (s >= 0 && s < p.num_pages * S) {
+          const int slot_page = static_cast<int>(s / S);
+          const int32_t* row = p.block_tables + static_cast<int64_t>(cb) * p.bt_stride;
+          const int last = cn - 1;  // decode appends at position ctx-1: the last page
+          if (__ldg(row + last) == slot_page) {
+            patch_idx = last;
+          } else {
+            for (int j0 = 0; j0 < cn && patch_idx < 0; j0 += 32) {
+              const bool hit = j0 + lane < cn && __ldg(row + j0 + lane) == slot_page;
+              const unsigned m = __ballot_sync(kFull, hit);
+              if (m) patch_idx = j0 + __ffs(m) - 1;
+            }
+          }
+        }
         const int64_t src = static_cast<int64_t>(cb) * p.new_stride + static_cast<int64_t>(ch) * D;
 #pragma unroll
         for (int e = 0; e < kPatch; ++e) {
           const int c = lane + 32 * e;
-          if (patch_tile >= 0 && c < 2 * kRowChunks) {
+          if (patch_idx >= 0 && c < 2 * kRowChunks) {
             const bool is_v = c >= kRowChunks;
             const int cc = is_v ? c - kRowChunks : c;
             patch_val[e] = *reinterpret_cast<const uint4*>(
@@ -477,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     }
-    if (kAppend && patch_tile >= 0 && s_tile[warp * NS + stage] == patch_tile) {
+    if (kAppend && cp == patch_idx) {
       // This stage holds the page of the request's new slot: overwrite that row of
       // the K and V tiles with the new values (swizzled like the TMA box).
       uint8_t* kt = tiles + (warp * NS + stage) * C::kStageBytes;

@@ -188,6 +188,7 @@ def test_fused_append_equals_copy_then_attend(dtype: torch.dtype) -> None:
     v_new = torch.randn((len(ctx), Hkv, D), generator=g).to(dtype).to(DEV)
     slots = [orc.slot_of(t, c - 1, S) for t, c in zip(tables, ctx)]
     slots[2] = -1  # a request without a new row this step
+    slots[4] = orc.slot_of(tables[4], 700, S)  # a rewrite inside the context, not at its end
     slot_t = torch.tensor(slots, dtype=torch.int64, device=DEV)
     bt = _tables_tensor(tables)
     ctx_t = torch.tensor(ctx, dtype=torch.int32, device=DEV)
