@@ -425,7 +425,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     # e2e through the public API with pinned host buffers
     e2e = None
-    if world == 1 and not args.skip_e2e:
+    if not args.skip_e2e:
         e2e = run_e2e(wl, args, stream)
 
     idx = bench_index_copy(dev, peaks["hbm_gbs"]) if (world == 1 and not args.skip_c2) else None
@@ -476,10 +476,15 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
     """
     from plastic_infer_b200 import kernels
 
+    # Each rank feeds its own shard (its KV heads' new rows and its query heads) from
+    # its own pinned buffers; with N > 1 the per-layer outputs are all-gathered and
+    # rank 0 reads the gathered [B, Hq, D] result back.
     q_h = wl.q.cpu().pin_memory()
     kn_h = wl.k_new.cpu().pin_memory()
     vn_h = wl.v_new.cpu().pin_memory()
-    out_h = torch.empty(wl.out.shape, dtype=wl.out.dtype, pin_memory=True)
+    result = wl.gathered if wl.world > 1 else wl.out
+    read_back = wl.world == 1 or int(os.environ.get("RANK", "0")) == 0
+    out_h = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
     q_d, kn_d, vn_d = torch.empty_like(wl.q), torch.empty_like(wl.k_new), torch.empty_like(wl.v_new)
     slots_d = torch.empty_like(wl.slots)
     ctx_d = torch.empty_like(wl.ctx_lens)
@@ -508,17 +513,25 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                 kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
                 kernels.paged_decode_attention(q_d[l], wl.k_pool, wl.v_pool, wl.block_tables[l],
                                                ctx_d, out=wl.out[l], workspace=wl.ws)
+            if wl.world > 1:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(wl.gathered[l], wl.out[l])
             ev_out[l].record(stream)
-        with torch.cuda.stream(d2h):
-            for l in range(L):
-                d2h.wait_event(ev_out[l])
-                out_h[l].copy_(wl.out[l], non_blocking=True)
-        stream.wait_stream(d2h)
+        if read_back:
+            with torch.cuda.stream(d2h):
+                for l in range(L):
+                    d2h.wait_event(ev_out[l])
+                    out_h[l].copy_(result[l], non_blocking=True)
+            stream.wait_stream(d2h)
 
     for _ in range(args.warmup):
         step()
-    ms = time_region(step, args.steps, stream)
-    h2d = sum(t.numel() * t.element_size() for t in (q_h, kn_h, vn_h, wl.slots_host, wl.ctx_host))
+    barrier(wl.world)
+    ms = max_over_ranks(time_region(step, args.steps, stream), wl.world)
+    # whole job: every rank copies its shard in; rank 0 reads the result out
+    h2d = wl.world * sum(t.numel() * t.element_size()
+                         for t in (q_h, kn_h, vn_h, wl.slots_host, wl.ctx_host))
     d2h = out_h.numel() * out_h.element_size()
     return dict(value=round(wl.cfg["batch"] * args.steps / (ms * 1e-3), 1), unit="tok/s",
                 h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
