@@ -395,7 +395,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             print(json.dumps(dict(profile=True, layers=cfg["layers"], steps=args.steps,
                                   attn_bytes_per_launch=int(wl.attn_bytes()))), flush=True)
         return
-    use_graph = world == 1
+    # The whole step (and at N > 1 its per-layer NCCL all-gathers) is one CUDA graph;
+    # graphs are dropped before the process group is destroyed.
+    use_graph = not args.no_graph
     step_fn = wl.step
     if use_graph:
         g_step = graph_of(wl.step)
@@ -465,6 +467,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    # release graphs (they may hold NCCL work) before the process group goes away
+    step_fn = attn_fn = copy_fn = None
+    if use_graph:
+        del g_step, ga, gc
+    torch.cuda.synchronize()
+    barrier(world)
 
 
 def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
@@ -564,6 +572,7 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
     ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
+    ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python")
     ap.add_argument("--fused", action="store_true",
                     help="one fused append+attention launch per layer instead of index-copy "
                          "then attention (measured slower today: 202.9 vs 197.5 us per layer)")

@@ -12,6 +12,7 @@ call raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 
 from . import _build
@@ -86,7 +87,9 @@ class KernelError(RuntimeError):
 
 
 def lib_path() -> str:
-    return str(_build.LIB_PATH)
+    """The in-tree library, or the file named by PLASTIC_KV_LIB (e.g. a build with
+    other compile-time tunables)."""
+    return os.environ.get("PLASTIC_KV_LIB") or str(_build.LIB_PATH)
 
 
 def load() -> ctypes.CDLL:
@@ -97,12 +100,13 @@ def load() -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        if not _build.LIB_PATH.exists():
+        path = lib_path()
+        if not os.path.exists(path):
             raise RuntimeError(
-                f"{_build.LIB_PATH} is not built; run `python -m plastic_infer_b200._build` "
+                f"{path} is not built; run `python -m plastic_infer_b200._build` "
                 "(the paged-KV path has no CPU or PyTorch fallback)"
             )
-        lib = ctypes.CDLL(str(_build.LIB_PATH))
+        lib = ctypes.CDLL(path)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.restype = res

@@ -44,7 +44,14 @@
 namespace pi {
 namespace attn {
 
-constexpr int kWarps = 4;            // warps per CTA (each an independent consumer)
+// Compile-time tunables (the defaults are the measured best on B200).
+#ifndef PI_ATTN_WARPS
+#define PI_ATTN_WARPS 4
+#endif
+#ifndef PI_ATTN_MAX_STAGES
+#define PI_ATTN_MAX_STAGES 4
+#endif
+constexpr int kWarps = PI_ATTN_WARPS;  // warps per CTA (each an independent consumer)
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxBatch = 4096;      // prefix table lives in shared memory
 constexpr int kMaxKvHeads = 64;      // arrival counters: kMaxBatch x kMaxKvHeads
@@ -95,9 +102,9 @@ struct Cfg {
 // ~2x the bytes in flight that HBM latency needs at D = 128, 16-token pages).
 template <int D, int S>
 constexpr int stages_for() {
-  constexpr int budget = 200 * 1024 - (kMaxBatch + 1) * 4 - 1024;
+  constexpr int budget = 224 * 1024 - (kMaxBatch + 1) * 4 - 1024 - kWarps * 8 * 8;
   constexpr int n = budget / (kWarps * Cfg<D, S>::kStageBytes);
-  return n < 1 ? 1 : (n > 4 ? 4 : n);
+  return n < 1 ? 1 : (n > PI_ATTN_MAX_STAGES ? PI_ATTN_MAX_STAGES : n);
 }
 
 template <int D, int S, int NS>
@@ -117,6 +124,59 @@ __device__ __forceinline__ int clamp_pages(int ctx, int S, int64_t bt_stride) {
   int64_t n = (static_cast<int64_t>(c) + S - 1) / S;
   if (n > bt_stride) n = bt_stride;
   return static_cast<int>(n);
+}
+
+// Last-arriver merge of the partial results (m, l, O) of one (request, KV head)
+// segment cut across `npieces` warps: out = sum_j w_j O_j / sum_j w_j l_j with
+// w_j = 2^(m_j - max m). Kept out of line: it runs at most once per segment and its
+// accumulators must not weigh on the page loop's register allocation.
+template <typename T, int D>
+__device__ __noinline__ void merge_pieces(T* ob, const float* ws_ml, const float* ws_o, int wa,
+                                          int npieces, int role_a, int G, int lane) {
+  // All heads at once: lanes split into G groups of `lph` lanes, lane = (head g,
+  // column chunk); every load of a phase is independent, so the merge costs two
+  // memory round trips whatever G and the piece count are.
+  const int gp = G <= 1 ? 1 : (G <= 2 ? 2 : (G <= 4 ? 4 : 8));
+  const int lph = (32 / gp) * 4 <= D ? 32 / gp : D / 4;  // lanes per head, >= 1 float4 each
+  const int g = lane / lph;
+  const int n4 = D / (4 * lph);      // float4 per lane
+  const int d0 = (lane % lph) * 4 * n4;
+  if (g >= G) return;
+  auto slot_of = [&](int j) { return static_cast<int64_t>(wa + j) * 2 + (j == 0 ? role_a : 0); };
+  float M = -INFINITY;
+  for (int j = 0; j < npieces; ++j) M = fmaxf(M, __ldcg(ws_ml + slot_of(j) * kHeadsPad * 2 + g * 2));
+  float L = 0.f;
+  float4 acc[D / 16];  // n4 <= D / 16 (G = 8)
+#pragma unroll
+  for (int e = 0; e < D / 16; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < npieces; ++j) {
+    const int64_t sl = slot_of(j);
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(ws_ml + sl * kHeadsPad * 2 + g * 2));
+    const float w = fast_exp2(ml.x - M);
+    L += w * ml.y;
+    const float4* src = reinterpret_cast<const float4*>(ws_o + sl * kHeadsPad * D + g * D + d0);
+#pragma unroll
+    for (int e = 0; e < D / 16; ++e) {
+      if (e < n4) {
+        const float4 v = __ldcg(src + e);
+        acc[e].x += w * v.x;
+        acc[e].y += w * v.y;
+        acc[e].z += w * v.z;
+        acc[e].w += w * v.w;
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int e = 0; e < D / 16; ++e) {
+    if (e < n4) {
+      T* o = ob + g * D + d0 + 4 * e;
+      o[0] = from_f32<T>(acc[e].x * inv);
+      o[1] = from_f32<T>(acc[e].y * inv);
+      o[2] = from_f32<T>(acc[e].z * inv);
+      o[3] = from_f32<T>(acc[e].w * inv);
+    }
+  }
 }
 
 template <typename T, int D, int S, int NS, bool kAppend>
@@ -385,32 +445,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (old != npieces - 1) return;
     __threadfence();
     const int role_a = (total * wa / NWe == seg_start) ? 0 : 1;
-    T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(cb) * p.out_stride +
-            static_cast<int64_t>(ch) * G * D;
-    for (int g = 0; g < G; ++g) {
-      float M = -INFINITY;
-      for (int j = 0; j < npieces; ++j) {
-        const int64_t sl = static_cast<int64_t>(wa + j) * 2 + (j == 0 ? role_a : 0);
-        M = fmaxf(M, __ldcg(p.ws_ml + sl * kHeadsPad * 2 + g * 2));
-      }
-      float L = 0.f;
-      float acc[D / 32];
-#pragma unroll
-      for (int e = 0; e < D / 32; ++e) acc[e] = 0.f;
-      for (int j = 0; j < npieces; ++j) {
-        const int64_t sl = static_cast<int64_t>(wa + j) * 2 + (j == 0 ? role_a : 0);
-        const float mj = __ldcg(p.ws_ml + sl * kHeadsPad * 2 + g * 2);
-        const float lj = __ldcg(p.ws_ml + sl * kHeadsPad * 2 + g * 2 + 1);
-        const float w = fast_exp2(mj - M);
-        L += w * lj;
-        const float* src = p.ws_o + sl * kHeadsPad * D + g * D;
-#pragma unroll
-        for (int e = 0; e < D / 32; ++e) acc[e] += w * __ldcg(src + lane + 32 * e);
-      }
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-      for (int e = 0; e < D / 32; ++e) ob[g * D + lane + 32 * e] = from_f32<T>(acc[e] * inv);
-    }
+    merge_pieces<T, D>(static_cast<T*>(p.out) + static_cast<int64_t>(cb) * p.out_stride +
+                           static_cast<int64_t>(ch) * G * D,
+                       p.ws_ml, p.ws_o, wa, npieces, role_a, G, lane);
     if (lane == 0) p.ws_cnt[cb * Hkv + ch] = 0;
   };
 
@@ -436,6 +473,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       l0 = l1 = 0.f;
       piece_start = pos;
       fresh = false;
+      {
+        // Pull the next segment's query rows into L2 now, so its start does not wait
+        // a full DRAM round trip (segments follow (request, head) order).
+        const int64_t seg_end = static_cast<int64_t>(s_poff[cb]) * Hkv +
+                                static_cast<int64_t>(ch + 1) * cn;
+        if (seg_end < hi) {
+          const int nh = ch + 1 < Hkv ? ch + 1 : 0;
+          const int nb = ch + 1 < Hkv ? cb : cb + 1;
+          const char* nq = reinterpret_cast<const char*>(
+              static_cast<const T*>(p.q) + static_cast<int64_t>(nb) * p.q_stride +
+              static_cast<int64_t>(nh) * G * D);
+          if (lane * 128 < G * D * static_cast<int>(sizeof(T)))
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(nq + lane * 128));
+        }
+      }
       if constexpr (kAppend) {
         // Fused append: find which of this request's pages holds its new slot and
         // fetch this head's new K/V row now (lane c holds 16-byte chunk c of
@@ -833,7 +885,10 @@ template <typename T, int D, int S>
 int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, int64_t rows,
                 int dtype, cudaStream_t stream) {
   constexpr int NS = stages_for<D, S>();
-  static_assert(fast_smem_bytes<D, S, NS>() <= 227 * 1024, "shared memory budget");
+  if constexpr (fast_smem_bytes<D, S, NS>() > 227 * 1024) {
+    // Not even one stage per warp fits with this many warps per CTA.
+    return PI_ERR_UNSUPPORTED;
+  } else {
   const bool append = fp.slot_mapping != nullptr;
   auto kern = append ? paged_decode_attn_tma_kernel<T, D, S, NS, true>
                      : paged_decode_attn_tma_kernel<T, D, S, NS, false>;
@@ -860,6 +915,7 @@ int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, in
   const unsigned grid = static_cast<unsigned>(device_sm_count() * *configured);
   kern<<<grid, kThreads, smem, stream>>>(tk, tv, fp);
   return cuda_status(cudaGetLastError());
+  }
 }
 
 }  // namespace attn

@@ -84,3 +84,21 @@ def test_partition_covers_and_merges(seed: int) -> None:
         for slot in expect:
             assert slot not in slots_written, "two partials share a workspace slot"
             slots_written.add(slot)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("G", range(1, 9))
+def test_merge_lane_map_covers_every_output_once(G: int, D: int) -> None:
+    # merge_pieces: lane -> (head g, columns d0 .. d0 + 4*n4), lanes with g >= G idle.
+    gp = 1 if G <= 1 else 2 if G <= 2 else 4 if G <= 4 else 8
+    lph = 32 // gp if (32 // gp) * 4 <= D else D // 4
+    n4 = D // (4 * lph)
+    assert 1 <= n4 <= D // 16
+    seen = np.zeros((G, D), dtype=int)
+    for lane in range(32):
+        g = lane // lph
+        if g >= G:
+            continue
+        d0 = (lane % lph) * 4 * n4
+        seen[g, d0:d0 + 4 * n4] += 1
+    assert (seen == 1).all()
