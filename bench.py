@@ -46,6 +46,22 @@ METRIC = "decode tok/s (Qwen3-8B shape, paged KV); index-copy GB/s vs HBM peak"
 C3 = dict(layers=36, batch=64, hq=32, hkv=8, head_dim=128, page_size=16, ctx_lo=512,
           ctx_hi=8192, seed=0)
 C2 = dict(pages=65536, page_size=16, hkv=8, head_dim=128, batches=(1, 64, 512, 4096, 65536))
+C3["desc"] = ("C3 qwen3-8b-shape paged decode KV path: 36 layers x (index-copy of 64 new K/V "
+              "rows + paged GQA decode attention), B=64, ctx U[512,8192] seed 0, 32q/8kv heads, "
+              "head_dim 128, page 16")
+# the attention/KV path of a Qwen3-30B-A3B-shape MoE decode step
+# (the expert FFN is outside the path).
+C4 = dict(layers=48, batch=128, hq=32, hkv=4, head_dim=128, page_size=16, ctx_lo=256,
+          ctx_hi=4096, seed=0,
+          desc="C4 qwen3-30b-a3b-shape paged decode KV path: 48 layers x (index-copy of 128 new "
+               "K/V rows + paged GQA decode attention, G=8), B=128, ctx U[256,4096] seed 0, "
+               "32q/4kv heads, head_dim 128, page 16",
+          metric="decode tok/s (Qwen3-30B-A3B shape, paged KV attention path)")
+# long-context offload. Device pool = 25% of all pages; layers
+# stream in from the pinned host KV store (LRU at layer granularity) on a side stream.
+C5 = dict(layers=36, batch=8, hq=32, hkv=8, head_dim=128, page_size=16, ctx=32768,
+          pool_frac=0.25, seed=0)
+WORKLOADS = {"c3": C3, "c4": C4}
 
 
 def measured_peaks() -> dict:
@@ -369,15 +385,188 @@ def run_c2_only(args, dev: torch.device) -> None:
     print(json.dumps(dict(profile=True, c2_batches=list(C2["batches"]))), flush=True)
 
 
+class OffloadWorkload:
+    """C5: decode over a KV cache four times larger than the device pool.
+
+    All K/V pages live in a pinned host store [layer][page] (the host KV store of
+    src/plastic_infer/kv/kv_store.py:185-406, here at page granularity, physical
+    layout). The device pool holds 25% of them. A layer must be resident to be
+    attended; a missing layer is brought in on the copy stream (one host->device copy
+    into a staging buffer, then page_scatter into free pool pages), evicting the least
+    recently used resident layer after writing its dirty pages (the pages that
+    received this step's new tokens) back to the host. Loads of the next layers
+    overlap the attention of the current one.
+    """
+
+    def __init__(self, cfg: dict, dev: torch.device) -> None:
+        from plastic_infer_b200 import kernels
+
+        self.k = kernels
+        self.cfg = cfg
+        self.dev = dev
+        L, B, S, D, H, Hq = (cfg[x] for x in ("layers", "batch", "page_size", "head_dim", "hkv", "hq"))
+        self.L, self.B, self.S = L, B, S
+        self.npg = cfg["ctx"] // S                    # pages per request per layer
+        self.per_layer = B * self.npg                 # pages per layer
+        self.pool_pages = int(cfg["pool_frac"] * L * self.per_layer)
+        self.slots_per_pool = self.pool_pages // self.per_layer
+        assert self.slots_per_pool >= 3, "pool must hold at least three layers"
+        page_shape = (H, S, D)
+        # host store, pinned, filled with random bf16 values layer by layer
+        self.kh = torch.empty((L, self.per_layer, *page_shape), dtype=torch.bfloat16, pin_memory=True)
+        self.vh = torch.empty_like(self.kh, pin_memory=True)
+        g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+        tmp = torch.empty((self.per_layer, *page_shape), dtype=torch.bfloat16, device=dev)
+        for l in range(L):
+            self.kh[l].copy_(tmp.normal_(generator=g))
+            self.vh[l].copy_(tmp.normal_(generator=g))
+        del tmp
+        self.k_pool = torch.empty((self.pool_pages, *page_shape), dtype=torch.bfloat16, device=dev)
+        self.v_pool = torch.empty_like(self.k_pool)
+        self.stage_k = [torch.empty((self.per_layer, *page_shape), dtype=torch.bfloat16, device=dev)
+                        for _ in range(2)]
+        self.stage_v = [torch.empty_like(self.stage_k[0]) for _ in range(2)]
+        self.q = torch.randn((L, B, Hq, D), dtype=torch.bfloat16, device=dev, generator=g)
+        self.k_new = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+        self.v_new = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+        self.out = torch.empty((L, B, Hq, D), dtype=torch.bfloat16, device=dev)
+        self.ctx = torch.full((B,), cfg["ctx"], dtype=torch.int32, device=dev)
+        self.ws = kernels.Workspace(dev)
+        self.copy_stream = torch.cuda.Stream(device=dev)
+        self.free = list(range(self.pool_pages - 1, -1, -1))
+        self.resident: dict[int, np.ndarray] = {}     # layer -> device page ids [per_layer]
+        self.tables: dict[int, torch.Tensor] = {}     # layer -> block table [B, npg]
+        self.slot: dict[int, torch.Tensor] = {}       # layer -> new-token slots [B]
+        self.loaded: dict[int, torch.cuda.Event] = {}
+        self.done: dict[int, torch.cuda.Event] = {}
+        self.lru: list[int] = []                      # resident layers, least recent first
+        self.stage_i = 0
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+
+    def _evict_one(self, keep: set) -> None:
+        v = next(x for x in self.lru if x not in keep)
+        self.lru.remove(v)
+        ids = self.resident.pop(v)
+        # write the dirty pages (the last page of every request got this step's token)
+        cs = self.copy_stream
+        cs.wait_event(self.done[v])
+        with torch.cuda.stream(cs):
+            for b in range(self.B):
+                j = b * self.npg + self.npg - 1
+                pid = int(ids[j])
+                self.kh[v, j].copy_(self.k_pool[pid], non_blocking=True)
+                self.vh[v, j].copy_(self.v_pool[pid], non_blocking=True)
+                self.d2h_bytes += 2 * self.k_pool[pid].numel() * 2
+        self.free.extend(int(x) for x in ids)
+        self.tables.pop(v)
+        self.slot.pop(v)
+
+    def load(self, l: int, keep: set) -> None:
+        if l in self.resident:
+            return
+        while len(self.free) < self.per_layer:
+            self._evict_one(keep)
+        ids = np.array([self.free.pop() for _ in range(self.per_layer)], dtype=np.int32)
+        ids_d = torch.from_numpy(ids).to(self.dev, non_blocking=False)
+        i = self.stage_i
+        self.stage_i ^= 1
+        cs = self.copy_stream
+        with torch.cuda.stream(cs):
+            self.stage_k[i].copy_(self.kh[l], non_blocking=True)
+            self.stage_v[i].copy_(self.vh[l], non_blocking=True)
+            self.k.page_scatter(self.stage_k[i], ids_d, self.k_pool)
+            self.k.page_scatter(self.stage_v[i], ids_d, self.v_pool)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+        ids_d.record_stream(cs)
+        self.h2d_bytes += 2 * self.stage_k[i].numel() * 2
+        self.loaded[l] = ev
+        self.resident[l] = ids
+        self.lru.append(l)
+        self.tables[l] = torch.from_numpy(ids.reshape(self.B, self.npg)).to(self.dev)
+        last = ids.reshape(self.B, self.npg)[:, -1].astype(np.int64) * self.S + (self.S - 1)
+        self.slot[l] = torch.from_numpy(last).to(self.dev)
+
+    def step(self, ahead: int = 2) -> None:
+        cur = torch.cuda.current_stream()
+        for l in range(self.L):
+            for a in range(ahead + 1):
+                nxt = (l + a) % self.L
+                self.load(nxt, keep={(l + x) % self.L for x in range(ahead + 1)})
+            if l in self.lru:
+                self.lru.remove(l)
+                self.lru.append(l)
+            cur.wait_event(self.loaded[l])
+            self.k.kv_index_copy(self.k_pool, self.v_pool, self.k_new[l], self.v_new[l], self.slot[l])
+            self.k.paged_decode_attention(self.q[l], self.k_pool, self.v_pool, self.tables[l], self.ctx,
+                                          out=self.out[l], workspace=self.ws)
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            self.done[l] = ev
+
+
+def run_c5(args, rank: int, world: int, dev: torch.device) -> None:
+    """C5 long-context offload line (rank 0, one GPU)."""
+    if rank != 0:
+        return
+    cfg = dict(C5)
+    if args.layers:
+        cfg["layers"] = args.layers
+    # link peak of this box: pinned 1 GiB host->device copy
+    h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    d.copy_(h)
+    torch.cuda.synchronize()
+    link = 1.0 / (time_region(lambda: d.copy_(h, non_blocking=True), 3,
+                              torch.cuda.current_stream()) / 3 * 1e-3) * (1 << 30) / 1e9
+    del h, d
+    wl = OffloadWorkload(cfg, dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(1, args.warmup)):
+        wl.step()
+    torch.cuda.synchronize()
+    wl.h2d_bytes = wl.d2h_bytes = 0
+    with ClockSampler(dev.index or 0) as clk:
+        ms = time_region(wl.step, args.steps, stream)
+    ms_step = ms / args.steps
+    h2d = wl.h2d_bytes / args.steps
+    d2h = wl.d2h_bytes / args.steps
+    link_gbs = h2d / (ms_step * 1e-3) / 1e9
+    line = dict(
+        metric="decode tok/s (long-context host offload, Qwen3-8B attention shape)",
+        value=round(cfg["batch"] * args.steps / (ms * 1e-3), 2), unit="tok/s", n_gpus=1,
+        steps=args.steps, warmup=args.warmup, ms_per_step=round(ms_step, 2), higher_is_better=True,
+        scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic",
+        config=dict(workload="C5 long-context offload: B=8 x 32768 tokens, 36 layers, 32q/8kv heads, "
+                    "head_dim 128, page 16; device pool = 25% of all pages; layer-granular LRU "
+                    "over a pinned host store; loads (H2D + page_scatter) on a side stream "
+                    "overlapped with index-copy + attention; dirty pages written back D2H",
+                    pool_pages=wl.pool_pages, pages_per_layer=wl.per_layer,
+                    host_store_gb=round(2 * wl.kh.numel() * 2 / 1e9, 1)),
+        roofline=dict(bound="host link", achieved=round(link_gbs, 1), peak=round(link, 1),
+                      unit="GB/s", frac=round(link_gbs / link, 3),
+                      peak_source="pinned 1 GiB host->device copy measured in this run"),
+        h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
+        gpu_launches=args.steps * cfg["layers"] * 4,
+        clocks=clk.summary(),
+    )
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     if args.c2_only:
         run_c2_only(args, dev)
         return
+    if args.workload == "c5":
+        run_c5(args, rank, world, dev)
+        return
     peaks = measured_peaks()
-    cfg = dict(C3)
-    cfg["layers"] = args.layers
+    cfg = dict(WORKLOADS[args.workload])
+    if args.layers:
+        cfg["layers"] = args.layers
     wl = DecodeWorkload(cfg, rank, world, dev)
     wl.fused = args.fused
     stream = torch.cuda.current_stream()
@@ -432,19 +621,21 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if not args.skip_e2e:
         e2e = run_e2e(wl, args, stream)
 
-    idx = bench_index_copy(dev, peaks["hbm_gbs"]) if (world == 1 and not args.skip_c2) else None
+    idx = (bench_index_copy(dev, peaks["hbm_gbs"])
+           if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
     cpu = cpu_baseline_sample(cfg) if (rank == 0 and world == 1 and not args.skip_cpu) else None
 
     traffic = _profile_traffic()
     if rank == 0:
         line = dict(
-            metric=METRIC, value=round(value, 1), unit="tok/s", n_gpus=world, steps=args.steps,
+            metric=cfg.get("metric", METRIC), value=round(value, 1), unit="tok/s", n_gpus=world,
+            steps=args.steps,
             warmup=args.warmup, ms_per_step=round(ms_step, 4), higher_is_better=True,
             scaling="strong", vs_baseline=None, dtype="bf16", data="synthetic",
-            config=dict(workload="C3 qwen3-8b-shape paged decode KV path: 36 layers x "
-                        "(index-copy of 64 new K/V rows + paged GQA decode attention), "
-                        "B=64, ctx U[512,8192] seed 0, 32q/8kv heads, head_dim 128, page 16",
-                        global_batch=cfg["batch"], layers=cfg["layers"], seq_len="ragged 512-8192",
+            config=dict(workload=cfg["desc"] + ("" if cfg["layers"] == WORKLOADS[args.workload]["layers"]
+                                                 else f" (profiling run: {cfg['layers']} layers)"),
+                        global_batch=cfg["batch"], layers=cfg["layers"],
+                        seq_len=f"ragged {cfg['ctx_lo']}-{cfg['ctx_hi']}",
                         parallelism=f"kv-head shard x{world}" if world > 1 else "single gpu",
                         kv_bytes_per_step=round(wl.attn_bytes() * cfg["layers"] * world / 1e9, 3),
                         l2="inputs larger than L2 (~41 GB KV per step), no flush",
@@ -569,8 +760,11 @@ def main() -> None:
     ap.add_argument("--skip-c2", action="store_true", help="skip the index-copy microbench")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the host-buffer e2e run")
-    ap.add_argument("--layers", type=int, default=C3["layers"],
-                    help="decoder layers per step (36 = Qwen3-8B; fewer only for profiling)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder layers per step (default: the workload's; fewer only for profiling)")
+    ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
+                    help="c3: Qwen3-8B shape (headline); c4: Qwen3-30B-A3B shape; "
+                         "c5: long-context host offload")
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
     ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
