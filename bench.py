@@ -625,7 +625,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
     cpu = cpu_baseline_sample(cfg) if (rank == 0 and world == 1 and not args.skip_cpu) else None
 
-    traffic = _profile_traffic()
+    # measured DRAM bytes per launch exist for the C3 single-GPU launch only
+    traffic = _profile_traffic() if (args.workload == "c3" and world == 1) else None
     if rank == 0:
         line = dict(
             metric=cfg.get("metric", METRIC), value=round(value, 1), unit="tok/s", n_gpus=world,
@@ -638,7 +639,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                         seq_len=f"ragged {cfg['ctx_lo']}-{cfg['ctx_hi']}",
                         parallelism=f"kv-head shard x{world}" if world > 1 else "single gpu",
                         kv_bytes_per_step=round(wl.attn_bytes() * cfg["layers"] * world / 1e9, 3),
-                        l2="inputs larger than L2 (~41 GB KV per step), no flush",
+                        l2=f"inputs larger than L2 "
+                           f"(~{wl.attn_bytes() * cfg['layers'] / 1e9:.0f} GB KV per step), no flush",
                         cuda_graph=use_graph),
             roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm_gbs"],
                           unit="GB/s", frac=round(achieved / peaks["hbm_gbs"], 4),
