@@ -151,6 +151,47 @@ int pi_paged_decode_attn_append(void* out, const void* q, void* k_pool, void* v_
                                 cudaStream_t stream);
 
 /*
+ * Multi-GPU decode attention with the all-gather fused into the kernel (no
+ * counterpart in the reference, which runs on one GPU; the exchange point is where
+ * the attention output meets o_proj, src/plastic_infer/exec/runner_paged.py:256-258).
+ *
+ * Each of `world` ranks holds the KV heads of one head shard and attends its own
+ * query heads (as pi_paged_decode_attn). Every rank owns a gathered-output buffer
+ * [world][batch][num_q_heads_local][head_dim] that all ranks have mapped (CUDA IPC);
+ * a rank writes its own slice of EVERY rank's buffer with NVLink peer stores as soon
+ * as each (request, KV head) row group is final. When all of a launch's stores have
+ * landed, the launch writes `epoch` into peer_flags[r][rank] on every rank r. A
+ * launch with wait_epoch != 0 first waits (bounded, ~2 s; PI_ERR_TIMEOUT through
+ * `err` on expiry) until its own flags[r] >= wait_epoch for all r, i.e. until every
+ * rank's previous launch has delivered its slice here.
+ *
+ *   out           must be peer_out[rank] + rank * rank_stride (this rank's slice of its
+ *                 own gathered buffer); out_stride as for pi_paged_decode_attn
+ *   workspace     as for pi_paged_decode_attn (its zeroed block also holds the
+ *                 launch-completion counter)
+ * Peer pointers are device addresses valid in this process (cudaIpcOpenMemHandle).
+ * Plain peer stores and flag writes only: no TMA or multicast access to peer memory.
+ */
+#define PI_MAX_PEERS 8
+typedef struct pi_peer_gather {
+  void* peer_out[PI_MAX_PEERS];
+  unsigned* peer_flags[PI_MAX_PEERS];
+  int rank;
+  int world;
+  int64_t rank_stride;
+  unsigned epoch;
+  unsigned wait_epoch;
+} pi_peer_gather_t;
+
+int pi_paged_decode_attn_gather(void* out, const void* q, const void* k_pool, const void* v_pool,
+                                const int32_t* block_tables, int64_t bt_stride,
+                                const int32_t* ctx_lens, int batch, int num_q_heads,
+                                int num_kv_heads, int head_dim, int page_size, int64_t num_pages,
+                                float scale, int dtype, int64_t q_stride, int64_t out_stride,
+                                void* workspace, size_t workspace_bytes,
+                                const pi_peer_gather_t* gather, int* err, cudaStream_t stream);
+
+/*
  * Allocation-free pi_paged_decode_attn (no counterpart in the reference).
  *
  * For callers that cannot allocate device memory when they attend: a host loop

@@ -57,6 +57,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
          _i64, _i64, _vp, _sz, _vp, _vp],
     ),
+    "pi_paged_decode_attn_gather": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
+         _i64, _i64, _vp, _sz, _vp, _vp, _vp],
+    ),
     "pi_paged_decode_attn_append": (
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32,
@@ -72,6 +77,23 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pi_page_gather": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _i32, _i64, _vp, _vp]),
     "pi_page_scatter": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _i32, _i64, _vp, _vp]),
 }
+
+MAX_PEERS = 8  # PI_MAX_PEERS
+
+
+class PeerGather(ctypes.Structure):
+    """pi_peer_gather_t (include/plastic_kv.h)."""
+
+    _fields_ = [
+        ("peer_out", ctypes.c_void_p * MAX_PEERS),
+        ("peer_flags", ctypes.c_void_p * MAX_PEERS),
+        ("rank", ctypes.c_int),
+        ("world", ctypes.c_int),
+        ("rank_stride", ctypes.c_int64),
+        ("epoch", ctypes.c_uint),
+        ("wait_epoch", ctypes.c_uint),
+    ]
+
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

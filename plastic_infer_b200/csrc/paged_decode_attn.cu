@@ -85,6 +85,10 @@ struct FastParams {
   int64_t new_stride;
   void* k_pool_w;
   void* v_pool_w;
+  // Fused peer all-gather (kGather instances only): see pi_peer_gather_t; ag_done is
+  // the grid-completion counter kept in the workspace's zeroed block.
+  pi_peer_gather_t ag;
+  unsigned* ag_done;
 };
 
 template <int D, int S>
@@ -179,7 +183,38 @@ __device__ __noinline__ void merge_pieces(T* ob, const float* ws_ml, const float
   }
 }
 
-template <typename T, int D, int S, int NS, bool kAppend>
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Copy this rank's finished row group (G query heads x D of one request) from the
+// local gathered buffer to the same place in every peer's gathered buffer (16-byte
+// loads of what this warp just wrote, 16-byte NVLink stores).
+template <typename T, int D>
+__device__ __forceinline__ void push_row_group(const pi_peer_gather_t& ag, int64_t off, int G,
+                                               int lane) {
+  __syncwarp();
+  const int chunks = G * D * static_cast<int>(sizeof(T)) / 16;
+  const char* src = static_cast<const char*>(ag.peer_out[ag.rank]) +
+                    (static_cast<int64_t>(ag.rank) * ag.rank_stride + off) * sizeof(T);
+  for (int c = lane; c < chunks; c += 32) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + c);
+    for (int r = 0; r < ag.world; ++r) {
+      if (r == ag.rank) continue;
+      char* dst = static_cast<char*>(ag.peer_out[r]) +
+                  (static_cast<int64_t>(ag.rank) * ag.rank_stride + off) * sizeof(T);
+      reinterpret_cast<uint4*>(dst)[c] = v;
+    }
+  }
+}
+
+template <typename T, int D, int S, int NS, bool kAppend, bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_attn_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                  const __grid_constant__ CUtensorMap tmap_v, const FastParams p) {
@@ -197,6 +232,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int B = p.batch;
   const int Hkv = p.hkv;
   const int G = p.group;
+
+  if constexpr (kGather) {
+    // Wait until every rank's previous launch has delivered its slice here (the
+    // dependency o_proj of the previous layer would have). Bounded: a missing peer
+    // is reported, never waited on forever.
+    if (p.ag.wait_epoch != 0 && warp == 0 && lane < p.ag.world) {
+      const unsigned* f = p.ag.peer_flags[p.ag.rank] + lane;
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t i = 0;; ++i) {
+        if (static_cast<int>(ld_acquire_sys(f) - p.ag.wait_epoch) >= 0) break;
+        if (i > (1u << 24) || global_timer_ns() - t0 > 2000000000ull) {
+          record_error(p.err, PI_ERR_TIMEOUT);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  // Exit bookkeeping of the gather variant: the last warp of the grid to finish
+  // publishes `epoch` to every rank once all warps' peer stores are visible.
+  auto finish = [&]() {
+    if constexpr (kGather) {
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0) {
+        const unsigned total_warps = gridDim.x * kWarps;
+        const unsigned old = atomicAdd(p.ag_done, 1u);
+        if (old == total_warps - 1) {
+          *p.ag_done = 0u;
+          __threadfence_system();
+          for (int r = 0; r < p.ag.world; ++r)
+            st_release_sys(p.ag.peer_flags[r] + p.ag.rank, p.ag.epoch);
+        }
+      }
+    }
+  };
 
   // ---- per-CTA exclusive prefix of page counts over the batch --------------------
   {
@@ -248,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (s_poff[b + 1] == s_poff[b]) {
       T* o = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride;
       for (int i = lane; i < hq * D; i += 32) o[i] = from_f32<T>(0.f);
+      if constexpr (kGather) push_row_group<T, D>(p.ag, static_cast<int64_t>(b) * p.out_stride, hq, lane);
     }
   }
 
@@ -257,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // memory from the source instead, so the result never depends on the order.
   constexpr int kRowChunks = D / 8;  // 16-byte chunks per head row
   auto append_rows = [&]() {
-    if constexpr (!kAppend) return;
+    if constexpr (kAppend) {
     for (int i = gw; i < B * Hkv; i += NW) {
       const int b = i / Hkv;
       const int h = i - b * Hkv;
@@ -278,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint4*>(static_cast<T*>(is_v ? p.v_pool_w : p.k_pool_w) + dst + cc * 8) = val;
       }
     }
+    }
   };
 
   // Partition over at most `total` warps so every active warp owns >= 1 page: a
@@ -285,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int NWe = static_cast<int>(total < NW ? total : NW);
   if (gw >= NWe) {
     append_rows();
+    finish();
     return;
   }
   const int64_t lo = total * gw / NWe;
@@ -413,6 +487,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ob[g1 * D + d + 8] = from_f32<T>(o[mt][3] * i1);
         }
       }
+      if constexpr (kGather)
+        push_row_group<T, D>(p.ag, static_cast<int64_t>(cb) * p.out_stride +
+                                       static_cast<int64_t>(ch) * G * D, G, lane);
       return;
     }
     // Partial piece: publish (m, l, O) and let the last arriving warp merge.
@@ -448,6 +525,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     merge_pieces<T, D>(static_cast<T*>(p.out) + static_cast<int64_t>(cb) * p.out_stride +
                            static_cast<int64_t>(ch) * G * D,
                        p.ws_ml, p.ws_o, wa, npieces, role_a, G, lane);
+    if constexpr (kGather)
+      push_row_group<T, D>(p.ag, static_cast<int64_t>(cb) * p.out_stride +
+                                     static_cast<int64_t>(ch) * G * D, G, lane);
     if (lane == 0) p.ws_cnt[cb * Hkv + ch] = 0;
   };
 
@@ -666,6 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_bounded(bar0 + 8 * static_cast<int>(j % NS), static_cast<uint32_t>((j / NS) & 1));
     }
   }
+  finish();
 }
 
 // ---------------------------------------------------------------------------------
@@ -869,7 +950,10 @@ inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255);
 // a fixed size and position whatever the batch shape, so a launch of one shape can
 // never find partials of an earlier launch of another shape where its counters are:
 // zeroed once, it stays zero because every launch resets the counters it used.
-constexpr size_t kCounterBytes = static_cast<size_t>(kMaxBatch) * kMaxKvHeads * sizeof(int);
+// The last 256 bytes of the block hold the grid-completion counter of the gather
+// variant (it also returns to zero at the end of every launch).
+constexpr size_t kSegCounterBytes = static_cast<size_t>(kMaxBatch) * kMaxKvHeads * sizeof(int);
+constexpr size_t kCounterBytes = kSegCounterBytes + 256;
 
 Layout ws_layout(int head_dim, int sms) {
   Layout L;
@@ -890,14 +974,17 @@ int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, in
     return PI_ERR_UNSUPPORTED;
   } else {
   const bool append = fp.slot_mapping != nullptr;
-  auto kern = append ? paged_decode_attn_tma_kernel<T, D, S, NS, true>
-                     : paged_decode_attn_tma_kernel<T, D, S, NS, false>;
+  const bool gather = fp.ag.world > 0;
+  const int variant = gather ? 2 : (append ? 1 : 0);
+  auto kern = gather ? paged_decode_attn_tma_kernel<T, D, S, NS, false, true>
+                     : (append ? paged_decode_attn_tma_kernel<T, D, S, NS, true, false>
+                               : paged_decode_attn_tma_kernel<T, D, S, NS, false, false>);
   constexpr size_t smem = fast_smem_bytes<D, S, NS>();
-  static int configured_ctas[2][64] = {{0}};  // per variant and device: CTAs per SM (0 = unset)
+  static int configured_ctas[3][64] = {{0}};  // per variant and device: CTAs per SM (0 = unset)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return PI_ERR_CUDA;
   if (dev < 0 || dev >= 64) return PI_ERR_UNSUPPORTED;
-  int* configured = &configured_ctas[append ? 1 : 0][dev];
+  int* configured = &configured_ctas[variant][dev];
   if (*configured == 0) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
@@ -948,7 +1035,7 @@ int attn_dispatch(void* out, const void* q, const void* k_pool, const void* v_po
                   int batch, int num_q_heads, int num_kv_heads, int head_dim, int page_size,
                   int64_t num_pages, float scale, int dtype, int64_t q_stride, int64_t out_stride,
                   void* workspace, size_t workspace_bytes, int* err, cudaStream_t stream,
-                  const AppendArgs* app) {
+                  const AppendArgs* app, const pi_peer_gather_t* ag = nullptr) {
   const int eb = elem_bytes_of(dtype);
   if (eb == 0) return PI_ERR_UNSUPPORTED;
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || page_size <= 0 ||
@@ -971,6 +1058,17 @@ int attn_dispatch(void* out, const void* q, const void* k_pool, const void* v_po
                     static_cast<int64_t>(batch) * bt_stride < (int64_t{1} << 31) &&
                     aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(q, 4) &&
                     q_stride % 2 == 0 && aligned(out, 2);
+  if (ag != nullptr) {
+    if (!fast) return PI_ERR_UNSUPPORTED;  // the peer all-gather lives in the TMA kernel only
+    if (ag->world < 1 || ag->world > PI_MAX_PEERS || ag->rank < 0 || ag->rank >= ag->world)
+      return PI_ERR_BAD_SHAPE;
+    if (ag->rank_stride < static_cast<int64_t>(batch) * out_stride) return PI_ERR_BAD_SHAPE;
+    for (int r = 0; r < ag->world; ++r)
+      if (ag->peer_out[r] == nullptr || ag->peer_flags[r] == nullptr) return PI_ERR_NULL_POINTER;
+    if (static_cast<char*>(ag->peer_out[ag->rank]) + ag->rank * ag->rank_stride * eb !=
+        static_cast<char*>(out))
+      return PI_ERR_BAD_SHAPE;  // out must be this rank's slice of its gathered buffer
+  }
   // The fused append stores whole 16-byte chunks of the new rows.
   const bool fuse = app != nullptr && fast && aligned(app->k_new, 16) &&
                     aligned(app->v_new, 16) && (app->new_stride * eb) % 16 == 0;
@@ -1010,6 +1108,15 @@ int attn_dispatch(void* out, const void* q, const void* k_pool, const void* v_po
     fp.new_stride = fuse ? app->new_stride : 0;
     fp.k_pool_w = const_cast<void*>(k_pool);
     fp.v_pool_w = const_cast<void*>(v_pool);
+    fp.ag = {};
+    fp.ag_done = reinterpret_cast<unsigned*>(ws + L.cnt_off + kSegCounterBytes);
+    if (ag != nullptr) {
+      // The gather output rows are pushed as 16-byte chunks of whole row groups.
+      if ((static_cast<int64_t>(group) * head_dim * eb) % 16 != 0 || (out_stride * eb) % 16 != 0 ||
+          (ag->rank_stride * eb) % 16 != 0)
+        return PI_ERR_MISALIGNED;
+      fp.ag = *ag;
+    }
 #define PI_FAST(T, D, S)                                                                  \
   if (head_dim == D && page_size == S)                                                    \
     return launch_fast<T, D, S>(fp, k_pool, v_pool, rows, dtype, stream);
@@ -1078,6 +1185,22 @@ extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool
                                  num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
                                  dtype, q_stride, out_stride, workspace, workspace_bytes, err,
                                  stream, nullptr);
+}
+
+extern "C" int pi_paged_decode_attn_gather(void* out, const void* q, const void* k_pool,
+                                           const void* v_pool, const int32_t* block_tables,
+                                           int64_t bt_stride, const int32_t* ctx_lens, int batch,
+                                           int num_q_heads, int num_kv_heads, int head_dim,
+                                           int page_size, int64_t num_pages, float scale,
+                                           int dtype, int64_t q_stride, int64_t out_stride,
+                                           void* workspace, size_t workspace_bytes,
+                                           const pi_peer_gather_t* gather, int* err,
+                                           cudaStream_t stream) {
+  if (gather == nullptr) return PI_ERR_NULL_POINTER;
+  return pi::attn::attn_dispatch(out, q, k_pool, v_pool, block_tables, bt_stride, ctx_lens, batch,
+                                 num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
+                                 dtype, q_stride, out_stride, workspace, workspace_bytes, err,
+                                 stream, nullptr, gather);
 }
 
 extern "C" int pi_paged_decode_attn_append(

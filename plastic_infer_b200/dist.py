@@ -102,3 +102,122 @@ def sharded_decode_attention(q: torch.Tensor, shard: HeadShard,
     paged_decode_attention kernel on GPU) and returns [B, Hq/N, D].
     """
     return gather_heads(attend(local_q(q, shard).contiguous()), shard, group)
+
+
+# ---------------------------------------------------------------------------------
+# Peer exchange: the all-gather fused into the attention kernel (NVLink peer stores)
+# ---------------------------------------------------------------------------------
+
+import ctypes  # noqa: E402
+
+_IPC_HANDLE_BYTES = 64
+_cudaIpcMemLazyEnablePeerAccess = 1
+
+
+class _IpcHandle(ctypes.Structure):
+    _fields_ = [("reserved", ctypes.c_char * _IPC_HANDLE_BYTES)]
+
+
+def _cudart() -> ctypes.CDLL:
+    """The CUDA runtime already loaded by torch (same SONAME), via ctypes."""
+    import torch  # noqa: F401  (makes sure torch's libcudart is loaded first)
+
+    lib = ctypes.CDLL("libcudart.so.12")
+    lib.cudaMalloc.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t]
+    lib.cudaFree.argtypes = [ctypes.c_void_p]
+    lib.cudaMemset.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t]
+    lib.cudaIpcGetMemHandle.argtypes = [ctypes.POINTER(_IpcHandle), ctypes.c_void_p]
+    lib.cudaIpcOpenMemHandle.argtypes = [ctypes.POINTER(ctypes.c_void_p), _IpcHandle, ctypes.c_uint]
+    lib.cudaIpcCloseMemHandle.argtypes = [ctypes.c_void_p]
+    return lib
+
+
+def _ck(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with cudaError {rc}")
+
+
+class _DevArray:
+    """__cuda_array_interface__ view of raw device memory (for torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str) -> None:
+        self.__cuda_array_interface__ = dict(shape=shape, typestr=typestr, data=(ptr, False),
+                                             version=3, strides=None)
+
+
+class PeerExchange:
+    """Gathered-output buffers that every rank maps, for pi_paged_decode_attn_gather.
+
+    Each rank cudaMallocs `slots` gathered-output buffers of [world, B, Hq/N, D] plus a
+    flag array, shares them with CUDA IPC, and opens every peer's (NVLink peer access).
+    Slots alternate per launch so a rank one layer ahead never overwrites an output
+    that a slower peer is still consuming; each launch waits for the previous launch
+    of every rank (`wait_epoch`) before it starts.
+    """
+
+    def __init__(self, batch: int, q_heads_local: int, head_dim: int, dtype, group=None,
+                 slots: int = 2) -> None:
+        import torch
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks (one NVSwitch domain)")
+        self.dtype = dtype
+        self.shape = (self.world * batch, q_heads_local, head_dim)
+        self.elem = torch.tensor([], dtype=dtype).element_size()
+        self.slot_elems = self.world * batch * q_heads_local * head_dim
+        self.rank_stride = batch * q_heads_local * head_dim
+        self.slots = slots
+        slot_bytes = (self.slot_elems * self.elem + 255) // 256 * 256
+        self.flag_off = slot_bytes * slots
+        self.nbytes = self.flag_off + 256
+        cu = _cudart()
+        self._cu = cu
+        base = ctypes.c_void_p()
+        _ck(cu.cudaMalloc(ctypes.byref(base), self.nbytes), "cudaMalloc")
+        _ck(cu.cudaMemset(base, 0, self.nbytes), "cudaMemset")
+        self.base = base.value
+        h = _IpcHandle()
+        _ck(cu.cudaIpcGetMemHandle(ctypes.byref(h), base), "cudaIpcGetMemHandle")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(h.reserved), group=group)
+        self.ptrs: list[int] = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self.base)
+                continue
+            peer = ctypes.c_void_p()
+            hr = _IpcHandle()
+            ctypes.memmove(ctypes.byref(hr), hb, _IPC_HANDLE_BYTES)
+            _ck(cu.cudaIpcOpenMemHandle(ctypes.byref(peer), hr, _cudaIpcMemLazyEnablePeerAccess),
+                "cudaIpcOpenMemHandle")
+            self.ptrs.append(peer.value)
+        self.slot_bytes = slot_bytes
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def slot_tensor(self, slot: int):
+        """This rank's local gathered buffer of `slot` as [world * B, Hq/N, D]."""
+        import torch
+
+        typestr = {2: "<f2", 4: "<f4"}[self.elem]
+        t = torch.as_tensor(_DevArray(self.base + slot * self.slot_bytes,
+                                      (self.slot_elems,), typestr), device="cuda")
+        return t.view(self.dtype).view(self.shape) if self.dtype != t.dtype else t.view(self.shape)
+
+    def close(self) -> None:
+        if self.base is None:
+            return
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._cu.cudaIpcCloseMemHandle(ctypes.c_void_p(p))
+        self._cu.cudaFree(ctypes.c_void_p(self.base))
+        self.base = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -20,6 +20,7 @@ non-zero status. Inputs must be CUDA tensors; there is no CPU path.
 
 from __future__ import annotations
 
+import ctypes
 import math
 import threading
 
@@ -305,3 +306,64 @@ def page_scatter(staging: torch.Tensor, page_ids: torch.Tensor, pool: torch.Tens
                  pages_per_group: int = 1, err: torch.Tensor | None = None) -> None:
     """pool pages <- staging (inverse of page_gather)."""
     _page_move("pi_page_scatter", pool, staging, page_ids, pages_per_group, err)
+
+
+# ---------------------------------------------------------------------------
+# e: decode attention with the all-gather fused in (multi-GPU, peer stores)
+# ---------------------------------------------------------------------------
+
+
+def paged_decode_attention_gather(
+    q: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_tables: torch.Tensor,
+    ctx_lens: torch.Tensor,
+    exchange,
+    scale: float | None = None,
+    workspace: Workspace | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """This rank's heads of decode attention, all-gathered across ranks in-kernel.
+
+    `exchange` is a dist.PeerExchange built for (B, Hq_local, D). Returns the gathered
+    [world * B, Hq_local, D] buffer (rank-major). The rows of other ranks are complete
+    once every rank has issued its next gather launch (each launch waits for the
+    previous launch of every rank before starting) or after a device synchronize plus
+    a process-group barrier.
+    """
+    P, Hkv, S, D = _check_pool(k_pool, "k_pool")
+    B, Hq, _ = q.shape
+    if q.dtype != k_pool.dtype or q.shape[2] != D:
+        raise ValueError("q must be [B, Hq_local, D] in the pool dtype")
+    if exchange.shape != (exchange.world * B, Hq, D) or exchange.dtype != q.dtype:
+        raise ValueError("exchange was built for another shape or dtype")
+    _require_cuda(q, k_pool, v_pool, block_tables, ctx_lens)
+    q = q.contiguous()
+    block_tables = block_tables.contiguous()
+    ctx_lens = ctx_lens.contiguous()
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    ex = exchange
+    ex.epoch += 1
+    slot = (ex.epoch - 1) % ex.slots
+    g = _capi.PeerGather()
+    for r in range(ex.world):
+        g.peer_out[r] = ex.ptrs[r] + slot * ex.slot_bytes
+        g.peer_flags[r] = ex.ptrs[r] + ex.flag_off
+    g.rank, g.world = ex.rank, ex.world
+    g.rank_stride = ex.rank_stride
+    g.epoch = ex.epoch
+    g.wait_epoch = ex.epoch - 1
+    gathered = ex.slot_tensor(slot)
+    out = gathered[ex.rank * B:(ex.rank + 1) * B]
+    nbytes = workspace_bytes(B, Hq, Hkv, D)
+    ws = (workspace or default_workspace(q.device)).get(nbytes)
+    _capi.call(
+        "pi_paged_decode_attn_gather",
+        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        block_tables.data_ptr(), block_tables.stride(0), ctx_lens.data_ptr(),
+        B, Hq, Hkv, D, S, P, float(scale), dtype_code(q.dtype), q.stride(0), out.stride(0),
+        ws.data_ptr(), ws.numel(), ctypes.byref(g), _err_ptr(err), _stream(),
+    )
+    return gathered

@@ -69,7 +69,8 @@ def test_host_validation_rejects_before_launch(lib: ctypes.CDLL) -> None:
     assert lib.pi_page_gather(fake, fake, fake, 1, 2, 24, 1, 4, None,
                               None) == _capi.PI_ERR_MISALIGNED
     assert lib.pi_page_scatter(None, None, None, 0, 2, 4096, 1, 4, None, None) == _capi.PI_OK
-    assert lib.pi_paged_decode_attn_ws_zero_bytes() == 4096 * 64 * 4
+    # arrival counters (4096 requests x 64 KV heads) + the grid-completion counter block
+    assert lib.pi_paged_decode_attn_ws_zero_bytes() == 4096 * 64 * 4 + 256
 
 
 def test_kernels_refuse_cpu_tensors() -> None:

@@ -1,0 +1,110 @@
+"""Multi-GPU KV-head sharding on real GPUs (row e): NCCL and the fused peer all-gather.
+
+Each rank (one process per GPU, NCCL) holds only its KV heads' pools, attends its
+query heads with the sm_100a kernel, and the outputs are gathered:
+  * through pi_paged_decode_attn_gather: the kernel pushes its finished row groups to
+    every peer's gathered buffer with NVLink stores and signals completion per launch;
+  * through dist.gather_heads (NCCL all-gather) as the reference point.
+Both must equal the unsharded single-GPU kernel on the full pools (bit-exact: the
+same kernel computes the same rows), for several consecutive launches (slots and
+epochs rotate). Skipped unless at least two GPUs are visible.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+NGPU = torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import datetime
+
+    import torch.distributed as dist
+
+    from plastic_infer_b200 import kernels
+    from plastic_infer_b200.dist import PeerExchange, gather_heads, head_shard
+
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        B, Hq, Hkv, D, S = 12, 32, 8, 128, 16
+        g = torch.Generator().manual_seed(0)
+        ctx = torch.randint(1, 900, (B,), generator=g)
+        ctx[0] = 0  # an empty request is gathered as zeros too
+        npg = (ctx + S - 1) // S
+        P = int(npg.sum()) + 4
+        perm = torch.randperm(P, generator=g)
+        bt = torch.zeros((B, int(npg.max())), dtype=torch.int32)
+        cur = 0
+        for b in range(B):
+            bt[b, :npg[b]] = perm[cur:cur + npg[b]].to(torch.int32)
+            cur += int(npg[b])
+        shard = head_shard(Hq, Hkv, world, rank)
+        ex = PeerExchange(B, shard.n_q, D, torch.bfloat16)
+        bt_d = bt.to(dev)
+        ctx_d = ctx.to(torch.int32).to(dev)
+        ok = True
+        for step in range(3):  # consecutive launches: slots and epochs rotate
+            q = torch.randn((B, Hq, D), generator=g).to(torch.bfloat16).to(dev)
+            kp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
+            vp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
+            full = kernels.paged_decode_attention(q, kp, vp, bt_d, ctx_d)
+            kpl = kp[:, shard.kv_lo:shard.kv_hi].contiguous()
+            vpl = vp[:, shard.kv_lo:shard.kv_hi].contiguous()
+            ql = q[:, shard.q_lo:shard.q_hi].contiguous()
+            gathered = kernels.paged_decode_attention_gather(ql, kpl, vpl, bt_d, ctx_d, ex)
+            torch.cuda.synchronize()
+            dist.barrier()
+            got = gathered.view(world, B, shard.n_q, D).permute(1, 0, 2, 3).reshape(B, Hq, D)
+            via_nccl = gather_heads(kernels.paged_decode_attention(ql, kpl, vpl, bt_d, ctx_d), shard)
+            ok &= bool(torch.equal(got, full)) and bool(torch.equal(via_nccl, full))
+        with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+            f.write("ok" if ok else "mismatch")
+        dist.barrier()
+        ex.close()
+        dist.destroy_process_group()
+    except Exception:
+        with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+            f.write(traceback.format_exc())
+        os._exit(3)
+
+
+@pytest.mark.skipif(NGPU < 2, reason="needs at least two GPUs")
+def test_peer_gather_equals_unsharded_and_nccl(tmp_path) -> None:
+    import torch.multiprocessing as mp
+
+    world = 2 if NGPU < 4 else (4 if NGPU < 8 else 8)
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+            p.join()
+    msgs = [(tmp_path / f"rank{r}.txt").read_text() if (tmp_path / f"rank{r}.txt").exists()
+            else "no result" for r in range(world)]
+    assert all(m == "ok" for m in msgs), msgs
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
