@@ -181,9 +181,17 @@ class DecodeWorkload:
         self.world = world
         self.fused = False
         self.gathered = None
+        self.exchange = None
         if world > 1:
             # rank-major [world * B, Hq/N, D] per layer (what o_proj would consume)
             self.gathered = torch.empty((L, world * B, self.hq, D), dtype=torch.bfloat16, device=dev)
+
+    def use_peer_gather(self) -> None:
+        """Gather through the kernel's NVLink peer stores (one slot per layer)."""
+        from plastic_infer_b200.dist import PeerExchange
+
+        self.exchange = PeerExchange(self.cfg["batch"], self.hq, self.cfg["head_dim"],
+                                     torch.bfloat16, slots=self.cfg["layers"])
 
     # algorithmic bytes of one attention launch (one layer) for this rank
     def attn_bytes(self) -> float:
@@ -199,6 +207,16 @@ class DecodeWorkload:
 
     def layer(self, l: int, attention: bool = True, copy: bool = True, gather: bool = True) -> None:
         k = self.kernels
+        if self.exchange is not None and attention and gather:
+            # N > 1: attention with the all-gather fused in (NVLink peer stores; the
+            # launch waits for every rank's previous launch before it starts)
+            if copy:
+                k.kv_index_copy(self.k_pool, self.v_pool, self.k_new[l], self.v_new[l],
+                                self.slots[l])
+            k.paged_decode_attention_gather(self.q[l], self.k_pool, self.v_pool,
+                                            self.block_tables[l], self.ctx_lens, self.exchange,
+                                            workspace=self.ws)
+            return
         if attention and copy and self.fused:
             # one launch: write the 64 new K/V rows, then attend
             k.paged_decode_attention(self.q[l], self.k_pool, self.v_pool, self.block_tables[l],
@@ -569,6 +587,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         cfg["layers"] = args.layers
     wl = DecodeWorkload(cfg, rank, world, dev)
     wl.fused = args.fused
+    if world > 1 and not args.nccl:
+        wl.use_peer_gather()
     stream = torch.cuda.current_stream()
 
     # warm-up (also configures kernels before graph capture)
@@ -637,7 +657,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                                  else f" (profiling run: {cfg['layers']} layers)"),
                         global_batch=cfg["batch"], layers=cfg["layers"],
                         seq_len=f"ragged {cfg['ctx_lo']}-{cfg['ctx_hi']}",
-                        parallelism=f"kv-head shard x{world}" if world > 1 else "single gpu",
+                        parallelism=(f"kv-head shard x{world}, "
+                                     + ("NCCL all-gather" if args.nccl else
+                                        "all-gather fused into the attention kernel (NVLink peer stores)")
+                                     if world > 1 else "single gpu"),
                         kv_bytes_per_step=round(wl.attn_bytes() * cfg["layers"] * world / 1e9, 3),
                         l2=f"inputs larger than L2 "
                            f"(~{wl.attn_bytes() * cfg['layers'] / 1e9:.0f} GB KV per step), no flush",
@@ -668,6 +691,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         del g_step, ga, gc
     torch.cuda.synchronize()
     barrier(world)
+    if wl.exchange is not None:
+        wl.exchange.close()
+        barrier(world)
 
 
 def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
@@ -685,9 +711,14 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
     q_h = wl.q.cpu().pin_memory()
     kn_h = wl.k_new.cpu().pin_memory()
     vn_h = wl.v_new.cpu().pin_memory()
+    L = wl.cfg["layers"]
     result = wl.gathered if wl.world > 1 else wl.out
-    read_back = wl.world == 1 or int(os.environ.get("RANK", "0")) == 0
     out_h = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
+    barrier_t = torch.zeros(1, device=wl.dev)
+    if wl.exchange is not None:
+        # one slot per layer: layer l's gathered output is slot l of this rank's buffer
+        result = [wl.exchange.slot_tensor(s) for s in range(L)]
+    read_back = wl.world == 1 or int(os.environ.get("RANK", "0")) == 0
     q_d, kn_d, vn_d = torch.empty_like(wl.q), torch.empty_like(wl.k_new), torch.empty_like(wl.v_new)
     slots_d = torch.empty_like(wl.slots)
     ctx_d = torch.empty_like(wl.ctx_lens)
@@ -708,7 +739,12 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                 ev_in[l].record(h2d)
         for l in range(L):
             stream.wait_event(ev_in[l])
-            if wl.fused:
+            if wl.exchange is not None:
+                kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
+                kernels.paged_decode_attention_gather(q_d[l], wl.k_pool, wl.v_pool,
+                                                      wl.block_tables[l], ctx_d, wl.exchange,
+                                                      workspace=wl.ws)
+            elif wl.fused:
                 kernels.paged_decode_attention(q_d[l], wl.k_pool, wl.v_pool, wl.block_tables[l],
                                                ctx_d, out=wl.out[l], workspace=wl.ws,
                                                k_new=kn_d[l], v_new=vn_d[l], slot_mapping=slots_d[l])
@@ -716,11 +752,18 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                 kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
                 kernels.paged_decode_attention(q_d[l], wl.k_pool, wl.v_pool, wl.block_tables[l],
                                                ctx_d, out=wl.out[l], workspace=wl.ws)
-            if wl.world > 1:
+            if wl.world > 1 and wl.exchange is None:
                 import torch.distributed as dist
 
                 dist.all_gather_into_tensor(wl.gathered[l], wl.out[l])
             ev_out[l].record(stream)
+        if wl.exchange is not None:
+            # every rank's last launch has pushed its slice once all ranks pass this point
+            import torch.distributed as dist
+
+            dist.all_reduce(barrier_t)
+            for l in range(L):
+                ev_out[l].record(stream)
         if read_back:
             with torch.cuda.stream(d2h):
                 for l in range(L):
@@ -771,6 +814,9 @@ def main() -> None:
                     help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
     ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python")
+    ap.add_argument("--nccl", action="store_true",
+                    help="N > 1: gather the per-layer outputs with NCCL all-gather instead of the "
+                         "kernel's NVLink peer stores")
     ap.add_argument("--fused", action="store_true",
                     help="one fused append+attention launch per layer instead of index-copy "
                          "then attention (measured slower today: 202.9 vs 197.5 us per layer)")
