@@ -115,7 +115,8 @@ _cudaIpcMemLazyEnablePeerAccess = 1
 
 
 class _IpcHandle(ctypes.Structure):
-    _fields_ = [("reserved", ctypes.c_char * _IPC_HANDLE_BYTES)]
+    # c_ubyte, not c_char: a c_char array reads back as a C string cut at the first NUL
+    _fields_ = [("reserved", ctypes.c_ubyte * _IPC_HANDLE_BYTES)]
 
 
 def _cudart() -> ctypes.CDLL:
@@ -182,7 +183,8 @@ class PeerExchange:
         h = _IpcHandle()
         _ck(cu.cudaIpcGetMemHandle(ctypes.byref(h), base), "cudaIpcGetMemHandle")
         handles: list = [None] * self.world
-        dist.all_gather_object(handles, bytes(h.reserved), group=group)
+        dist.all_gather_object(handles, ctypes.string_at(ctypes.addressof(h), _IPC_HANDLE_BYTES),
+                               group=group)
         self.ptrs: list[int] = []
         for r, hb in enumerate(handles):
             if r == self.rank:
