@@ -76,9 +76,23 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             dist.barrier()
             got = gathered.view(world, B, shard.n_q, D).permute(1, 0, 2, 3).reshape(B, Hq, D)
             via_nccl = gather_heads(kernels.paged_decode_attention(ql, kpl, vpl, bt_d, ctx_d), shard)
-            ok &= bool(torch.equal(got, full)) and bool(torch.equal(via_nccl, full))
+            # bit-exact reference: every shard attended on this GPU with the same kernel
+            # (same work split as on its owner rank), concatenated in rank order
+            parts = []
+            for r in range(world):
+                sr = head_shard(Hq, Hkv, world, r)
+                parts.append(kernels.paged_decode_attention(
+                    q[:, sr.q_lo:sr.q_hi].contiguous(), kp[:, sr.kv_lo:sr.kv_hi].contiguous(),
+                    vp[:, sr.kv_lo:sr.kv_hi].contiguous(), bt_d, ctx_d))
+            expect = torch.cat(parts, dim=1)
+            close = (got.float() - full.float()).abs().max().item()
+            if not (torch.equal(got, expect) and torch.equal(via_nccl, expect) and close < 2e-2):
+                ok = False
+                msg = (f"step {step}: fused==local {torch.equal(got, expect)} "
+                       f"nccl==local {torch.equal(via_nccl, expect)} max|fused-full| {close:.3e} "
+                       f"max|fused-local| {(got.float() - expect.float()).abs().max().item():.3e}")
         with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
-            f.write("ok" if ok else "mismatch")
+            f.write("ok" if ok else msg)
         dist.barrier()
         ex.close()
         dist.destroy_process_group()
