@@ -190,6 +190,8 @@ class DecodeWorkload:
         """Gather through the kernel's NVLink peer stores (one slot per layer)."""
         from plastic_infer_b200.dist import PeerExchange
 
+        if self.cfg["layers"] < 3:
+            raise SystemExit("the peer all-gather path needs at least 3 layers (output slots)")
         self.exchange = PeerExchange(self.cfg["batch"], self.hq, self.cfg["head_dim"],
                                      torch.bfloat16, slots=self.cfg["layers"])
 
@@ -604,11 +606,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             print(json.dumps(dict(profile=True, layers=cfg["layers"], steps=args.steps,
                                   attn_bytes_per_launch=int(wl.attn_bytes()))), flush=True)
         return
-    # At N = 1 the whole step is one CUDA graph. At N > 1 the step runs eagerly: a
-    # captured NCCL all-gather of the 512 KB per-layer output measured ~25 us per layer
-    # on B200 x2, slower than the eager launch sequence. Graphs are dropped before the
-    # process group is destroyed.
-    use_graph = not args.no_graph and world == 1
+    # The whole step is one CUDA graph at N = 1 and with the fused peer all-gather at
+    # N > 1 (its launches take their epochs from a device counter, so one capture
+    # replays every step). With --nccl the step runs eagerly: a captured NCCL
+    # all-gather of the 512 KB per-layer output measured ~25 us per layer on B200 x2,
+    # slower than the eager launch sequence. Graphs are dropped before the process
+    # group is destroyed.
+    use_graph = not args.no_graph and (world == 1 or wl.exchange is not None)
     step_fn = wl.step
     if use_graph:
         g_step = graph_of(wl.step)
@@ -714,7 +718,6 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
     L = wl.cfg["layers"]
     result = wl.gathered if wl.world > 1 else wl.out
     out_h = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
-    barrier_t = torch.zeros(1, device=wl.dev)
     if wl.exchange is not None:
         # one slot per layer: layer l's gathered output is slot l of this rank's buffer
         result = [wl.exchange.slot_tensor(s) for s in range(L)]
@@ -726,6 +729,7 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
     ev_in = [torch.cuda.Event() for _ in range(L)]
     ev_out = [torch.cuda.Event() for _ in range(L)]
+    ev_read = [torch.cuda.Event() for _ in range(L)]
 
     def step():
         h2d.wait_stream(stream)  # device inputs of the previous step are no longer read
@@ -739,6 +743,14 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                 ev_in[l].record(h2d)
         for l in range(L):
             stream.wait_event(ev_in[l])
+            if wl.exchange is not None and read_back:
+                # Peers store into this rank's slots without waiting for its reads: a
+                # peer's launch e starts once this rank has finished launch e - 1, so
+                # the read of a slot's previous output (launch e - L) must be done
+                # before this rank's launch e - 1 starts; waiting here for the read
+                # issued two launches back keeps that for L >= 3 and still lets each
+                # read overlap the next launch.
+                stream.wait_event(ev_read[(l - 2) % L])
             if wl.exchange is not None:
                 kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
                 kernels.paged_decode_attention_gather(q_d[l], wl.k_pool, wl.v_pool,
@@ -757,18 +769,13 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
 
                 dist.all_gather_into_tensor(wl.gathered[l], wl.out[l])
             ev_out[l].record(stream)
-        if wl.exchange is not None:
-            # every rank's last launch has pushed its slice once all ranks pass this point
-            import torch.distributed as dist
-
-            dist.all_reduce(barrier_t)
-            for l in range(L):
-                ev_out[l].record(stream)
-        if read_back:
-            with torch.cuda.stream(d2h):
-                for l in range(L):
+            if read_back:
+                # a gather launch ends once every rank's slice is here: read it now
+                with torch.cuda.stream(d2h):
                     d2h.wait_event(ev_out[l])
                     out_h[l].copy_(result[l], non_blocking=True)
+                    ev_read[l].record(d2h)
+        if read_back:
             stream.wait_stream(d2h)
 
     for _ in range(args.warmup):

@@ -160,10 +160,11 @@ int pi_paged_decode_attn_append(void* out, const void* q, void* k_pool, void* v_
  * [world][batch][num_q_heads_local][head_dim] that all ranks have mapped (CUDA IPC);
  * a rank writes its own slice of EVERY rank's buffer with NVLink peer stores as soon
  * as each (request, KV head) row group is final. When all of a launch's stores have
- * landed, the launch writes `epoch` into peer_flags[r][rank] on every rank r. A
- * launch with wait_epoch != 0 first waits (bounded, ~2 s; PI_ERR_TIMEOUT through
- * `err` on expiry) until its own flags[r] >= wait_epoch for all r, i.e. until every
- * rank's previous launch has delivered its slice here.
+ * landed, the launch writes `epoch` into peer_flags[r][rank] on every rank r, then
+ * waits (bounded, ~2 s; PI_ERR_TIMEOUT through `err` on expiry) until its own
+ * flags[r] >= epoch for all r. When the launch completes, the whole gathered buffer
+ * is in place for the work that follows it on `stream` (o_proj). Epochs increase by
+ * one per launch on every rank.
  *
  *   out           must be peer_out[rank] + rank * rank_stride (this rank's slice of its
  *                 own gathered buffer); out_stride as for pi_paged_decode_attn
@@ -171,6 +172,19 @@ int pi_paged_decode_attn_append(void* out, const void* q, void* k_pool, void* v_
  *                 launch-completion counter)
  * Peer pointers are device addresses valid in this process (cudaIpcOpenMemHandle).
  * Plain peer stores and flag writes only: no TMA or multicast access to peer memory.
+ *
+ * Output slots: consecutive launches must write different buffers (peer_out), so that
+ * a rank's stores for launch e never land in a buffer a peer still reads for launch
+ * e - 1; two buffers used alternately are enough, because launch e on any rank starts
+ * only after every rank has finished launch e - 1's work and hence the reads of
+ * launch e - 2's output that preceded it in stream order.
+ *
+ * Epochs from the device: with launch_counter != NULL (a word in this rank's own
+ * memory counting its completed gather launches, zero at start) `epoch` is ignored;
+ * a launch uses *launch_counter + 1 and stores it back. The arguments of every
+ * launch are then the same from step to step, so a sequence of launches can be
+ * captured in a CUDA graph and replayed (a sequence whose length is a multiple of the
+ * number of output slots keeps the alternation across replays).
  */
 #define PI_MAX_PEERS 8
 typedef struct pi_peer_gather {
@@ -180,7 +194,7 @@ typedef struct pi_peer_gather {
   int world;
   int64_t rank_stride;
   unsigned epoch;
-  unsigned wait_epoch;
+  unsigned* launch_counter;
 } pi_peer_gather_t;
 
 int pi_paged_decode_attn_gather(void* out, const void* q, const void* k_pool, const void* v_pool,

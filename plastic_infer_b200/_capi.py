@@ -34,7 +34,7 @@ PI_DTYPE_F32 = 0
 PI_DTYPE_BF16 = 1
 PI_DTYPE_F16 = 2
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int
@@ -91,7 +91,7 @@ class PeerGather(ctypes.Structure):
         ("world", ctypes.c_int),
         ("rank_stride", ctypes.c_int64),
         ("epoch", ctypes.c_uint),
-        ("wait_epoch", ctypes.c_uint),
+        ("launch_counter", ctypes.c_void_p),
     ]
 
 

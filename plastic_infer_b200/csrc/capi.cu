@@ -20,7 +20,7 @@ int device_sm_count() {
 
 }  // namespace pi
 
-extern "C" int pi_abi_version(void) { return 1; }
+extern "C" int pi_abi_version(void) { return 2; }
 
 extern "C" const char* pi_error_string(int code) {
   switch (code) {

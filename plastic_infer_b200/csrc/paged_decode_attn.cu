@@ -134,9 +134,19 @@ __device__ __forceinline__ int clamp_pages(int ctx, int S, int64_t bt_stride) {
 // segment cut across `npieces` warps: out = sum_j w_j O_j / sum_j w_j l_j with
 // w_j = 2^(m_j - max m). Kept out of line: it runs at most once per segment and its
 // accumulators must not weigh on the page loop's register allocation.
+// Where one finished row group (G query heads x D of one request) is written: this
+// rank's output, and in the gather variant the same rows of every peer's gathered
+// buffer (NVLink peer stores straight from registers).
+template <typename T>
+struct RowDsts {
+  T* p[PI_MAX_PEERS];
+  int n;
+};
+
 template <typename T, int D>
-__device__ __noinline__ void merge_pieces(T* ob, const float* ws_ml, const float* ws_o, int wa,
-                                          int npieces, int role_a, int G, int lane) {
+__device__ __noinline__ void merge_pieces(const RowDsts<T> dst, const float* ws_ml,
+                                          const float* ws_o, int wa, int npieces, int role_a,
+                                          int G, int lane) {
   // All heads at once: lanes split into G groups of `lph` lanes, lane = (head g,
   // column chunk); every load of a phase is independent, so the merge costs two
   // memory round trips whatever G and the piece count are.
@@ -171,14 +181,16 @@ __device__ __noinline__ void merge_pieces(T* ob, const float* ws_ml, const float
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (int k = 0; k < dst.n; ++k) {
 #pragma unroll
-  for (int e = 0; e < D / 16; ++e) {
-    if (e < n4) {
-      T* o = ob + g * D + d0 + 4 * e;
-      o[0] = from_f32<T>(acc[e].x * inv);
-      o[1] = from_f32<T>(acc[e].y * inv);
-      o[2] = from_f32<T>(acc[e].z * inv);
-      o[3] = from_f32<T>(acc[e].w * inv);
+    for (int e = 0; e < D / 16; ++e) {
+      if (e < n4) {
+        T* o = dst.p[k] + g * D + d0 + 4 * e;
+        o[0] = from_f32<T>(acc[e].x * inv);
+        o[1] = from_f32<T>(acc[e].y * inv);
+        o[2] = from_f32<T>(acc[e].z * inv);
+        o[3] = from_f32<T>(acc[e].w * inv);
+      }
     }
   }
 }
@@ -189,29 +201,9 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Copy this rank's finished row group (G query heads x D of one request) from the
-// local gathered buffer to the same place in every peer's gathered buffer (16-byte
-// loads of what this warp just wrote, 16-byte NVLink stores).
-template <typename T, int D>
-__device__ __forceinline__ void push_row_group(const pi_peer_gather_t& ag, int64_t off, int G,
-                                               int lane) {
-  __syncwarp();
-  const int chunks = G * D * static_cast<int>(sizeof(T)) / 16;
-  const char* src = static_cast<const char*>(ag.peer_out[ag.rank]) +
-                    (static_cast<int64_t>(ag.rank) * ag.rank_stride + off) * sizeof(T);
-  for (int c = lane; c < chunks; c += 32) {
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + c);
-    for (int r = 0; r < ag.world; ++r) {
-      if (r == ag.rank) continue;
-      char* dst = static_cast<char*>(ag.peer_out[r]) +
-                  (static_cast<int64_t>(ag.rank) * ag.rank_stride + off) * sizeof(T);
-      reinterpret_cast<uint4*>(dst)[c] = v;
-    }
-  }
+// Relaxed system-scope store: callers put the fence.sys that makes it a release.
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 template <typename T, int D, int S, int NS, bool kAppend, bool kGather>
@@ -233,40 +225,70 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int Hkv = p.hkv;
   const int G = p.group;
 
+  // Epoch of this gather launch: from the arguments, or one past this rank's launch
+  // counter (written only by the previous launch's last warp, so every thread of this
+  // launch reads the same value).
+  unsigned ag_epoch = 0;
   if constexpr (kGather) {
-    // Wait until every rank's previous launch has delivered its slice here (the
-    // dependency o_proj of the previous layer would have). Bounded: a missing peer
-    // is reported, never waited on forever.
-    if (p.ag.wait_epoch != 0 && warp == 0 && lane < p.ag.world) {
-      const unsigned* f = p.ag.peer_flags[p.ag.rank] + lane;
-      const uint64_t t0 = global_timer_ns();
-      for (uint32_t i = 0;; ++i) {
-        if (static_cast<int>(ld_acquire_sys(f) - p.ag.wait_epoch) >= 0) break;
-        if (i > (1u << 24) || global_timer_ns() - t0 > 2000000000ull) {
-          record_error(p.err, PI_ERR_TIMEOUT);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
+    ag_epoch = p.ag.launch_counter != nullptr ? __ldcg(p.ag.launch_counter) + 1u : p.ag.epoch;
   }
-  // Exit bookkeeping of the gather variant: the last warp of the grid to finish
-  // publishes `epoch` to every rank once all warps' peer stores are visible.
+  // Exit bookkeeping of the gather variant. The last warp of the grid to finish
+  // publishes `epoch` to every rank once all warps' peer stores are visible, then
+  // waits until every rank has published `epoch` here: when the launch completes, the
+  // whole gathered buffer is in place for whatever the stream runs next. Bounded: a
+  // missing peer is reported (PI_ERR_TIMEOUT), never waited on forever.
+  //
+  // Ordering: each warp's peer stores precede its completion count through a GPU-scope
+  // fence (release to the last warp, on the same GPU); the last warp's one system-scope
+  // fence then orders everything it has observed before its flag stores (causality
+  // order is transitive across the two scopes), so a rank that reads the flag with an
+  // acquire load sees every row of the launch.
   auto finish = [&]() {
     if constexpr (kGather) {
-      __threadfence_system();
+      __threadfence();
       __syncwarp();
+      unsigned last = 0;
       if (lane == 0) {
         const unsigned total_warps = gridDim.x * kWarps;
-        const unsigned old = atomicAdd(p.ag_done, 1u);
-        if (old == total_warps - 1) {
-          *p.ag_done = 0u;
-          __threadfence_system();
-          for (int r = 0; r < p.ag.world; ++r)
-            st_release_sys(p.ag.peer_flags[r] + p.ag.rank, p.ag.epoch);
+        last = atomicAdd(p.ag_done, 1u) == total_warps - 1;
+      }
+      if (last) {
+        // lane 0 observed every warp's count: its fence.sys + relaxed stores release
+        __threadfence_system();
+        *p.ag_done = 0u;
+        if (p.ag.launch_counter != nullptr) *p.ag.launch_counter = ag_epoch;
+        for (int r = 0; r < p.ag.world; ++r) st_relaxed_sys(p.ag.peer_flags[r] + p.ag.rank, ag_epoch);
+      }
+      last = __shfl_sync(kFull, last, 0);
+      if (last) {
+        if (lane < p.ag.world) {
+          const unsigned* f = p.ag.peer_flags[p.ag.rank] + lane;
+          const uint64_t t0 = global_timer_ns();
+          for (uint32_t i = 0;; ++i) {
+            if (static_cast<int>(ld_acquire_sys(f) - ag_epoch) >= 0) break;
+            if (i > (1u << 24) || global_timer_ns() - t0 > 2000000000ull) {
+              record_error(p.err, PI_ERR_TIMEOUT);
+              break;
+            }
+            if (i >= 4096u) __nanosleep(64);  // spin tight first: peers end within us
+          }
         }
       }
     }
+  };
+
+  // Destinations of the row group at element offset `off` of this rank's output.
+  auto row_dsts = [&](int64_t off) {
+    RowDsts<T> d;
+    d.p[0] = static_cast<T*>(p.out) + off;
+    d.n = 1;
+    if constexpr (kGather) {
+      for (int r = 0; r < p.ag.world; ++r)
+        if (r != p.ag.rank)
+          d.p[d.n++] = static_cast<T*>(p.ag.peer_out[r]) +
+                       static_cast<int64_t>(p.ag.rank) * p.ag.rank_stride + off;
+    }
+    return d;
   };
 
   // ---- per-CTA exclusive prefix of page counts over the batch --------------------
@@ -317,9 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Requests with no context produce zeros (SDPA over zero keys).
   for (int b = gw; b < B; b += NW) {
     if (s_poff[b + 1] == s_poff[b]) {
-      T* o = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.out_stride;
-      for (int i = lane; i < hq * D; i += 32) o[i] = from_f32<T>(0.f);
-      if constexpr (kGather) push_row_group<T, D>(p.ag, static_cast<int64_t>(b) * p.out_stride, hq, lane);
+      const RowDsts<T> dst = row_dsts(static_cast<int64_t>(b) * p.out_stride);
+      for (int k = 0; k < dst.n; ++k)
+        for (int i = lane; i < hq * D; i += 32) dst.p[k][i] = from_f32<T>(0.f);
     }
   }
 
@@ -471,25 +493,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t seg_end = seg_start + cn;
     const int g0 = 2 * tig, g1 = 2 * tig + 1;
     if (piece_start == seg_start && piece_end == seg_end) {
-      T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(cb) * p.out_stride +
-              static_cast<int64_t>(ch) * G * D;
+      const RowDsts<T> dst = row_dsts(static_cast<int64_t>(cb) * p.out_stride +
+                                      static_cast<int64_t>(ch) * G * D);
       const float i0 = lt0 > 0.f ? 1.f / lt0 : 0.f;
       const float i1 = lt1 > 0.f ? 1.f / lt1 : 0.f;
+      for (int k = 0; k < dst.n; ++k) {
+        T* ob = dst.p[k];
 #pragma unroll
-      for (int mt = 0; mt < C::kMT; ++mt) {
-        const int d = 16 * mt + gid;
-        if (g0 < G) {
-          ob[g0 * D + d] = from_f32<T>(o[mt][0] * i0);
-          ob[g0 * D + d + 8] = from_f32<T>(o[mt][2] * i0);
-        }
-        if (g1 < G) {
-          ob[g1 * D + d] = from_f32<T>(o[mt][1] * i1);
-          ob[g1 * D + d + 8] = from_f32<T>(o[mt][3] * i1);
+        for (int mt = 0; mt < C::kMT; ++mt) {
+          const int d = 16 * mt + gid;
+          if (g0 < G) {
+            ob[g0 * D + d] = from_f32<T>(o[mt][0] * i0);
+            ob[g0 * D + d + 8] = from_f32<T>(o[mt][2] * i0);
+          }
+          if (g1 < G) {
+            ob[g1 * D + d] = from_f32<T>(o[mt][1] * i1);
+            ob[g1 * D + d + 8] = from_f32<T>(o[mt][3] * i1);
+          }
         }
       }
-      if constexpr (kGather)
-        push_row_group<T, D>(p.ag, static_cast<int64_t>(cb) * p.out_stride +
-                                       static_cast<int64_t>(ch) * G * D, G, lane);
       return;
     }
     // Partial piece: publish (m, l, O) and let the last arriving warp merge.
@@ -522,12 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (old != npieces - 1) return;
     __threadfence();
     const int role_a = (total * wa / NWe == seg_start) ? 0 : 1;
-    merge_pieces<T, D>(static_cast<T*>(p.out) + static_cast<int64_t>(cb) * p.out_stride +
-                           static_cast<int64_t>(ch) * G * D,
+    merge_pieces<T, D>(row_dsts(static_cast<int64_t>(cb) * p.out_stride +
+                                static_cast<int64_t>(ch) * G * D),
                        p.ws_ml, p.ws_o, wa, npieces, role_a, G, lane);
-    if constexpr (kGather)
-      push_row_group<T, D>(p.ag, static_cast<int64_t>(cb) * p.out_stride +
-                                     static_cast<int64_t>(ch) * G * D, G, lane);
     if (lane == 0) p.ws_cnt[cb * Hkv + ch] = 0;
   };
 
@@ -1113,7 +1132,8 @@ int attn_dispatch(void* out, const void* q, const void* k_pool, const void* v_po
     if (ag != nullptr) {
       // The gather output rows are pushed as 16-byte chunks of whole row groups.
       if ((static_cast<int64_t>(group) * head_dim * eb) % 16 != 0 || (out_stride * eb) % 16 != 0 ||
-          (ag->rank_stride * eb) % 16 != 0)
+          (ag->rank_stride * eb) % 16 != 0 ||
+          (ag->launch_counter != nullptr && !aligned(ag->launch_counter, 4)))
         return PI_ERR_MISALIGNED;
       fp.ag = *ag;
     }

@@ -151,14 +151,24 @@ class PeerExchange:
 
     Each rank cudaMallocs `slots` gathered-output buffers of [world, B, Hq/N, D] plus a
     flag array, shares them with CUDA IPC, and opens every peer's (NVLink peer access).
-    Slots alternate per launch so a rank one layer ahead never overwrites an output
-    that a slower peer is still consuming; each launch waits for the previous launch
-    of every rank (`wait_epoch`) before it starts.
+    A launch completes only once every rank's slice of it has landed here, so the
+    gathered buffer can be read by whatever follows on the stream. Slots alternate per
+    launch so that a rank one launch ahead never overwrites an output a slower peer is
+    still reading (two slots suffice).
+
+    With `device_epochs` (the default) the epochs live in a launch counter in this
+    rank's buffer and the kernel advances it itself, so the arguments of the i-th
+    launch of a step are the same every step: a step of a multiple of `slots`
+    launches can be captured in a CUDA graph. Otherwise the host passes the epochs.
+    The per-slot argument blocks and output views are built once here, keeping the
+    per-launch host work to the kernel call.
     """
 
     def __init__(self, batch: int, q_heads_local: int, head_dim: int, dtype, group=None,
-                 slots: int = 2) -> None:
+                 slots: int = 2, device_epochs: bool = True) -> None:
         import torch
+
+        from . import _capi
 
         self.group = group
         self.rank = dist.get_rank(group)
@@ -197,17 +207,44 @@ class PeerExchange:
                 "cudaIpcOpenMemHandle")
             self.ptrs.append(peer.value)
         self.slot_bytes = slot_bytes
-        self.epoch = 0
+        # flags: one word per rank at flag_off; this rank's launch counter after them
+        self.counter_off = self.flag_off + 4 * _capi.MAX_PEERS
+        self.device_epochs = device_epochs
+        self.epoch = 0      # host epochs (device_epochs=False)
+        self.calls = 0      # launches issued from the host (slot rotation)
+        self.args = []
+        for slot in range(slots):
+            g = _capi.PeerGather()
+            for r in range(self.world):
+                g.peer_out[r] = self.ptrs[r] + slot * slot_bytes
+                g.peer_flags[r] = self.ptrs[r] + self.flag_off
+            g.rank, g.world, g.rank_stride = self.rank, self.world, self.rank_stride
+            g.launch_counter = self.base + self.counter_off if device_epochs else None
+            self.args.append(g)
+        self.views = [self._slot_view(s) for s in range(slots)]
         dist.barrier(group=group)
 
-    def slot_tensor(self, slot: int):
-        """This rank's local gathered buffer of `slot` as [world * B, Hq/N, D]."""
+    def _slot_view(self, slot: int):
         import torch
 
         typestr = {2: "<f2", 4: "<f4"}[self.elem]
         t = torch.as_tensor(_DevArray(self.base + slot * self.slot_bytes,
                                       (self.slot_elems,), typestr), device="cuda")
         return t.view(self.dtype).view(self.shape) if self.dtype != t.dtype else t.view(self.shape)
+
+    def slot_tensor(self, slot: int):
+        """This rank's local gathered buffer of `slot` as [world * B, Hq/N, D]."""
+        return self.views[slot]
+
+    def next_launch(self):
+        """(slot, argument block) of the next gather launch; advances the rotation."""
+        slot = self.calls % self.slots
+        self.calls += 1
+        g = self.args[slot]
+        if not self.device_epochs:
+            self.epoch += 1
+            g.epoch = self.epoch
+        return slot, g
 
     def close(self) -> None:
         if self.base is None:

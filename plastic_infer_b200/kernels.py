@@ -327,10 +327,9 @@ def paged_decode_attention_gather(
     """This rank's heads of decode attention, all-gathered across ranks in-kernel.
 
     `exchange` is a dist.PeerExchange built for (B, Hq_local, D). Returns the gathered
-    [world * B, Hq_local, D] buffer (rank-major). The rows of other ranks are complete
-    once every rank has issued its next gather launch (each launch waits for the
-    previous launch of every rank before starting) or after a device synchronize plus
-    a process-group barrier.
+    [world * B, Hq_local, D] buffer (rank-major), complete (every rank's rows) for the
+    work that follows on the current stream: the launch ends only after every rank's
+    slice has landed (bounded wait; `err` gets PI_ERR_TIMEOUT if a rank never launches).
     """
     P, Hkv, S, D = _check_pool(k_pool, "k_pool")
     B, Hq, _ = q.shape
@@ -345,16 +344,7 @@ def paged_decode_attention_gather(
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     ex = exchange
-    ex.epoch += 1
-    slot = (ex.epoch - 1) % ex.slots
-    g = _capi.PeerGather()
-    for r in range(ex.world):
-        g.peer_out[r] = ex.ptrs[r] + slot * ex.slot_bytes
-        g.peer_flags[r] = ex.ptrs[r] + ex.flag_off
-    g.rank, g.world = ex.rank, ex.world
-    g.rank_stride = ex.rank_stride
-    g.epoch = ex.epoch
-    g.wait_epoch = ex.epoch - 1
+    slot, g = ex.next_launch()
     gathered = ex.slot_tensor(slot)
     out = gathered[ex.rank * B:(ex.rank + 1) * B]
     nbytes = workspace_bytes(B, Hq, Hkv, D)

@@ -3,11 +3,14 @@
 Each rank (one process per GPU, NCCL) holds only its KV heads' pools, attends its
 query heads with the sm_100a kernel, and the outputs are gathered:
   * through pi_paged_decode_attn_gather: the kernel pushes its finished row groups to
-    every peer's gathered buffer with NVLink stores and signals completion per launch;
+    every peer's gathered buffer with NVLink stores and ends once every rank's slice
+    has landed, so the buffer is read in stream order right after the launch;
   * through dist.gather_heads (NCCL all-gather) as the reference point.
-Both must equal the unsharded single-GPU kernel on the full pools (bit-exact: the
-same kernel computes the same rows), for several consecutive launches (slots and
-epochs rotate). Skipped unless at least two GPUs are visible.
+Both must equal, bit for bit, every shard attended on one GPU by the same kernel and
+concatenated, and agree with the unsharded kernel within the attention tolerance, for
+consecutive launches (slots and epochs rotate), with epochs from the host and from the
+device counter, and for a CUDA graph of launches replayed with new inputs. Skipped
+unless at least two GPUs are visible.
 """
 
 from __future__ import annotations
@@ -59,23 +62,19 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             bt[b, :npg[b]] = perm[cur:cur + npg[b]].to(torch.int32)
             cur += int(npg[b])
         shard = head_shard(Hq, Hkv, world, rank)
-        ex = PeerExchange(B, shard.n_q, D, torch.bfloat16)
         bt_d = bt.to(dev)
         ctx_d = ctx.to(torch.int32).to(dev)
-        ok = True
-        for step in range(3):  # consecutive launches: slots and epochs rotate
+        ws = kernels.Workspace(dev)
+
+        def inputs():
             q = torch.randn((B, Hq, D), generator=g).to(torch.bfloat16).to(dev)
             kp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
             vp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
-            full = kernels.paged_decode_attention(q, kp, vp, bt_d, ctx_d)
-            kpl = kp[:, shard.kv_lo:shard.kv_hi].contiguous()
-            vpl = vp[:, shard.kv_lo:shard.kv_hi].contiguous()
-            ql = q[:, shard.q_lo:shard.q_hi].contiguous()
-            gathered = kernels.paged_decode_attention_gather(ql, kpl, vpl, bt_d, ctx_d, ex)
-            torch.cuda.synchronize()
-            dist.barrier()
-            got = gathered.view(world, B, shard.n_q, D).permute(1, 0, 2, 3).reshape(B, Hq, D)
-            via_nccl = gather_heads(kernels.paged_decode_attention(ql, kpl, vpl, bt_d, ctx_d), shard)
+            return (q, kp, vp, q[:, shard.q_lo:shard.q_hi].contiguous(),
+                    kp[:, shard.kv_lo:shard.kv_hi].contiguous(),
+                    vp[:, shard.kv_lo:shard.kv_hi].contiguous())
+
+        def expected(q, kp, vp):
             # bit-exact reference: every shard attended on this GPU with the same kernel
             # (same work split as on its owner rank), concatenated in rank order
             parts = []
@@ -84,17 +83,78 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
                 parts.append(kernels.paged_decode_attention(
                     q[:, sr.q_lo:sr.q_hi].contiguous(), kp[:, sr.kv_lo:sr.kv_hi].contiguous(),
                     vp[:, sr.kv_lo:sr.kv_hi].contiguous(), bt_d, ctx_d))
-            expect = torch.cat(parts, dim=1)
+            return torch.cat(parts, dim=1)
+
+        def as_heads(gathered):
+            return gathered.view(world, B, shard.n_q, D).permute(1, 0, 2, 3).reshape(B, Hq, D)
+
+        ok, msg = True, ""
+
+        def check(tag, got, q, kp, vp, nccl=None):
+            nonlocal ok, msg
+            expect = expected(q, kp, vp)
+            full = kernels.paged_decode_attention(q, kp, vp, bt_d, ctx_d)
             close = (got.float() - full.float()).abs().max().item()
-            if not (torch.equal(got, expect) and torch.equal(via_nccl, expect) and close < 2e-2):
+            good = torch.equal(got, expect) and close < 2e-2
+            if nccl is not None:
+                good = good and torch.equal(nccl, expect)
+            if not good and ok:
                 ok = False
-                msg = (f"step {step}: fused==local {torch.equal(got, expect)} "
-                       f"nccl==local {torch.equal(via_nccl, expect)} max|fused-full| {close:.3e} "
-                       f"max|fused-local| {(got.float() - expect.float()).abs().max().item():.3e}")
+                msg = (f"{tag}: fused==local {torch.equal(got, expect)} max|fused-full| "
+                       f"{close:.3e} max|fused-local| "
+                       f"{(got.float() - expect.float()).abs().max().item():.3e}")
+
+        # 1) device epochs, eager, consecutive launches (slots and epochs rotate). The
+        #    gathered buffer is read in stream order right after the launch: no
+        #    synchronize or barrier, the launch itself ends once every slice is here.
+        ex = PeerExchange(B, shard.n_q, D, torch.bfloat16)
+        for step in range(3):
+            q, kp, vp, ql, kpl, vpl = inputs()
+            snap = as_heads(kernels.paged_decode_attention_gather(
+                ql, kpl, vpl, bt_d, ctx_d, ex, workspace=ws)).clone()
+            via_nccl = gather_heads(kernels.paged_decode_attention(ql, kpl, vpl, bt_d, ctx_d), shard)
+            check(f"device-epoch step {step}", snap, q, kp, vp, via_nccl)
+
+        # 2) host epochs (launch_counter NULL): the same results
+        exh = PeerExchange(B, shard.n_q, D, torch.bfloat16, device_epochs=False)
+        for step in range(2):
+            q, kp, vp, ql, kpl, vpl = inputs()
+            snap = as_heads(kernels.paged_decode_attention_gather(
+                ql, kpl, vpl, bt_d, ctx_d, exh, workspace=ws)).clone()
+            check(f"host-epoch step {step}", snap, q, kp, vp)
+
+        # 3) CUDA graph of two launches (one per slot) plus the copies that read them,
+        #    replayed twice with new inputs written in place
+        exg = PeerExchange(B, shard.n_q, D, torch.bfloat16)
+        q, kp, vp, ql, kpl, vpl = inputs()
+        ql2 = ql.clone()
+        snaps = [torch.empty((B, Hq, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        for s_, qq in zip(snaps, (ql, ql2)):  # eager warm-up (workspace, slots 0 and 1)
+            s_.copy_(as_heads(kernels.paged_decode_attention_gather(
+                qq, kpl, vpl, bt_d, ctx_d, exg, workspace=ws)))
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for s_, qq in zip(snaps, (ql, ql2)):
+                s_.copy_(as_heads(kernels.paged_decode_attention_gather(
+                    qq, kpl, vpl, bt_d, ctx_d, exg, workspace=ws)))
+        for rep in range(2):
+            qa, kpa, vpa, qla, kpla, vpla = inputs()
+            qb = torch.randn((B, Hq, D), generator=g).to(torch.bfloat16).to(dev)
+            ql.copy_(qla)
+            ql2.copy_(qb[:, shard.q_lo:shard.q_hi])
+            kpl.copy_(kpla)
+            vpl.copy_(vpla)
+            graph.replay()
+            check(f"graph replay {rep} slot 0", snaps[0].clone(), qa, kpa, vpa)
+            check(f"graph replay {rep} slot 1", snaps[1].clone(), qb, kpa, vpa)
+        torch.cuda.synchronize()
+        del graph
         with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
             f.write("ok" if ok else msg)
         dist.barrier()
-        ex.close()
+        for e in (ex, exh, exg):
+            e.close()
         dist.destroy_process_group()
     except Exception:
         with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
