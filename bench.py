@@ -21,8 +21,10 @@ and MLP are outside the path and not run.
 
 `--impl reference` times the CPU reference path instead (rank 0 only).
 Multi-GPU (torchrun, N = 2/4/8): KV heads and their pools are split across ranks;
-each rank attends its heads and the per-layer outputs are all-gathered (NCCL) before
-o_proj would run; time is the max over ranks.
+each rank attends its heads and the per-layer outputs are all-gathered before o_proj
+would run, inside the attention kernel (NVLink peer stores; --nccl: an NCCL
+all-gather after it instead); time is the max over ranks, every rank's timed region
+starting together on the device.
 """
 
 from __future__ import annotations
@@ -79,23 +81,29 @@ def c3_contexts(cfg: dict) -> np.ndarray:
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """nvidia-smi clock/throttle sampling during the timed region.
+
+    One sampler process per job (rank 0) covering every GPU of the job: `indices` are
+    the local GPU indices to query (None: sample nothing).
+    """
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int, interval_ms: int = 20) -> None:
-        self.index = index
+    def __init__(self, indices, interval_ms: int = 20) -> None:
+        self.indices = indices
         self.interval_ms = interval_ms
         self.proc = None
         self.out = ""
         self.first = ""
 
     def __enter__(self):
+        if not self.indices:
+            return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", "-i", ",".join(map(str, self.indices)), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             # nvidia-smi needs a moment to start; the first line marks it sampling
@@ -242,11 +250,20 @@ class DecodeWorkload:
             self.layer(l, attention, copy, gather)
 
 
-def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
-    """Device ms for `steps` calls of fn, events on the launching stream."""
+def time_region(fn, steps: int, stream: torch.cuda.Stream, world: int = 1) -> float:
+    """Device ms for `steps` calls of fn, events on the launching stream.
+
+    With several ranks a one-element all-reduce is queued right before the start
+    event, so every rank's timed region starts when the last rank is ready (host-side
+    skew before the region is not counted by the ranks that started early).
+    """
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(torch.zeros(1, device=stream.device))
     start.record(stream)
     for _ in range(steps):
         fn()
@@ -313,39 +330,64 @@ def bench_index_copy(dev: torch.device, peak: float) -> dict:
     return res
 
 
-def cpu_baseline_sample(cfg: dict, layers_sample: int = 1, requests_sample: int = 4) -> dict:
-    """Oracle (numpy port of the reference path) on a bounded sample, scaled to a step."""
-    from oracle import paged_kv_oracle as orc
+class CpuSample:
+    """The C3 KV path of `requests` requests on the CPU (the oracle, a numpy port of the
+    reference's _write_kv_layer + paged_attention_v1), built once and run per layer.
 
-    rng = np.random.default_rng(99)
-    ctx = c3_contexts(cfg)
-    S, D, Hq, Hkv = cfg["page_size"], cfg["head_dim"], cfg["hq"], cfg["hkv"]
-    idx = np.arange(requests_sample)
-    sub = ctx[idx]
-    npg = (sub + S - 1) // S
-    P = int(npg.sum())
-    kp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
-    vp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
-    perm = rng.permutation(P)
-    tables, cur = [], 0
-    for n in npg:
-        tables.append([int(x) for x in perm[cur:cur + n]])
-        cur += n
-    q = rng.standard_normal((len(sub), Hq, D), dtype=np.float32)
-    kn = rng.standard_normal((len(sub), Hkv, D), dtype=np.float32)
-    slots = np.array([orc.slot_of(t, int(c) - 1, S) for t, c in zip(tables, sub)])
-    t0 = time.perf_counter()
-    for _ in range(layers_sample):
-        orc.write_kv_slots(kp, vp, kn, kn, slots, S)
-        orc.paged_attention_decode(q, kp, vp, tables, sub, S)
-    dt = time.perf_counter() - t0
-    scale = (ctx.sum() / sub.sum()) * (cfg["layers"] / layers_sample)
-    step_s = dt * scale
-    return dict(value=round(cfg["batch"] / step_s, 3), unit="tok/s",
-                cores=_blas_threads(), kind="port",
-                sample=f"{layers_sample} layer x {requests_sample} of {cfg['batch']} requests "
-                       f"({int(sub.sum())} of {int(ctx.sum())} context tokens), fp32 numpy oracle, "
-                       f"scaled x{scale:.1f} to one {cfg['layers']}-layer step; {dt:.2f} s measured")
+    Pools are fp32 in the reference's logical layout [pages, Hkv, D, S]; every layer
+    run reuses the same pools (the work per layer is the same for every layer).
+    """
+
+    def __init__(self, cfg: dict, requests: int | None = None) -> None:
+        from oracle import paged_kv_oracle as orc
+
+        self.orc = orc
+        self.cfg = cfg
+        rng = np.random.default_rng(99)
+        self.ctx = c3_contexts(cfg)
+        S, D, Hq, Hkv = cfg["page_size"], cfg["head_dim"], cfg["hq"], cfg["hkv"]
+        self.sub = self.ctx[: (requests or cfg["batch"])]
+        npg = (self.sub + S - 1) // S
+        P = int(npg.sum())
+        self.kp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+        self.vp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+        perm = rng.permutation(P)
+        self.tables, cur = [], 0
+        for n in npg:
+            self.tables.append([int(x) for x in perm[cur:cur + n]])
+            cur += n
+        self.q = rng.standard_normal((len(self.sub), Hq, D), dtype=np.float32)
+        self.kn = rng.standard_normal((len(self.sub), Hkv, D), dtype=np.float32)
+        self.slots = np.array([orc.slot_of(t, int(c) - 1, S) for t, c in zip(self.tables, self.sub)])
+
+    def layer(self) -> None:
+        self.orc.write_kv_slots(self.kp, self.vp, self.kn, self.kn, self.slots, self.cfg["page_size"])
+        self.orc.paged_attention_decode(self.q, self.kp, self.vp, self.tables, self.sub,
+                                        self.cfg["page_size"])
+
+    def measure(self, target_s: float) -> dict:
+        """Run layers until `target_s` seconds of CPU work (at least one); tok/s of a step."""
+        cfg = self.cfg
+        layers, t0 = 0, time.perf_counter()
+        while True:
+            self.layer()
+            layers += 1
+            dt = time.perf_counter() - t0
+            if dt >= target_s or layers >= cfg["layers"]:
+                break
+        scale = (self.ctx.sum() / self.sub.sum()) * (cfg["layers"] / layers)
+        step_s = dt * scale
+        return dict(value=round(cfg["batch"] / step_s, 3), unit="tok/s",
+                    cores=_blas_threads(), kind="port",
+                    sample=f"{layers} layer(s) x {len(self.sub)} of {cfg['batch']} requests "
+                           f"({int(self.sub.sum())} of {int(self.ctx.sum())} context tokens per "
+                           f"layer), fp32 numpy oracle, scaled x{scale:.2f} to one "
+                           f"{cfg['layers']}-layer step; {dt:.1f} s measured")
+
+
+def cpu_baseline_sample(cfg: dict, target_s: float = 12.0) -> dict:
+    """Oracle on a bounded sample (all requests, ~target_s of CPU work), scaled to a step."""
+    return CpuSample(cfg).measure(target_s)
 
 
 def _blas_threads() -> int:
@@ -364,10 +406,12 @@ def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     cfg = dict(C3)
+    # one step = one layer of every request of the workload, scaled to the 36-layer step
+    sample = CpuSample(cfg)
     for _ in range(args.warmup):
-        cpu_baseline_sample(cfg, 1, 2)
-    vals = [cpu_baseline_sample(cfg, 1, 4) for _ in range(args.steps)]
-    v = statistics.median(x["value"] for x in vals)
+        sample.measure(0.0)
+    vals = [sample.measure(0.0) for _ in range(args.steps)]
+    v = round(statistics.median(x["value"] for x in vals), 4)
     cb = dict(vals[0])
     cb["value"] = v
     line = dict(metric=METRIC, value=v, unit="tok/s", impl="reference", n_gpus=world,
@@ -547,7 +591,7 @@ def run_c5(args, rank: int, world: int, dev: torch.device) -> None:
         wl.step()
     torch.cuda.synchronize()
     wl.h2d_bytes = wl.d2h_bytes = 0
-    with ClockSampler(dev.index or 0) as clk:
+    with ClockSampler([dev.index or 0]) as clk:
         ms = time_region(wl.step, args.steps, stream)
     ms_step = ms / args.steps
     h2d = wl.h2d_bytes / args.steps
@@ -621,8 +665,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             step_fn()
 
     barrier(world)
-    with ClockSampler(local_rank) as clk:
-        ms = time_region(step_fn, args.steps, stream)
+    with ClockSampler(list(range(world)) if rank == 0 else None) as clk:
+        ms = time_region(step_fn, args.steps, stream, world)
     barrier(world)
     ms = max_over_ranks(ms, world)
     ms_step = ms / args.steps
@@ -635,8 +679,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         ga, gc = graph_of(attn_fn), graph_of(copy_fn)
         attn_fn, copy_fn = ga.replay, gc.replay
     reps = max(2, args.steps)
-    attn_ms = time_region(attn_fn, reps, stream) / (reps * cfg["layers"])
-    copy_ms = time_region(copy_fn, reps, stream) / (reps * cfg["layers"])
+    attn_ms = time_region(attn_fn, reps, stream, world) / (reps * cfg["layers"])
+    copy_ms = time_region(copy_fn, reps, stream, world) / (reps * cfg["layers"])
     attn_ms = max_over_ranks(attn_ms, world)
     achieved = wl.attn_bytes() / (attn_ms * 1e-3) / 1e9
 
@@ -781,7 +825,7 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
     for _ in range(args.warmup):
         step()
     barrier(wl.world)
-    ms = max_over_ranks(time_region(step, args.steps, stream), wl.world)
+    ms = max_over_ranks(time_region(step, args.steps, stream, wl.world), wl.world)
     # whole job: every rank copies its shard in; rank 0 reads the result out
     h2d = wl.world * sum(t.numel() * t.element_size()
                          for t in (q_h, kn_h, vn_h, wl.slots_host, wl.ctx_host))
