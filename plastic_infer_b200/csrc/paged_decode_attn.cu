@@ -158,11 +158,15 @@ __device__ __noinline__ void merge_pieces(const RowDsts<T> dst, const float* ws_
   if (g >= G) return;
   auto slot_of = [&](int j) { return static_cast<int64_t>(wa + j) * 2 + (j == 0 ? role_a : 0); };
   float M = -INFINITY;
+#pragma unroll 8
   for (int j = 0; j < npieces; ++j) M = fmaxf(M, __ldcg(ws_ml + slot_of(j) * kHeadsPad * 2 + g * 2));
   float L = 0.f;
   float4 acc[D / 16];  // n4 <= D / 16 (G = 8)
 #pragma unroll
   for (int e = 0; e < D / 16; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Four pieces' loads in flight at once at D <= 128 (at D = 256 it would spill the page loop).
+  constexpr int kPieceUnroll = D <= 128 ? 4 : 1;
+#pragma unroll kPieceUnroll
   for (int j = 0; j < npieces; ++j) {
     const int64_t sl = slot_of(j);
     const float2 ml = __ldcg(reinterpret_cast<const float2*>(ws_ml + sl * kHeadsPad * 2 + g * 2));
