@@ -462,6 +462,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   using Mma = MmaOp<T>;
   uint32_t qf[C::kMT][2];
+  // The next segment's query fragment, loaded one segment ahead (D <= 128: at D = 256
+  // the extra registers would spill the page loop, and the rows go to L2 instead).
+  constexpr bool kQAhead = D <= 128;
+  uint32_t qn[kQAhead ? C::kMT : 1][2];
+  bool qn_valid = false;
+  // Query rows of (request b, KV head h) as the MMA B fragment (heads >= G are zero).
+  auto load_q = [&](int b, int h, uint32_t (*dst)[2]) {
+    const T* qb = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.q_stride +
+                  static_cast<int64_t>(h) * G * D;
+#pragma unroll
+    for (int kk = 0; kk < C::kMT; ++kk) {
+      if (gid < G) {
+        const uint32_t* qr = reinterpret_cast<const uint32_t*>(qb + gid * D + 16 * kk + 2 * tig);
+        dst[kk][0] = __ldg(qr);
+        dst[kk][1] = __ldg(qr + 4);
+      } else {
+        dst[kk][0] = 0u;
+        dst[kk][1] = 0u;
+      }
+    }
+  };
   float o[C::kMT][4];
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
@@ -557,18 +578,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   while (pos < hi) {
     if (fresh) {
       // New (b, h) piece: load this KV head's G query rows as the MMA B operand.
-      const T* qb = static_cast<const T*>(p.q) + static_cast<int64_t>(cb) * p.q_stride +
-                    static_cast<int64_t>(ch) * G * D;
+      // The fragment was loaded one segment ahead (except for the warp's first).
+      if (kQAhead && qn_valid) {
 #pragma unroll
-      for (int kk = 0; kk < C::kMT; ++kk) {
-        if (gid < G) {
-          const uint32_t* qr = reinterpret_cast<const uint32_t*>(qb + gid * D + 16 * kk + 2 * tig);
-          qf[kk][0] = __ldg(qr);
-          qf[kk][1] = __ldg(qr + 4);
-        } else {
-          qf[kk][0] = 0u;
-          qf[kk][1] = 0u;
+        for (int kk = 0; kk < (kQAhead ? C::kMT : 1); ++kk) {
+          qf[kk][0] = qn[kk][0];
+          qf[kk][1] = qn[kk][1];
         }
+      } else {
+        load_q(cb, ch, qf);
       }
 #pragma unroll
       for (int mt = 0; mt < C::kMT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
@@ -577,18 +595,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       piece_start = pos;
       fresh = false;
       {
-        // Pull the next segment's query rows into L2 now, so its start does not wait
-        // a full DRAM round trip (segments follow (request, head) order).
+        // Load the next segment's query rows now, so its start does not stall on them
+        // (segments follow (request, head) order, skipping empty requests, as below).
         const int64_t seg_end = static_cast<int64_t>(s_poff[cb]) * Hkv +
                                 static_cast<int64_t>(ch + 1) * cn;
-        if (seg_end < hi) {
-          const int nh = ch + 1 < Hkv ? ch + 1 : 0;
-          const int nb = ch + 1 < Hkv ? cb : cb + 1;
-          const char* nq = reinterpret_cast<const char*>(
-              static_cast<const T*>(p.q) + static_cast<int64_t>(nb) * p.q_stride +
-              static_cast<int64_t>(nh) * G * D);
-          if (lane * 128 < G * D * static_cast<int>(sizeof(T)))
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(nq + lane * 128));
+        qn_valid = seg_end < hi;
+        if (qn_valid) {
+          int nh = ch + 1, nb = cb;
+          if (nh == Hkv) {
+            nh = 0;
+            do { ++nb; } while (nb < B && s_poff[nb + 1] == s_poff[nb]);
+          }
+          if constexpr (kQAhead) {
+            load_q(nb, nh, qn);
+          } else {
+            const char* nq = reinterpret_cast<const char*>(
+                static_cast<const T*>(p.q) + static_cast<int64_t>(nb) * p.q_stride +
+                static_cast<int64_t>(nh) * G * D);
+            if (lane * 128 < G * D * static_cast<int>(sizeof(T)))
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(nq + lane * 128));
+          }
         }
       }
       if constexpr (kAppend) {
