@@ -150,10 +150,14 @@ class DecodeWorkload:
 
         self.kernels = kernels
         self.cfg = cfg
+        from plastic_infer_b200.dist import head_shard
+
         L, B, S, D = cfg["layers"], cfg["batch"], cfg["page_size"], cfg["head_dim"]
-        assert cfg["hkv"] % world == 0 and cfg["hq"] % world == 0
-        self.hkv = cfg["hkv"] // world
-        self.hq = cfg["hq"] // world
+        # This rank's KV heads and query heads; with fewer KV heads than ranks (C4 on 8
+        # GPUs) each KV head is replicated and its replicas split its query heads.
+        self.shard = head_shard(cfg["hq"], cfg["hkv"], world, rank)
+        self.hkv = self.shard.n_kv
+        self.hq = self.shard.n_q
         self.dev = dev
         self.ctx = c3_contexts(cfg)
         npg = (self.ctx + S - 1) // S
@@ -631,6 +635,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     cfg = dict(WORKLOADS[args.workload])
     if args.layers:
         cfg["layers"] = args.layers
+    # Programmatic dependent launch: each attention computes its work split and fetches
+    # its first page ids while the step's index-copy runs, then waits for it; every
+    # kernel still reads its inputs only after the kernel before it has completed.
+    from plastic_infer_b200 import kernels
+
+    kernels.set_programmatic_launch(not args.no_pdl)
     wl = DecodeWorkload(cfg, rank, world, dev)
     wl.fused = args.fused
     if world > 1 and not args.nccl:
@@ -712,7 +722,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                         kv_bytes_per_step=round(wl.attn_bytes() * cfg["layers"] * world / 1e9, 3),
                         l2=f"inputs larger than L2 "
                            f"(~{wl.attn_bytes() * cfg['layers'] / 1e9:.0f} GB KV per step), no flush",
-                        cuda_graph=use_graph),
+                        cuda_graph=use_graph, programmatic_launch=not args.no_pdl),
             roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm_gbs"],
                           unit="GB/s", frac=round(achieved / peaks["hbm_gbs"], 4),
                           traffic=traffic, kernel="paged_decode_attn_tma_kernel<bf16,128,16>",
@@ -868,6 +878,9 @@ def main() -> None:
     ap.add_argument("--nccl", action="store_true",
                     help="N > 1: gather the per-layer outputs with NCCL all-gather instead of the "
                          "kernel's NVLink peer stores")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch kernels without programmatic dependent launch (each attention "
+                         "then computes its work split only after the previous kernel ends)")
     ap.add_argument("--fused", action="store_true",
                     help="one fused append+attention launch per layer instead of index-copy "
                          "then attention (measured slower today: 202.9 vs 197.5 us per layer)")

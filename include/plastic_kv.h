@@ -63,6 +63,21 @@ extern "C" {
 /* Version of this ABI (bumped on any signature change). */
 int pi_abi_version(void);
 
+/*
+ * Programmatic dependent launch (no reference counterpart; off by default). When on,
+ * the index-copy and the TMA attention kernels are launched with CUDA's programmatic
+ * stream-serialization attribute. Each lets the next kernel on its stream launch as
+ * soon as it has started. The index-copy waits for the previous kernel before reading
+ * anything. The attention kernel reads only `ctx_lens` and `block_tables` before
+ * waiting: it computes its work split and fetches its first page ids while the
+ * previous kernel (e.g. the step's index-copy) finishes.
+ *
+ * So with it on, `ctx_lens` and `block_tables` must not be written by the kernel
+ * launched immediately before the attention on the same stream (host copies are
+ * fine). Applies to launches made after the call, in every thread. Returns PI_OK.
+ */
+int pi_set_programmatic_launch(int enable);
+
 /* Static description of a status code. Never NULL. */
 const char* pi_error_string(int code);
 

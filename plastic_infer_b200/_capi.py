@@ -44,6 +44,7 @@ _f32 = ctypes.c_float
 
 # name -> (restype, argtypes); the one table of what the header declares.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "pi_set_programmatic_launch": (_i32, [_i32]),
     "pi_abi_version": (_i32, []),
     "pi_error_string": (ctypes.c_char_p, [_i32]),
     "pi_kv_index_copy": (

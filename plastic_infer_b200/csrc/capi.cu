@@ -1,4 +1,5 @@
 // Library-wide C entry points: ABI version, status strings, device queries.
+#include <atomic>
 #include <mutex>
 
 #include "pi_common.cuh"
@@ -18,9 +19,20 @@ int device_sm_count() {
   return cache[dev];
 }
 
+namespace {
+std::atomic<int> g_programmatic{0};
+}  // namespace
+
+bool programmatic_launch() { return g_programmatic.load(std::memory_order_relaxed) != 0; }
+
 }  // namespace pi
 
 extern "C" int pi_abi_version(void) { return 2; }
+
+extern "C" int pi_set_programmatic_launch(int enable) {
+  pi::g_programmatic.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return PI_OK;
+}
 
 extern "C" const char* pi_error_string(int code) {
   switch (code) {

@@ -60,6 +60,10 @@ __global__ void __launch_bounds__(256) kv_index_copy_kernel(
     int* err) {
   using V = typename VecT<VEC>::type;
   constexpr int kPerLane = VEC == 16 ? 8 : 16;
+  // Programmatic launch: nothing is read before the previous kernel has completed
+  // (the new rows are its output); the next kernel may launch from here on.
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -166,18 +170,13 @@ int launch_index_copy(void* k_pool, void* v_pool, const void* k_new, const void*
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   const bool fixed = (32 % (row_bytes / VEC)) == 0;
-  if (fixed) {
-    kv_index_copy_kernel<VEC, true><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-        static_cast<char*>(k_pool), static_cast<char*>(v_pool), static_cast<const char*>(k_new),
-        static_cast<const char*>(v_new), slot_mapping, n_tokens, kv_heads, row_bytes, page_size,
-        num_slots, src_stride_bytes, err);
-  } else {
-    kv_index_copy_kernel<VEC, false><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-        static_cast<char*>(k_pool), static_cast<char*>(v_pool), static_cast<const char*>(k_new),
-        static_cast<const char*>(v_new), slot_mapping, n_tokens, kv_heads, row_bytes, page_size,
-        num_slots, src_stride_bytes, err);
-  }
-  return cuda_status(cudaGetLastError());
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const cudaError_t e = launch_kernel(
+      fixed ? kv_index_copy_kernel<VEC, true> : kv_index_copy_kernel<VEC, false>, grid,
+      dim3(kThreads), 0, stream, static_cast<char*>(k_pool), static_cast<char*>(v_pool),
+      static_cast<const char*>(k_new), static_cast<const char*>(v_new), slot_mapping, n_tokens,
+      kv_heads, row_bytes, page_size, num_slots, src_stride_bytes, err);
+  return cuda_status(e);
 }
 
 }  // namespace

@@ -229,13 +229,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int Hkv = p.hkv;
   const int G = p.group;
 
+  // Programmatic launch: the next kernel on the stream may launch from here on (it
+  // waits for this one before it reads what this one writes).
+  pdl_trigger();
+
   // Epoch of this gather launch: from the arguments, or one past this rank's launch
   // counter (written only by the previous launch's last warp, so every thread of this
-  // launch reads the same value).
+  // launch reads the same value). Read after the programmatic wait below.
   unsigned ag_epoch = 0;
-  if constexpr (kGather) {
-    ag_epoch = p.ag.launch_counter != nullptr ? __ldcg(p.ag.launch_counter) + 1u : p.ag.epoch;
-  }
   // Exit bookkeeping of the gather variant. The last warp of the grid to finish
   // publishes `epoch` to every rank once all warps' peer stores are visible, then
   // waits until every rank has published `epoch` here: when the launch completes, the
@@ -340,14 +341,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t total = static_cast<int64_t>(s_poff[B]) * Hkv;
   const int hq = Hkv * G;
 
-  // Requests with no context produce zeros (SDPA over zero keys).
-  for (int b = gw; b < B; b += NW) {
-    if (s_poff[b + 1] == s_poff[b]) {
-      const RowDsts<T> dst = row_dsts(static_cast<int64_t>(b) * p.out_stride);
-      for (int k = 0; k < dst.n; ++k)
-        for (int i = lane; i < hq * D; i += 32) dst.p[k][i] = from_f32<T>(0.f);
-    }
-  }
 
   // Fused append: store the step's new K/V rows in the pools (one warp per
   // (request, head) row pair). A TMA load of the same page may see the row before or
@@ -382,13 +375,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Partition over at most `total` warps so every active warp owns >= 1 page: a
   // segment's pieces are then exactly the warps [first, last] that overlap it.
   const int NWe = static_cast<int>(total < NW ? total : NW);
-  if (gw >= NWe) {
-    append_rows();
-    finish();
-    return;
-  }
-  const int64_t lo = total * gw / NWe;
-  const int64_t hi = total * (gw + 1) / NWe;
+  const bool active = gw < NWe;
+  const int64_t lo = active ? total * gw / NWe : 0;
+  const int64_t hi = active ? total * (gw + 1) / NWe : 0;
 
   // (b, h, page) of a stream position: largest b with s_poff[b] * Hkv <= pos.
   auto locate = [&](int64_t pos, int& b, int& h, int& pg) {
@@ -422,6 +411,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   int64_t pbase = lo;
   int id_cur = load_ids(lo);
   int id_nxt = load_ids(lo + 32);
+
+  // Everything above reads only ctx_lens and block_tables. Under a programmatic launch
+  // the previous kernel on the stream may still be running up to here; from here on
+  // its results (q, the pools, the launch counter) are complete and visible.
+  pdl_wait();
+  if constexpr (kGather) {
+    ag_epoch = p.ag.launch_counter != nullptr ? __ldcg(p.ag.launch_counter) + 1u : p.ag.epoch;
+  }
+
+  // Requests with no context produce zeros (SDPA over zero keys).
+  for (int b = gw; b < B; b += NW) {
+    if (s_poff[b + 1] == s_poff[b]) {
+      const RowDsts<T> dst = row_dsts(static_cast<int64_t>(b) * p.out_stride);
+      for (int k = 0; k < dst.n; ++k)
+        for (int i = lane; i < hq * D; i += 32) dst.p[k][i] = from_f32<T>(0.f);
+    }
+  }
+  if (!active) {
+    append_rows();
+    finish();
+    return;
+  }
 
   auto issue = [&](int64_t pos, int stage) {
     if (pos - pbase >= 32) {
@@ -1049,8 +1060,7 @@ int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, in
       !pool_tensor_map(&tv, v_pool, static_cast<uint64_t>(rows), D, S, dtype))
     return PI_ERR_CUDA;
   const unsigned grid = static_cast<unsigned>(device_sm_count() * *configured);
-  kern<<<grid, kThreads, smem, stream>>>(tk, tv, fp);
-  return cuda_status(cudaGetLastError());
+  return cuda_status(launch_kernel(kern, dim3(grid), dim3(kThreads), smem, stream, tk, tv, fp));
   }
 }
 

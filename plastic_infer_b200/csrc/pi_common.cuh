@@ -37,6 +37,39 @@ inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? PI_OK : PI_ERR
 int device_sm_count();
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch (pi_set_programmatic_launch). A kernel launched with
+// the programmatic stream-serialization attribute may start while the kernel before
+// it on the stream is still running: pdl_wait() blocks until that kernel has
+// completed and its memory operations are visible (a no-op for an ordinary launch),
+// and pdl_trigger() lets the next kernel on the stream launch early.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Whether launches carry the programmatic attribute (process-wide switch).
+bool programmatic_launch();
+
+// Launch `kern` on `stream`, with the programmatic attribute when it is switched on.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = programmatic_launch() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
+// ---------------------------------------------------------------------------
 // Device-side error word: kernels never trap; they record the first error code
 // in an optional int the caller owns and skip the offending access.
 // ---------------------------------------------------------------------------

@@ -157,6 +157,18 @@ def default_workspace(device: torch.device) -> Workspace:
         return ws
 
 
+def set_programmatic_launch(enable: bool) -> None:
+    """Programmatic dependent launch for every later index-copy and attention launch.
+
+    When on, a kernel may launch while the previous kernel on its stream is still
+    running: the attention computes its work split and fetches its first page ids
+    (reading only ctx_lens and block_tables) before it waits for that kernel. So the
+    kernel launched just before an attention must not write its ctx_lens or
+    block_tables. Off by default.
+    """
+    _capi.call("pi_set_programmatic_launch", 1 if enable else 0)
+
+
 def workspace_bytes(batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int) -> int:
     return int(_capi.load().pi_paged_decode_attn_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim))
 

@@ -9,8 +9,9 @@ query heads with the sm_100a kernel, and the outputs are gathered:
 Both must equal, bit for bit, every shard attended on one GPU by the same kernel and
 concatenated, and agree with the unsharded kernel within the attention tolerance, for
 consecutive launches (slots and epochs rotate), with epochs from the host and from the
-device counter, and for a CUDA graph of launches replayed with new inputs. Skipped
-unless at least two GPUs are visible.
+device counter, for a CUDA graph of launches replayed with new inputs, for a KV head
+replicated on every rank (fewer KV heads than ranks), and with programmatic launch on. Skipped unless at least two
+GPUs are visible.
 """
 
 from __future__ import annotations
@@ -66,27 +67,29 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
         ctx_d = ctx.to(torch.int32).to(dev)
         ws = kernels.Workspace(dev)
 
-        def inputs():
-            q = torch.randn((B, Hq, D), generator=g).to(torch.bfloat16).to(dev)
-            kp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
-            vp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
-            return (q, kp, vp, q[:, shard.q_lo:shard.q_hi].contiguous(),
-                    kp[:, shard.kv_lo:shard.kv_hi].contiguous(),
-                    vp[:, shard.kv_lo:shard.kv_hi].contiguous())
+        def inputs(hq=Hq, hkv=Hkv):
+            sh = head_shard(hq, hkv, world, rank)
+            q = torch.randn((B, hq, D), generator=g).to(torch.bfloat16).to(dev)
+            kp = torch.randn((P, hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
+            vp = torch.randn((P, hkv, S, D), generator=g).to(torch.bfloat16).to(dev)
+            return (q, kp, vp, q[:, sh.q_lo:sh.q_hi].contiguous(),
+                    kp[:, sh.kv_lo:sh.kv_hi].contiguous(),
+                    vp[:, sh.kv_lo:sh.kv_hi].contiguous())
 
         def expected(q, kp, vp):
             # bit-exact reference: every shard attended on this GPU with the same kernel
             # (same work split as on its owner rank), concatenated in rank order
             parts = []
             for r in range(world):
-                sr = head_shard(Hq, Hkv, world, r)
+                sr = head_shard(q.shape[1], kp.shape[1], world, r)
                 parts.append(kernels.paged_decode_attention(
                     q[:, sr.q_lo:sr.q_hi].contiguous(), kp[:, sr.kv_lo:sr.kv_hi].contiguous(),
                     vp[:, sr.kv_lo:sr.kv_hi].contiguous(), bt_d, ctx_d))
             return torch.cat(parts, dim=1)
 
-        def as_heads(gathered):
-            return gathered.view(world, B, shard.n_q, D).permute(1, 0, 2, 3).reshape(B, Hq, D)
+        def as_heads(gathered, hq=Hq):
+            nq = hq // world
+            return gathered.view(world, B, nq, D).permute(1, 0, 2, 3).reshape(B, hq, D)
 
         ok, msg = True, ""
 
@@ -150,10 +153,32 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             check(f"graph replay {rep} slot 1", snaps[1].clone(), qb, kpa, vpa)
         torch.cuda.synchronize()
         del graph
+
+        # 4) fewer KV heads than ranks: the KV head is replicated and its replicas split
+        #    its query heads (C4 on 8 GPUs)
+        hq2, hkv2 = 8, 1
+        sh2 = head_shard(hq2, hkv2, world, rank)
+        exr = PeerExchange(B, sh2.n_q, D, torch.bfloat16)
+        for step in range(2):
+            q, kp, vp, ql, kpl, vpl = inputs(hq2, hkv2)
+            snap = as_heads(kernels.paged_decode_attention_gather(
+                ql, kpl, vpl, bt_d, ctx_d, exr, workspace=ws), hq2).clone()
+            check(f"replicated KV head step {step}", snap, q, kp, vp)
         with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
             f.write("ok" if ok else msg)
         dist.barrier()
-        for e in (ex, exh, exg):
+        # 5) programmatic launch on: back-to-back gather launches may start while the
+        #    previous one runs; each reads its epoch only after the programmatic wait
+        kernels.set_programmatic_launch(True)
+        try:
+            for step in range(3):
+                q, kp, vp, ql, kpl, vpl = inputs()
+                snap = as_heads(kernels.paged_decode_attention_gather(
+                    ql, kpl, vpl, bt_d, ctx_d, ex, workspace=ws)).clone()
+                check(f"programmatic launch step {step}", snap, q, kp, vp)
+        finally:
+            kernels.set_programmatic_launch(False)
+        for e in (ex, exh, exg, exr):
             e.close()
         dist.destroy_process_group()
     except Exception:
