@@ -697,7 +697,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # e2e through the public API with pinned host buffers
     e2e = None
     if not args.skip_e2e:
-        e2e = run_e2e(wl, args, stream)
+        e2e = run_e2e(wl, args, stream, use_graph)
 
     idx = (bench_index_copy(dev, peaks["hbm_gbs"])
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
@@ -754,12 +754,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         barrier(world)
 
 
-def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
+def run_e2e(wl: DecodeWorkload, args, stream, use_graph: bool = False) -> dict:
     """Whole step through the public API, inputs from pinned host memory each step.
 
     Layer l's inputs are copied host->device on one copy stream and its attention
     output device->host on another, so the copies of layer l+1 / l-1 overlap the
-    kernels of layer l; the step ends when the last output is on the host.
+    kernels of layer l; the step ends when the last output is on the host. With
+    `use_graph` the step (copies, kernels and the streams' event edges) is captured once
+    through the same API calls and replayed: every replay copies that step's inputs in
+    and its outputs out.
     """
     from plastic_infer_b200 import kernels
 
@@ -786,7 +789,8 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
     ev_read = [torch.cuda.Event() for _ in range(L)]
 
     def step():
-        h2d.wait_stream(stream)  # device inputs of the previous step are no longer read
+        cur = torch.cuda.current_stream()  # the capture stream while capturing
+        h2d.wait_stream(cur)  # device inputs of the previous step are no longer read
         with torch.cuda.stream(h2d):
             ctx_d.copy_(wl.ctx_host, non_blocking=True)
             for l in range(L):
@@ -796,15 +800,15 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                 slots_d[l].copy_(wl.slots_host[l], non_blocking=True)
                 ev_in[l].record(h2d)
         for l in range(L):
-            stream.wait_event(ev_in[l])
-            if wl.exchange is not None and read_back:
+            cur.wait_event(ev_in[l])
+            if wl.exchange is not None and read_back and l >= 2:
                 # Peers store into this rank's slots without waiting for its reads: a
                 # peer's launch e starts once this rank has finished launch e - 1, so
-                # the read of a slot's previous output (launch e - L) must be done
-                # before this rank's launch e - 1 starts; waiting here for the read
-                # issued two launches back keeps that for L >= 3 and still lets each
-                # read overlap the next launch.
-                stream.wait_event(ev_read[(l - 2) % L])
+                # the read of a slot's previous output must be done before this rank's
+                # launch e - 1 starts. Waiting here for the read issued two launches back
+                # keeps that within the step and still lets each read overlap the next
+                # launch; across steps the end-of-step wait on the copy stream keeps it.
+                cur.wait_event(ev_read[l - 2])
             if wl.exchange is not None:
                 kernels.kv_index_copy(wl.k_pool, wl.v_pool, kn_d[l], vn_d[l], slots_d[l])
                 kernels.paged_decode_attention_gather(q_d[l], wl.k_pool, wl.v_pool,
@@ -822,7 +826,7 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                 import torch.distributed as dist
 
                 dist.all_gather_into_tensor(wl.gathered[l], wl.out[l])
-            ev_out[l].record(stream)
+            ev_out[l].record(cur)
             if read_back:
                 # a gather launch ends once every rank's slice is here: read it now
                 with torch.cuda.stream(d2h):
@@ -830,19 +834,29 @@ def run_e2e(wl: DecodeWorkload, args, stream) -> dict:
                     out_h[l].copy_(result[l], non_blocking=True)
                     ev_read[l].record(d2h)
         if read_back:
-            stream.wait_stream(d2h)
+            cur.wait_stream(d2h)
 
     for _ in range(args.warmup):
         step()
+    step_fn = step
+    if use_graph:
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        step_fn = graph.replay
+        for _ in range(args.warmup):
+            step_fn()
     barrier(wl.world)
-    ms = max_over_ranks(time_region(step, args.steps, stream, wl.world), wl.world)
+    ms = max_over_ranks(time_region(step_fn, args.steps, stream, wl.world), wl.world)
     # whole job: every rank copies its shard in; rank 0 reads the result out
     h2d = wl.world * sum(t.numel() * t.element_size()
                          for t in (q_h, kn_h, vn_h, wl.slots_host, wl.ctx_host))
     d2h = out_h.numel() * out_h.element_size()
     return dict(value=round(wl.cfg["batch"] * args.steps / (ms * 1e-3), 1), unit="tok/s",
                 h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
-                ms_per_step=round(ms / args.steps, 4), api="plastic_infer_b200.kernels")
+                ms_per_step=round(ms / args.steps, 4), api="plastic_infer_b200.kernels",
+                cuda_graph=use_graph)
 
 
 def _profile_traffic():
