@@ -334,6 +334,67 @@ def bench_index_copy(dev: torch.device, peak: float) -> dict:
     return res
 
 
+def bench_prologue(dev: torch.device, peak: float) -> dict:
+    """Fused decode prologue (QK-norm + RoPE + K/V slot write) per layer vs the unfused ops.
+
+    The unfused sequence is what the reference's runners launch for the same work on the
+    GPU (qk_norm, rope_positions on q and k over a model-dtype table, then the slot write,
+    here our index-copy). Per-launch times from CUDA-graph replays of back-to-back steps.
+    """
+    from plastic_infer_b200 import kernels
+    from plastic_infer_b200.exec.attention import build_rope_cache, qk_norm, rope_positions
+
+    D, S, P = 128, 16, 4096
+    shapes = {"c3": dict(B=64, Hq=32, Hkv=8, qk=False), "c4": dict(B=128, Hq=32, Hkv=4, qk=True)}
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(21)
+    for name, sh in shapes.items():
+        B, Hq, Hkv, qk = sh["B"], sh["Hq"], sh["Hkv"], sh["qk"]
+        q = torch.randn((B, Hq, D), dtype=torch.bfloat16, device=dev, generator=g)
+        k = torch.randn((B, Hkv, D), dtype=torch.bfloat16, device=dev, generator=g)
+        v = torch.randn((B, Hkv, D), dtype=torch.bfloat16, device=dev, generator=g)
+        pos = torch.randint(0, 8192, (B,), device=dev, generator=g)
+        slots = torch.randperm(P * S, device=dev, generator=g)[:B]
+        kp = torch.zeros((P, Hkv, S, D), dtype=torch.bfloat16, device=dev)
+        vp = torch.zeros_like(kp)
+        qw = kw = None
+        if qk:
+            qw = 1 + 0.1 * torch.randn(D, device=dev, generator=g).to(torch.bfloat16)
+            kw = 1 + 0.1 * torch.randn(D, device=dev, generator=g).to(torch.bfloat16)
+        inv = kernels.rope_inv_freq(D, 1e6, dev)
+        q_out = torch.empty_like(q)
+        q_out2 = torch.empty_like(q)
+        cos, sin = build_rope_cache(8192, D, base=1e6, device=dev, dtype=torch.bfloat16)
+
+        def fused():
+            kernels.decode_prologue(q, k, v, pos, inv, slots, kp, vp, qw, kw, q_out=q_out)
+
+        def unfused():
+            q4, k4 = q[None], k[None]  # one position per request: [1, B, heads, D]
+            if qk:
+                q4, k4 = qk_norm(q4, k4, qw, kw, D)
+            kr = rope_positions(cos, sin, pos, k4)
+            q_out2.copy_(rope_positions(cos, sin, pos, q4)[0])
+            kernels.kv_index_copy(kp, vp, kr[0], v, slots)
+
+        times = {}
+        for label, fn in (("fused", fused), ("unfused", unfused)):
+            graph = graph_of(fn)
+            graph.replay()
+            reps = 200
+            times[label] = time_region(graph.replay, reps, torch.cuda.current_stream()) / reps * 1e3
+            del graph
+        byts = 2.0 * B * (Hq + 2 * Hkv) * D * 2 + 16.0 * B + 2.0 * D
+        res[name] = dict(B=B, hq=Hq, hkv=Hkv, qk_norm=qk,
+                         us_per_launch=round(times["fused"], 2),
+                         unfused_us=round(times["unfused"], 2),
+                         speedup=round(times["unfused"] / times["fused"], 2),
+                         bytes_per_launch=int(byts),
+                         gbs=round(byts / (times["fused"] * 1e-6) / 1e9, 1),
+                         frac_of_hbm=round(byts / (times["fused"] * 1e-6) / 1e9 / peak, 4))
+    return res
+
+
 class CpuSample:
     """The C3 KV path of `requests` requests on the CPU (the oracle, a numpy port of the
     reference's _write_kv_layer + paged_attention_v1), built once and run per layer.
@@ -701,6 +762,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     idx = (bench_index_copy(dev, peaks["hbm_gbs"])
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
+    pro = (bench_prologue(dev, peaks["hbm_gbs"])
+           if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
     cpu = cpu_baseline_sample(cfg) if (rank == 0 and world == 1 and not args.skip_cpu) else None
 
     # measured DRAM bytes per launch exist for the C3 single-GPU launch only
@@ -740,6 +803,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             line["index_copy"] = dict(workload="C2: 65536-page bf16 pool x 16 x 8 x 128, "
                                       "random distinct slots", bytes_per_row=8200,
                                       per_batch=idx, peak=peaks["hbm_gbs"])
+        if pro is not None:
+            line["decode_prologue"] = dict(
+                workload="fused QK-norm + RoPE + K/V slot write of one decode layer (bf16, D=128, "
+                         "theta 1e6, positions < 8192) vs the reference's unfused GPU ops",
+                per_shape=pro, peak=peaks["hbm_gbs"])
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

@@ -253,6 +253,34 @@ int pi_paged_decode_attn_noalloc(void* out, const void* q, const void* k_pool,
                                  int64_t out_stride, int* err, cudaStream_t stream);
 
 /*
+ * Fused decode prologue of one layer (no single reference counterpart; it replaces the
+ * op sequence qk_norm -> rope_positions on q and k -> _write_kv_layer of the reference
+ * runners: src/plastic_infer/exec/attention.py:23-95 and
+ * src/plastic_infer/exec/runner_paged.py:112-129, runner_moe_paged.py:135-142). For each
+ * request b (one new token at position positions[b]):
+ *   q_out[b, h]   = rope(qknorm(q_in[b, h], q_norm_w), positions[b])      h < Hq
+ *   K slot[b], h  = rope(qknorm(k_in[b, h], k_norm_w), positions[b])      h < Hkv
+ *   V slot[b], h  = v_in[b, h]
+ * qknorm(x, w) = x / sqrt(mean(x^2) + eps) * w over head_dim (skipped when both weights
+ * are NULL); rope is rotate_half with angle positions[b] * inv_freq[j mod D/2] in fp32
+ * (inv_freq [head_dim/2] fp32 on the device, e.g. 1 / base^(2j/D) as build_rope_cache
+ * computes it). fp32 arithmetic, one rounding to the pool dtype. slot_mapping[b] < 0
+ * writes no K/V row for b; the pools are the physical [P, Hkv, S, D] layout.
+ *   q_in, k_in, v_in   projection outputs in `in_dtype`; request strides q_in_stride
+ *                      and kv_in_stride elements (heads contiguous): separate q/k/v
+ *                      tensors or the three slices of one fused QKV output
+ *   q_out              pool dtype, request stride q_out_stride elements
+ * head_dim 64, 128 or 256.
+ */
+int pi_decode_prologue(void* q_out, int64_t q_out_stride, void* k_pool, void* v_pool,
+                       const void* q_in, int64_t q_in_stride, const void* k_in, const void* v_in,
+                       int64_t kv_in_stride, int in_dtype, const void* q_norm_w,
+                       const void* k_norm_w, float eps, const float* inv_freq,
+                       const int64_t* positions, const int64_t* slot_mapping, int batch,
+                       int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                       int64_t num_slots, int pool_dtype, int* err, cudaStream_t stream);
+
+/*
  * Contiguous gather of a request's pages in the reference's gather layout:
  *   out[t, h, :] = pool[block_table[t / page_size], h, t % page_size, :]
  * for t in [0, num_tokens). out is [num_tokens, kv_heads, head_dim].

@@ -143,6 +143,56 @@ def paged_attention_decode(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarr
 
 
 # ---------------------------------------------------------------------------
+# Decode prologue: QK-norm + RoPE of the step's q / k rows (then the slot write above)
+# ---------------------------------------------------------------------------
+
+
+def rms_norm_rows(x: np.ndarray, weight: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """x / sqrt(mean(x^2) + eps) * weight over the last axis, in float32.
+
+    src/plastic_infer/exec/attention.py:77-80 (rms_norm), applied per head as qk_norm does
+    (attention.py:83-95: the norm acts over head_dim, before RoPE).
+    """
+    x = np.asarray(x, dtype=np.float32)
+    rms = np.sqrt(np.mean(x * x, axis=-1, keepdims=True, dtype=np.float32) + np.float32(eps))
+    return (x / rms * np.asarray(weight, dtype=np.float32)).astype(np.float32)
+
+
+def rope_rows(x: np.ndarray, positions: np.ndarray, inv_freq: np.ndarray) -> np.ndarray:
+    """Rotary embedding of x [B, H, D] at per-request positions [B], in float32.
+
+    src/plastic_infer/exec/attention.py:23-49 (rope_positions: x * cos + rotate_half(x) *
+    sin, rotate_half = cat(-x2, x1)) over the table of attention.py:52-74
+    (cos/sin of cat(freqs, freqs), freqs = outer(t, inv_freq)): the angle of (pos, j) is
+    the float32 product pos * inv_freq[j mod D/2].
+    """
+    x = np.asarray(x, dtype=np.float32)
+    half = x.shape[-1] // 2
+    ang = (np.asarray(positions, dtype=np.float32)[:, None] * np.asarray(inv_freq, np.float32)[None, :])
+    ang = np.concatenate([ang, ang], axis=-1).astype(np.float32)
+    cos = np.cos(ang.astype(np.float64)).astype(np.float32)[:, None, :]
+    sin = np.sin(ang.astype(np.float64)).astype(np.float32)[:, None, :]
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    return (x * cos + rot * sin).astype(np.float32)
+
+
+def decode_prologue(q: np.ndarray, k: np.ndarray, v: np.ndarray, positions: np.ndarray,
+                    inv_freq: np.ndarray, q_norm_w: np.ndarray | None = None,
+                    k_norm_w: np.ndarray | None = None, eps: float = 1e-5):
+    """(q_rot, k_rot, v) of one decode step: optional QK-norm, then RoPE on q and k.
+
+    The order of the reference's MoE runner (src/plastic_infer/exec/runner_moe_paged.py:135-142:
+    qk_norm, then rope_positions); the dense runner has no QK-norm
+    (src/plastic_infer/exec/runner_paged.py:247-248). The K/V rows then go to their slots
+    as write_kv_slots does.
+    """
+    if q_norm_w is not None:
+        q = rms_norm_rows(q, q_norm_w, eps)
+        k = rms_norm_rows(k, k_norm_w, eps)
+    return rope_rows(q, positions, inv_freq), rope_rows(k, positions, inv_freq), v
+
+
+# ---------------------------------------------------------------------------
 # a3: page moves between the pool and host chunks
 # ---------------------------------------------------------------------------
 

@@ -119,6 +119,94 @@ def kv_index_copy(
 
 
 # ---------------------------------------------------------------------------
+# f1: fused decode prologue (QK-norm + RoPE + slot-mapping write)
+# ---------------------------------------------------------------------------
+
+
+def rope_inv_freq(head_dim: int, base: float, device: torch.device | str = "cpu") -> torch.Tensor:
+    """fp32 [head_dim / 2] rotary frequencies 1 / base^(2j / head_dim).
+
+    Computed on the CPU with the expression of build_rope_cache's fp32 table
+    (src/plastic_infer/exec/attention.py:68), so pos * inv_freq[j] is exactly the angle
+    that table holds at (pos, j); then moved to `device`.
+    """
+    inv = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    return inv.to(device)
+
+
+def decode_prologue(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    positions: torch.Tensor,
+    inv_freq: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    q_norm_weight: torch.Tensor | None = None,
+    k_norm_weight: torch.Tensor | None = None,
+    eps: float = 1e-5,
+    q_out: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One launch per layer: QK-norm (optional) + RoPE of the step's q and k rows, and the
+    write of the new K/V rows at their slots (the kv_index_copy semantics).
+
+    q [B, Hq, D], k / v [B, Hkv, D]: the projection outputs (heads contiguous; any request
+    stride, k and v sharing one, e.g. slices of a fused QKV output). positions int64
+    [B]: each request's new-token position. inv_freq fp32 [D/2] (rope_inv_freq).
+    slot_mapping int64 [B] (< 0: no K/V row). Returns q_out [B, Hq, D] in the pool dtype.
+    Replaces qk_norm + rope_positions + _write_kv_layer of the reference runners
+    (src/plastic_infer/exec/attention.py:23-95, src/plastic_infer/exec/runner_paged.py:112-129).
+    """
+    P, Hkv, S, D = _check_pool(k_pool, "k_pool")
+    if v_pool.shape != k_pool.shape or v_pool.dtype != k_pool.dtype:
+        raise ValueError("k_pool and v_pool must have the same shape and dtype")
+    B, Hq = q.shape[0], q.shape[1]
+    if q.dim() != 3 or q.shape[2] != D or tuple(k.shape) != (B, Hkv, D) or k.shape != v.shape:
+        raise ValueError(f"q must be [B, Hq, {D}] and k, v [B, {Hkv}, {D}]")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError("q, k and v must share one dtype")
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        if t.stride(2) != 1 or t.stride(1) != D:
+            raise ValueError(f"{name}: heads must be contiguous rows of head_dim elements")
+    if k.stride(0) != v.stride(0):
+        raise ValueError("k and v must share one request stride")
+    if positions.dtype != torch.int64 or positions.shape != (B,):
+        raise ValueError("positions must be int64 [B]")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (B,):
+        raise ValueError("slot_mapping must be int64 [B]")
+    if inv_freq.dtype != torch.float32 or inv_freq.numel() != D // 2:
+        raise ValueError(f"inv_freq must be float32 [{D // 2}]")
+    if (q_norm_weight is None) != (k_norm_weight is None):
+        raise ValueError("give both QK-norm weights or neither")
+    _require_cuda(q, k, v, positions, inv_freq, slot_mapping, k_pool, v_pool)
+    if q_out is None:
+        q_out = torch.empty((B, Hq, D), dtype=k_pool.dtype, device=q.device)
+    elif q_out.dtype != k_pool.dtype or tuple(q_out.shape) != (B, Hq, D) or q_out.stride(2) != 1 \
+            or q_out.stride(1) != D:
+        raise ValueError("q_out must be [B, Hq, D] in the pool dtype with contiguous heads")
+    qw = kw = None
+    if q_norm_weight is not None:
+        qw = q_norm_weight.to(q.dtype).contiguous()
+        kw = k_norm_weight.to(q.dtype).contiguous()
+        if qw.numel() != D or kw.numel() != D:
+            raise ValueError(f"QK-norm weights must have {D} elements")
+    positions = positions.contiguous()
+    slot_mapping = slot_mapping.contiguous()
+    inv_freq = inv_freq.contiguous()
+    _capi.call(
+        "pi_decode_prologue",
+        q_out.data_ptr(), q_out.stride(0), k_pool.data_ptr(), v_pool.data_ptr(),
+        q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0), dtype_code(q.dtype),
+        qw.data_ptr() if qw is not None else None, kw.data_ptr() if kw is not None else None,
+        float(eps), inv_freq.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),
+        B, Hq, Hkv, D, S, P * S, dtype_code(k_pool.dtype), _err_ptr(err), _stream(),
+    )
+    return q_out
+
+
+# ---------------------------------------------------------------------------
 # a2: paged decode attention
 # ---------------------------------------------------------------------------
 

@@ -36,6 +36,38 @@ ATTENTION_CASES = [
 ]
 
 
+# Decode-prologue cases (QK-norm + RoPE of one new token per request): positions span
+# the first token to 32k, where angles reach ~3e4 rad.
+PROLOGUE_CASES = [
+    # Qwen3-8B head shape, dense runner (no QK-norm), theta 1e6
+    dict(name="pro_8b", seed=201, B=6, Hq=32, Hkv=8, D=128, base=1e6, qk_norm=False,
+         positions=[0, 1, 511, 4095, 8191, 32767]),
+    # Qwen3-30B-A3B head shape with QK-norm (MoE runner)
+    dict(name="pro_moe_qk", seed=202, B=5, Hq=32, Hkv=4, D=128, base=1e6, qk_norm=True,
+         positions=[3, 100, 2047, 4096, 30000]),
+    # C1 shape (head_dim 64)
+    dict(name="pro_c1", seed=203, B=4, Hq=4, Hkv=2, D=64, base=1e6, qk_norm=False,
+         positions=[7, 22, 47, 63]),
+    # head_dim 256, theta 1e4, QK-norm
+    dict(name="pro_d256_qk", seed=204, B=3, Hq=8, Hkv=2, D=256, base=1e4, qk_norm=True,
+         positions=[0, 777, 16383]),
+]
+
+
+def prologue_inputs(case: dict) -> dict:
+    """q [B,Hq,D], k / v [B,Hkv,D] float32 ~N(0,1); QK-norm weights ~1 + 0.1 N(0,1)."""
+    rng = np.random.default_rng(case["seed"])
+    B, Hq, Hkv, D = (case[k] for k in ("B", "Hq", "Hkv", "D"))
+    out = dict(q=rng.standard_normal((B, Hq, D), dtype=np.float32),
+               k=rng.standard_normal((B, Hkv, D), dtype=np.float32),
+               v=rng.standard_normal((B, Hkv, D), dtype=np.float32),
+               positions=np.asarray(case["positions"], dtype=np.int64))
+    if case["qk_norm"]:
+        out["q_norm_w"] = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+        out["k_norm_w"] = (1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    return out
+
+
 def attention_inputs(case: dict) -> dict:
     """q [B,Hq,D], logical pools [P,Hkv,D,S] (float32 values; bf16-representable for
     bf16 cases, plus their bit patterns) and block tables of distinct random pages."""

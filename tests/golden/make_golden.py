@@ -14,6 +14,8 @@ tests/golden/inputs.py, and writes small fixtures next to this file:
   chunk_keys.json             compute_prefix_hashes outputs
   allocator.json              PageAllocator alloc/free traces
   c1_tiny.npz                 prefill_forward_paged + 32 decode_step_paged greedy steps (C1)
+  prologue.npz                qk_norm + rope_positions (fp32 table of build_rope_cache) outputs
+                              for every PROLOGUE_CASES entry
 
 The fixtures are what the oracle is pinned against (tests/test_oracle_golden.py)
 and what the GPU parity tests compare with; the reference tree itself is never
@@ -39,8 +41,8 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 from tests.golden.inputs import (  # noqa: E402
-    ATTENTION_CASES, C1_DECODE_STEPS, C1_LOGIT_STEPS, C1_MODEL, attention_inputs, c1_prompts,
-    c1_weights, checksum, token_kv,
+    ATTENTION_CASES, C1_DECODE_STEPS, C1_LOGIT_STEPS, C1_MODEL, PROLOGUE_CASES, attention_inputs,
+    c1_prompts, c1_weights, checksum, prologue_inputs, token_kv,
 )
 from oracle.paged_kv_oracle import f32_to_bf16_bits  # noqa: E402
 
@@ -236,9 +238,44 @@ def gen_c1(ref) -> None:
     )
 
 
+def gen_prologue(ref) -> None:
+    """qk_norm + rope_positions of the reference on one new token per request.
+
+    The reference applies rope_positions to [batch, seq, heads, D] with one position per
+    seq index; B requests with one token each are passed as seq = B. The table is
+    build_rope_cache's fp32 one. inv_freq is stored as that function computes it
+    (attention.py:68), and checked to reproduce the table's cos column by column.
+    """
+    build_rope_cache, rope_positions, qk_norm = (ref["build_rope_cache"], ref["rope_positions"],
+                                                 ref["qk_norm"])
+    out = {}
+    for case in PROLOGUE_CASES:
+        x = prologue_inputs(case)
+        D, base = case["D"], case["base"]
+        pos = torch.from_numpy(x["positions"])
+        cos, sin = build_rope_cache(int(pos.max()) + 1, D, base=base, dtype=torch.float32)
+        inv = 1.0 / (base ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+        freqs = torch.outer(torch.arange(int(pos.max()) + 1, dtype=torch.float32), inv)
+        assert torch.equal(cos, torch.cat((freqs, freqs), dim=-1).cos())
+        q = torch.from_numpy(x["q"])[None]
+        k = torch.from_numpy(x["k"])[None]
+        if case["qk_norm"]:
+            q, k = qk_norm(q, k, torch.from_numpy(x["q_norm_w"]), torch.from_numpy(x["k_norm_w"]), D)
+        qr = rope_positions(cos, sin, pos, q)[0]
+        kr = rope_positions(cos, sin, pos, k)[0]
+        n = case["name"]
+        out[f"{n}__q"] = qr.numpy().copy()
+        out[f"{n}__k"] = kr.numpy().copy()
+        out[f"{n}__inv_freq"] = inv.numpy().copy()
+        out[f"{n}__checksum"] = np.float64(checksum(*(x[k_] for k_ in sorted(x))))
+    np.savez_compressed(HERE / "prologue.npz", **out)
+
+
 def load_reference(src: str) -> dict:
     sys.path.insert(0, src)
-    from plastic_infer.exec.attention import paged_attention_v1
+    from plastic_infer.exec.attention import (
+        build_rope_cache, paged_attention_v1, qk_norm, rope_positions,
+    )
     from plastic_infer.exec.runner import DenseWeights, ModelConfig
     from plastic_infer.exec.runner_paged import (
         _write_kv_layer, decode_step_paged, make_kv_config, prefill_forward_paged,
@@ -252,17 +289,24 @@ def load_reference(src: str) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path to the reference's src/ directory")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="generate only these fixtures (index_copy, attention, store, "
+                         "chunk_keys, allocator, c1, prologue)")
     args = ap.parse_args()
     torch.manual_seed(0)
     ref = load_reference(args.ref)
-    gen_index_copy(ref, "bf16")
-    gen_index_copy(ref, "f32")
-    gen_attention(ref)
-    gen_store(ref, "f32")
-    gen_store(ref, "bf16")
-    gen_chunk_keys(ref)
-    gen_allocator(ref)
-    gen_c1(ref)
+    gens = dict(
+        index_copy=lambda: (gen_index_copy(ref, "bf16"), gen_index_copy(ref, "f32")),
+        attention=lambda: gen_attention(ref),
+        store=lambda: (gen_store(ref, "f32"), gen_store(ref, "bf16")),
+        chunk_keys=lambda: gen_chunk_keys(ref),
+        allocator=lambda: gen_allocator(ref),
+        c1=lambda: gen_c1(ref),
+        prologue=lambda: gen_prologue(ref),
+    )
+    for name, gen in gens.items():
+        if args.only is None or name in args.only:
+            gen()
     for p in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
         print(f"{p.name:28s} {p.stat().st_size:9d} B")
 

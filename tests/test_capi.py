@@ -69,6 +69,25 @@ def test_host_validation_rejects_before_launch(lib: ctypes.CDLL) -> None:
     assert lib.pi_page_gather(fake, fake, fake, 1, 2, 24, 1, 4, None,
                               None) == _capi.PI_ERR_MISALIGNED
     assert lib.pi_page_scatter(None, None, None, 0, 2, 4096, 1, 4, None, None) == _capi.PI_OK
+    # fused decode prologue: head_dim 96 unsupported; nothing to do; null pointers
+    pro = lib.pi_decode_prologue
+    assert pro(fake, 1024, fake, fake, fake, 1024, fake, fake, 256, _capi.PI_DTYPE_BF16, None,
+               None, 1e-5, fake, fake, fake, 4, 8, 2, 96, 16, 64, _capi.PI_DTYPE_BF16, None,
+               None) == _capi.PI_ERR_UNSUPPORTED
+    assert pro(None, 1024, None, None, None, 1024, None, None, 256, _capi.PI_DTYPE_BF16, None,
+               None, 1e-5, None, None, None, 0, 8, 2, 128, 16, 64, _capi.PI_DTYPE_BF16, None,
+               None) == _capi.PI_OK
+    assert pro(None, 1024, None, None, None, 1024, None, None, 256, _capi.PI_DTYPE_BF16, None,
+               None, 1e-5, None, None, None, 4, 8, 2, 128, 16, 64, _capi.PI_DTYPE_BF16, None,
+               None) == _capi.PI_ERR_NULL_POINTER
+    # one QK-norm weight without the other
+    assert pro(fake, 1024, fake, fake, fake, 1024, fake, fake, 256, _capi.PI_DTYPE_BF16, fake,
+               None, 1e-5, fake, fake, fake, 4, 8, 2, 128, 16, 64, _capi.PI_DTYPE_BF16, None,
+               None) == _capi.PI_ERR_NULL_POINTER
+    # request stride shorter than the q heads
+    assert pro(fake, 1024, fake, fake, fake, 100, fake, fake, 256, _capi.PI_DTYPE_BF16, None,
+               None, 1e-5, fake, fake, fake, 4, 8, 2, 128, 16, 64, _capi.PI_DTYPE_BF16, None,
+               None) == _capi.PI_ERR_BAD_SHAPE
     # arrival counters (4096 requests x 64 KV heads) + the grid-completion counter block
     assert lib.pi_paged_decode_attn_ws_zero_bytes() == 4096 * 64 * 4 + 256
 

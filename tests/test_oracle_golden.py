@@ -2,8 +2,9 @@
 
 tests/golden/make_golden.py ran the reference's own functions (append_token,
 _write_kv_layer, paged_attention_v1, sink_completed_chunks, load_prefix,
-compute_prefix_hashes) on seeded inputs; here the numpy restatement must reproduce
-every one of those results (bit-exact for copies, 1e-5 for fp32 attention).
+compute_prefix_hashes, qk_norm + rope_positions) on seeded inputs; here the numpy
+restatement must reproduce every one of those results (bit-exact for copies, 1e-5 for
+fp32 attention and the fp32 decode prologue).
 """
 
 from __future__ import annotations
@@ -15,7 +16,9 @@ import numpy as np
 import pytest
 
 from oracle import paged_kv_oracle as orc
-from tests.golden.inputs import ATTENTION_CASES, attention_inputs, checksum
+from tests.golden.inputs import (
+    ATTENTION_CASES, PROLOGUE_CASES, attention_inputs, checksum, prologue_inputs,
+)
 
 GOLD = pathlib.Path(__file__).resolve().parent / "golden"
 
@@ -106,3 +109,27 @@ def test_bf16_rounding_is_round_to_nearest_even() -> None:
     bits = orc.f32_to_bf16_bits(x)
     ref = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     assert np.array_equal(bits, ref)
+
+
+@pytest.mark.parametrize("case", PROLOGUE_CASES, ids=[c["name"] for c in PROLOGUE_CASES])
+def test_decode_prologue_matches_reference(case: dict) -> None:
+    g = np.load(GOLD / "prologue.npz")
+    n = case["name"]
+    x = prologue_inputs(case)
+    assert checksum(*(x[k] for k in sorted(x))) == pytest.approx(float(g[n + "__checksum"]), rel=1e-12)
+    q, k, v = orc.decode_prologue(x["q"], x["k"], x["v"], x["positions"], g[n + "__inv_freq"],
+                                  x.get("q_norm_w"), x.get("k_norm_w"))
+    # fp32 both sides; cos/sin of angles up to ~3e4 rad differ by an ulp between libms
+    np.testing.assert_allclose(q, g[n + "__q"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(k, g[n + "__k"], rtol=1e-5, atol=1e-5)
+    assert np.array_equal(v, x["v"])
+
+
+@pytest.mark.parametrize("case", PROLOGUE_CASES, ids=[c["name"] for c in PROLOGUE_CASES])
+def test_rope_inv_freq_is_the_reference_table_frequency(case: dict) -> None:
+    # the product path's frequencies are bit-identical to the reference's fp32 table's
+    from plastic_infer_b200.kernels import rope_inv_freq
+
+    g = np.load(GOLD / "prologue.npz")
+    assert np.array_equal(rope_inv_freq(case["D"], case["base"]).numpy(),
+                          g[case["name"] + "__inv_freq"])
