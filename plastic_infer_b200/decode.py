@@ -6,8 +6,9 @@ gathers the whole context and runs SDPA (src/plastic_infer/exec/runner_paged.py:
 called per request by src/plastic_infer/runtime/engine.py:530-536). Here a step of B
 requests keeps device-resident block tables [n_layers, B, max_pages] (int32), context
 lengths [B] and slot mappings [n_layers, B], refreshed only when the host allocator
-hands out a page, so each layer costs one `kv_index_copy` and one
-`paged_decode_attention` launch for the whole batch.
+hands out a page. Past the projections, each layer costs two launches for the whole
+batch: `decode_prologue` (QK-norm, RoPE, and the write of the new K/V rows) and
+`paged_decode_attention`.
 """
 
 from __future__ import annotations
@@ -16,9 +17,8 @@ import torch
 import torch.nn.functional as F
 
 from . import kernels
-from .exec.attention import rms_norm, rope_positions
+from .exec.attention import rms_norm
 from .exec.runner import DenseWeights, ModelConfig, linear
-from .exec.runner_paged import _rope_table
 from .kv.kv_store import KVRequestCache, KVStore
 
 
@@ -64,8 +64,12 @@ def decode_step_paged_batched(weights: DenseWeights, config: ModelConfig, store:
                               tables: BatchTables | None = None) -> torch.Tensor:
     """One greedy-decode step for B requests; returns logits [B, vocab].
 
-    Per request the math is decode_step_paged's (src/plastic_infer/exec/runner_paged.py:209-274);
-    requests may have different lengths.
+    Per request the math is decode_step_paged's (src/plastic_infer/exec/runner_paged.py:209-274),
+    with the QK-norm of the MoE runner when the config has it
+    (src/plastic_infer/exec/runner_moe_paged.py:135-142); requests may have different
+    lengths. RoPE angles are pos * inv_freq in fp32, the values of the reference's fp32
+    table; the reference builds its table in the model dtype, which in bf16 runs rounds
+    the angles of late positions.
     """
     B = len(caches)
     dev, dt = weights.device, weights.dtype
@@ -80,25 +84,23 @@ def decode_step_paged_batched(weights: DenseWeights, config: ModelConfig, store:
     slots = torch.tensor([[c.block_table.slot(l, p) for c, p in zip(caches, positions)]
                           for l in range(L)], dtype=torch.int64, device=dev)
     ctx = torch.tensor([p + 1 for p in positions], dtype=torch.int32, device=dev)
-    pos_t = torch.tensor(positions, device=dev)
-    cos, sin = _rope_table(cfg.max_seq_len, cfg.head_dim, float(cfg.rope_base), dev, dt)
+    pos_t = torch.tensor(positions, dtype=torch.int64, device=dev)
+    inv_freq = kernels.rope_inv_freq(cfg.head_dim, float(cfg.rope_base), dev)
     x = weights["embed_tokens.weight"][torch.tensor(input_ids, device=dev)].to(dt).view(B, 1, -1)
     gpu = store.gpu
     for l in range(L):
         p = f"layers.{l}."
         h = rms_norm(x, weights[p + "input_layernorm.weight"])
-        q = linear(h, weights[p + "self_attn.q_proj.weight"]).view(B, 1, cfg.n_heads, cfg.head_dim)
-        k = linear(h, weights[p + "self_attn.k_proj.weight"]).view(B, 1, cfg.n_kv_heads, cfg.head_dim)
-        v = linear(h, weights[p + "self_attn.v_proj.weight"]).view(B, 1, cfg.n_kv_heads, cfg.head_dim)
-        # rope_positions broadcasts one position list over the batch; here each
-        # request has its own position, so apply it per row via the seq axis.
-        q = rope_positions(cos, sin, pos_t, q.transpose(0, 1)).transpose(0, 1)
-        k = rope_positions(cos, sin, pos_t, k.transpose(0, 1)).transpose(0, 1)
-        # one launch per layer: write the new K/V rows, then attend
-        attn = kernels.paged_decode_attention(q[:, 0].contiguous().to(gpu.dtype), gpu.k_phys,
-                                              gpu.v_phys, tables.tables[l], ctx,
-                                              k_new=k[:, 0].to(gpu.dtype), v_new=v[:, 0].to(gpu.dtype),
-                                              slot_mapping=slots[l])
+        q = linear(h, weights[p + "self_attn.q_proj.weight"]).view(B, cfg.n_heads, cfg.head_dim)
+        k = linear(h, weights[p + "self_attn.k_proj.weight"]).view(B, cfg.n_kv_heads, cfg.head_dim)
+        v = linear(h, weights[p + "self_attn.v_proj.weight"]).view(B, cfg.n_kv_heads, cfg.head_dim)
+        qw = kw = None
+        if cfg.qk_norm:
+            qw, kw = weights[p + "self_attn.q_norm.weight"], weights[p + "self_attn.k_norm.weight"]
+        # one launch: QK-norm + RoPE of q and k, new K/V rows written at their slots
+        qr = kernels.decode_prologue(q, k, v, pos_t, inv_freq, slots[l], gpu.k_phys, gpu.v_phys,
+                                     qw, kw)
+        attn = kernels.paged_decode_attention(qr, gpu.k_phys, gpu.v_phys, tables.tables[l], ctx)
         attn = attn.to(dt).view(B, 1, cfg.n_heads * cfg.head_dim)
         x = x + linear(attn, weights[p + "self_attn.o_proj.weight"])
         h = rms_norm(x, weights[p + "post_attention_layernorm.weight"])
