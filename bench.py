@@ -395,6 +395,73 @@ def bench_prologue(dev: torch.device, peak: float) -> dict:
     return res
 
 
+def bench_expert_copy(dev: torch.device) -> dict:
+    """MoE expert-slot copy: the step's missing experts, host banks -> device slot caches.
+
+    Qwen3-30B-A3B expert banks in bf16 (gate_up 2 x 768 x 2048, down 2048 x 768 per expert;
+    128 experts of one layer in pinned host memory, 32 device slots). Ours against the
+    reference's own fused multi-bank kernel (compiled from the reference tree into
+    oracle/_ref/, when present) and against the host link's measured pinned copy rate.
+    """
+    from plastic_infer_b200 import kernels
+
+    rows = (2 * 768 * 2048 * 2, 2048 * 768 * 2)  # bytes per expert row of each bank
+    E, SL = 128, 32
+    src = [torch.empty((E, rb), dtype=torch.uint8, pin_memory=True) for rb in rows]
+    for t in src:
+        t.random_(0, 256)
+    dst = [torch.empty((SL, rb), dtype=torch.uint8, device=dev) for rb in rows]
+    dptr = torch.tensor([d.data_ptr() for d in dst], dtype=torch.int64, device=dev)
+    sptr = torch.tensor([x.data_ptr() for x in src], dtype=torch.int64, device=dev)
+    feat = torch.tensor(list(rows), dtype=torch.int64, device=dev)
+    # link peak: one pinned 1 GiB host->device copy
+    h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    d.copy_(h)
+    torch.cuda.synchronize()
+    link = (1 << 30) / (time_region(lambda: d.copy_(h, non_blocking=True), 3,
+                                    torch.cuda.current_stream()) / 3 * 1e-3) / 1e9
+    del h, d
+    ref = None
+    ref_path = os.path.join(ROOT, "oracle", "_ref", "libref_expert_copy.so")
+    if os.path.exists(ref_path):
+        import ctypes
+
+        ref = ctypes.CDLL(ref_path)
+        ref.ref_fast_index_copy_multi_launch.argtypes = [ctypes.c_void_p] * 5 + [
+            ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        ref.ref_fast_index_copy_multi_launch.restype = None
+    res = dict(link_gbs=round(link, 1), banks="gate_up 6.0 MiB + down 3.0 MiB per expert",
+               reference_kernel="built" if ref is not None else "not built")
+    rng = np.random.default_rng(5)
+    for n in (1, 8, 32):
+        di = torch.from_numpy(rng.permutation(SL)[:n].astype(np.int32)).to(dev)
+        si = torch.from_numpy(rng.permutation(E)[:n].astype(np.int32)).to(dev)
+        num = torch.tensor([n], dtype=torch.int64, device=dev)
+        byts = float(n * sum(rows))
+
+        def ours():
+            kernels.expert_slot_copy(dptr, sptr, feat, di, si, num)
+
+        def theirs():
+            ref.ref_fast_index_copy_multi_launch(dptr.data_ptr(), sptr.data_ptr(), feat.data_ptr(),
+                                                 di.data_ptr(), si.data_ptr(), n, num.data_ptr(),
+                                                 len(rows), 1, torch.cuda.current_stream().cuda_stream)
+
+        entry = {}
+        for label, fn in (("ours", ours), ("reference_kernel", theirs)):
+            if label == "reference_kernel" and ref is None:
+                continue
+            fn()
+            torch.cuda.synchronize()
+            reps = 20
+            us = time_region(fn, reps, torch.cuda.current_stream()) / reps * 1e3
+            entry[label] = dict(us=round(us, 1), gbs=round(byts / (us * 1e-6) / 1e9, 1),
+                                frac_of_link=round(byts / (us * 1e-6) / 1e9 / link, 3))
+        res[f"experts_{n}"] = dict(bytes=int(byts), **entry)
+    return res
+
+
 class CpuSample:
     """The C3 KV path of `requests` requests on the CPU (the oracle, a numpy port of the
     reference's _write_kv_layer + paged_attention_v1), built once and run per layer.
@@ -689,6 +756,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if args.c2_only:
         run_c2_only(args, dev)
         return
+    if args.expert_copy_only:
+        print(json.dumps(dict(expert_copy=bench_expert_copy(dev))), flush=True)
+        return
+    if args.prologue_only:
+        print(json.dumps(dict(decode_prologue=bench_prologue(dev, measured_peaks()["hbm_gbs"]))),
+              flush=True)
+        return
     if args.workload == "c5":
         run_c5(args, rank, world, dev)
         return
@@ -764,6 +838,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
     pro = (bench_prologue(dev, peaks["hbm_gbs"])
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
+    exc = (bench_expert_copy(dev)
+           if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
     cpu = cpu_baseline_sample(cfg) if (rank == 0 and world == 1 and not args.skip_cpu) else None
 
     # measured DRAM bytes per launch exist for the C3 single-GPU launch only
@@ -808,6 +884,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 workload="fused QK-norm + RoPE + K/V slot write of one decode layer (bf16, D=128, "
                          "theta 1e6, positions < 8192) vs the reference's unfused GPU ops",
                 per_shape=pro, peak=peaks["hbm_gbs"])
+        if exc is not None:
+            line["expert_copy"] = exc
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -956,6 +1034,10 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
     ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
+    ap.add_argument("--expert-copy-only", action="store_true",
+                    help="run only the MoE expert-slot copy microbench")
+    ap.add_argument("--prologue-only", action="store_true",
+                    help="run only the fused decode-prologue microbench")
     ap.add_argument("--no-graph", action="store_true", help="launch every kernel from Python")
     ap.add_argument("--nccl", action="store_true",
                     help="N > 1: gather the per-layer outputs with NCCL all-gather instead of the "

@@ -253,6 +253,27 @@ int pi_paged_decode_attn_noalloc(void* out, const void* q, const void* k_pool,
                                  int64_t out_stride, int* err, cudaStream_t stream);
 
 /*
+ * MoE expert-slot copy, all banks in one launch (replaces the reference's fused
+ * multi-bank copy, plasticinfer_fast_index_copy_multi_launch:
+ * src/plastic_infer/kernel/fast_index_copy.py:190-244, kernel
+ * src/plastic_infer/kernel/csrc/jit/fast_index_copy.cuh:436-503; called by
+ * OffloadMoeCache.copy_missing, src/plastic_infer/moe/offload_cache.py:998-1012). Same
+ * arguments and meaning:
+ *   for b < num_banks, i < n:  dst_b[dst_indices[i]] = src_b[src_indices[i]]
+ * with row bytes feat_bytes[b], base addresses dst_ptrs[b] / src_ptrs[b] (int64 device
+ * arrays; the sources are pinned host banks read through their device alias), and
+ * n = min(num_indices[0], length) when num_indices (device int64 [1]) is given, else
+ * length. Indices are int32 when use_int32 != 0, else int64. A bank whose row bytes or
+ * base addresses are not 16-byte multiples is skipped with PI_ERR_MISALIGNED in `err`; a
+ * negative index skips its row with PI_ERR_SLOT_RANGE. Destination rows must be distinct.
+ * At most 32 banks.
+ */
+int pi_expert_slot_copy(const int64_t* dst_ptrs, const int64_t* src_ptrs,
+                        const int64_t* feat_bytes, int num_banks, const void* dst_indices,
+                        const void* src_indices, int64_t length, const int64_t* num_indices,
+                        int use_int32, int* err, cudaStream_t stream);
+
+/*
  * Fused decode prologue of one layer (no single reference counterpart; it replaces the
  * op sequence qk_norm -> rope_positions on q and k -> _write_kv_layer of the reference
  * runners: src/plastic_infer/exec/attention.py:23-95 and

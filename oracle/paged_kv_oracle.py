@@ -193,6 +193,26 @@ def decode_prologue(q: np.ndarray, k: np.ndarray, v: np.ndarray, positions: np.n
 
 
 # ---------------------------------------------------------------------------
+# MoE expert-slot copy (row gather by index, every bank)
+# ---------------------------------------------------------------------------
+
+
+def expert_slot_copy(dst_banks: list, src_banks: list, dst_idx: np.ndarray, src_idx: np.ndarray,
+                     n: int | None = None) -> None:
+    """dst_b[dst_idx[i]] = src_b[src_idx[i]] for every bank and i < n, in place.
+
+    The per-bank semantics of the reference's fused multi-bank copy
+    (src/plastic_infer/kernel/csrc/jit/fast_index_copy.cuh:448-472: row u // units of
+    src_indices, 16-byte units of the row) and of copy_missing's pageable path
+    (src/plastic_infer/moe/offload_cache.py:992-996: index_select + index_copy_). Banks are
+    2-D arrays [rows, feature]; destination rows must be distinct.
+    """
+    n = len(dst_idx) if n is None else min(int(n), len(dst_idx))
+    for dst, src in zip(dst_banks, src_banks):
+        dst[np.asarray(dst_idx[:n], dtype=np.int64)] = src[np.asarray(src_idx[:n], dtype=np.int64)]
+
+
+# ---------------------------------------------------------------------------
 # a3: page moves between the pool and host chunks
 # ---------------------------------------------------------------------------
 

@@ -74,6 +74,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
          _i64, _i64, _vp, _vp],
     ),
+    # dst_ptrs, src_ptrs, feat_bytes, num_banks, dst_indices, src_indices, length,
+    # num_indices, use_int32, err, stream
+    "pi_expert_slot_copy": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _i64, _vp, _i32, _vp, _vp]),
     # q_out, q_out_stride, k_pool, v_pool, q_in, q_in_stride, k_in, v_in, kv_in_stride,
     # in_dtype, q_norm_w, k_norm_w, eps, inv_freq, positions, slot_mapping, batch, hq, hkv,
     # head_dim, page_size, num_slots, pool_dtype, err, stream

@@ -207,6 +207,52 @@ def decode_prologue(
 
 
 # ---------------------------------------------------------------------------
+# f4: MoE expert-slot copy (all banks, one launch)
+# ---------------------------------------------------------------------------
+
+
+def expert_slot_copy(
+    dst_ptrs: torch.Tensor,
+    src_ptrs: torch.Tensor,
+    feat_bytes: torch.Tensor,
+    dst_indices: torch.Tensor,
+    src_indices: torch.Tensor,
+    num_indices: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+) -> None:
+    """dst_b[dst_indices[i]] = src_b[src_indices[i]] for every bank b and i < n, one launch.
+
+    The signature of the reference's fast_index_copy_multi_jit
+    (src/plastic_infer/kernel/fast_index_copy.py:208-244): dst_ptrs / src_ptrs / feat_bytes
+    are int64 [num_banks] CUDA tensors (slot-cache base, host-bank device alias, row
+    bytes), the index tensors int32 or int64 CUDA [L], num_indices an optional CUDA
+    int64 [1] valid length (n = min(num_indices[0], L)).
+    """
+    for t, name in ((dst_ptrs, "dst_ptrs"), (src_ptrs, "src_ptrs"), (feat_bytes, "feat_bytes")):
+        if t.dtype != torch.int64 or t.dim() != 1:
+            raise ValueError(f"{name} must be an int64 [num_banks] tensor")
+    if not (dst_ptrs.numel() == src_ptrs.numel() == feat_bytes.numel()):
+        raise ValueError("dst_ptrs, src_ptrs and feat_bytes must have one entry per bank")
+    if dst_indices.shape != src_indices.shape or dst_indices.dtype != src_indices.dtype \
+            or dst_indices.dtype not in (torch.int32, torch.int64) or dst_indices.dim() != 1:
+        raise ValueError("dst_indices and src_indices must be matching int32/int64 [L] tensors")
+    if num_indices is not None and (num_indices.dtype != torch.int64 or num_indices.numel() < 1):
+        raise ValueError("num_indices must be an int64 [1] tensor")
+    tensors = [dst_ptrs, src_ptrs, feat_bytes, dst_indices, src_indices]
+    if num_indices is not None:
+        tensors.append(num_indices)
+    _require_cuda(*tensors)
+    _capi.call(
+        "pi_expert_slot_copy",
+        dst_ptrs.contiguous().data_ptr(), src_ptrs.contiguous().data_ptr(),
+        feat_bytes.contiguous().data_ptr(), dst_ptrs.numel(), dst_indices.contiguous().data_ptr(),
+        src_indices.contiguous().data_ptr(), dst_indices.numel(),
+        num_indices.data_ptr() if num_indices is not None else None,
+        1 if dst_indices.dtype == torch.int32 else 0, _err_ptr(err), _stream(),
+    )
+
+
+# ---------------------------------------------------------------------------
 # a2: paged decode attention
 # ---------------------------------------------------------------------------
 

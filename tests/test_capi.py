@@ -88,6 +88,11 @@ def test_host_validation_rejects_before_launch(lib: ctypes.CDLL) -> None:
     assert pro(fake, 1024, fake, fake, fake, 100, fake, fake, 256, _capi.PI_DTYPE_BF16, None,
                None, 1e-5, fake, fake, fake, 4, 8, 2, 128, 16, 64, _capi.PI_DTYPE_BF16, None,
                None) == _capi.PI_ERR_BAD_SHAPE
+    # expert-slot copy: too many banks; nothing to do; null pointers
+    ec = lib.pi_expert_slot_copy
+    assert ec(fake, fake, fake, 33, fake, fake, 4, None, 1, None, None) == _capi.PI_ERR_BAD_SHAPE
+    assert ec(None, None, None, 2, None, None, 0, None, 1, None, None) == _capi.PI_OK
+    assert ec(None, fake, fake, 2, fake, fake, 4, None, 1, None, None) == _capi.PI_ERR_NULL_POINTER
     # arrival counters (4096 requests x 64 KV heads) + the grid-completion counter block
     assert lib.pi_paged_decode_attn_ws_zero_bytes() == 4096 * 64 * 4 + 256
 
