@@ -554,13 +554,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int role = (piece_start == lo) ? 0 : 1;
     const int64_t slot = static_cast<int64_t>(gw) * 2 + role;
     float* wo = p.ws_o + slot * kHeadsPad * D;
+    // only the G real heads (the MMA pads them to 8); the merge reads no others
 #pragma unroll
     for (int mt = 0; mt < C::kMT; ++mt) {
       const int d = 16 * mt + gid;
-      wo[g0 * D + d] = o[mt][0];
-      wo[g1 * D + d] = o[mt][1];
-      wo[g0 * D + d + 8] = o[mt][2];
-      wo[g1 * D + d + 8] = o[mt][3];
+      if (g0 < G) {
+        wo[g0 * D + d] = o[mt][0];
+        wo[g0 * D + d + 8] = o[mt][2];
+      }
+      if (g1 < G) {
+        wo[g1 * D + d] = o[mt][1];
+        wo[g1 * D + d + 8] = o[mt][3];
+      }
     }
     if (gid == 0) {
       float* wml = p.ws_ml + slot * kHeadsPad * 2;
