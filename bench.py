@@ -71,8 +71,9 @@ def measured_peaks() -> dict:
     if os.path.exists(path):
         with open(path) as f:
             d = json.load(f)
-        return dict(hbm_gbs=float(d["hbm_gbs"]), source="measured")
-    return dict(hbm_gbs=6650.0, source="fallback")
+        return dict(hbm_gbs=float(d["hbm_gbs"]), bf16_tflops=float(d.get("bf16_tflops", 1590.0)),
+                    source="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, source="fallback")
 
 
 def c3_contexts(cfg: dict) -> np.ndarray:
@@ -462,6 +463,60 @@ def bench_expert_copy(dev: torch.device) -> dict:
     return res
 
 
+def bench_prefill(dev: torch.device, peaks: dict) -> dict:
+    """Paged prefill attention of one request at the Qwen3-8B head shape (32 q / 8 KV heads,
+    head_dim 128, 16-token pages, bf16): a first 4096-token prefill (causal from 0) and a
+    1024-token chunk at position 3072 (the reference's offset-mask path). Ours against the
+    reference's algorithm on the same GPU (page gather, repeat_interleave, SDPA with
+    is_causal or with its dense mask). FLOPs = 4 * D * Hq * sum of the rows' key counts.
+    """
+    import torch.nn.functional as F
+
+    from plastic_infer_b200 import kernels
+
+    Hq, Hkv, D, S = 32, 8, 128, 16
+    kv = 4096
+    P = kv // S + 8
+    g = torch.Generator(device=dev).manual_seed(31)
+    kp = torch.randn((P, Hkv, S, D), dtype=torch.bfloat16, device=dev, generator=g)
+    vp = torch.randn_like(kp)
+    bt = torch.randperm(P, device=dev, generator=g)[:kv // S].to(torch.int32)
+    res = {}
+    for name, (q_len, q_start) in {"first_4096": (4096, 0), "chunk_1024_at_3072": (1024, 3072)}.items():
+        q = torch.randn((q_len, Hq, D), dtype=torch.bfloat16, device=dev, generator=g)
+        rows = torch.arange(q_start, q_start + q_len, dtype=torch.float64) + 1
+        flops = 4.0 * D * Hq * float(rows.clamp(max=kv).sum())
+
+        def ours():
+            kernels.paged_prefill_attention(q, kp, vp, bt, kv, q_start, True)
+
+        def reference():
+            k = kp[bt.long()].permute(0, 2, 1, 3).reshape(-1, Hkv, D)[:kv]
+            v = vp[bt.long()].permute(0, 2, 1, 3).reshape(-1, Hkv, D)[:kv]
+            qt = q.transpose(0, 1)[None]
+            kt = k.transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)[None]
+            vt = v.transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)[None]
+            if q_start == 0:
+                return F.scaled_dot_product_attention(qt, kt, vt, is_causal=True)
+            qpos = torch.arange(q_start, q_start + q_len, device=dev)
+            mask = torch.arange(kv, device=dev)[None, :] <= qpos[:, None]
+            am = torch.zeros(q_len, kv, dtype=q.dtype, device=dev).masked_fill(~mask, float("-inf"))
+            return F.scaled_dot_product_attention(qt, kt, vt, attn_mask=am[None, None])
+
+        entry = dict(q_len=q_len, q_start=q_start, kv_len=kv, gflop=round(flops / 1e9, 1))
+        for label, fn in (("ours", ours), ("reference_algorithm", reference)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            reps = 10
+            us = time_region(fn, reps, torch.cuda.current_stream()) / reps * 1e3
+            entry[label] = dict(us=round(us, 1), tflops=round(flops / (us * 1e-6) / 1e12, 1))
+        entry["speedup"] = round(entry["reference_algorithm"]["us"] / entry["ours"]["us"], 2)
+        entry["ours"]["frac_of_bf16_peak"] = round(entry["ours"]["tflops"] / peaks["bf16_tflops"], 3)
+        res[name] = entry
+    return res
+
+
 class CpuSample:
     """The C3 KV path of `requests` requests on the CPU (the oracle, a numpy port of the
     reference's _write_kv_layer + paged_attention_v1), built once and run per layer.
@@ -756,6 +811,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if args.c2_only:
         run_c2_only(args, dev)
         return
+    if args.prefill_only:
+        print(json.dumps(dict(prefill=bench_prefill(dev, measured_peaks()))), flush=True)
+        return
     if args.expert_copy_only:
         print(json.dumps(dict(expert_copy=bench_expert_copy(dev))), flush=True)
         return
@@ -1034,6 +1092,8 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
     ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the paged prefill attention microbench")
     ap.add_argument("--expert-copy-only", action="store_true",
                     help="run only the MoE expert-slot copy microbench")
     ap.add_argument("--prologue-only", action="store_true",

@@ -253,6 +253,30 @@ int pi_paged_decode_attn_noalloc(void* out, const void* q, const void* k_pool,
                                  int64_t out_stride, int* err, cudaStream_t stream);
 
 /*
+ * Paged prefill attention of one request: q_len new tokens against the first kv_len
+ * tokens of its pages, straight from the pool (replaces the prefill branch of
+ * _attn_paged, src/plastic_infer/exec/runner_paged.py:36-95: gather_paged_kv +
+ * repeat_interleave + SDPA, with is_causal when q_start_pos == 0 and a dense mask
+ * otherwise).
+ *   out[i, h, :] = softmax(scale * q[i, h, :] . K_{h/G}[j]) V_{h/G}[j]   over
+ *   j < lim(i),  lim(i) = min(kv_len, q_start + i + 1) if causal, else kv_len.
+ * With q_start == 0 and causal this is SDPA's is_causal (top-left aligned); with
+ * q_start > 0 it is the reference's offset mask (query i at position q_start + i).
+ *   q, out        [q_len, num_q_heads, head_dim], token strides q_tok_stride /
+ *                 out_tok_stride elements (heads contiguous)
+ *   block_table   [table_len] int32 page ids, device; kv_len <= table_len * page_size
+ * bf16 or f16 pools; head_dim 64 or 128; page_size 16 or 32; num_q_heads / num_kv_heads
+ * in {1, 2, 4, 8, 16}. Other shapes return PI_ERR_UNSUPPORTED. fp32 softmax and
+ * accumulation. Rows with no key (kv_len == 0) are zero.
+ */
+int pi_paged_prefill_attn(void* out, const void* q, const void* k_pool, const void* v_pool,
+                          const int32_t* block_table, int64_t table_len, int q_len, int kv_len,
+                          int q_start, int causal, int num_q_heads, int num_kv_heads,
+                          int head_dim, int page_size, int64_t num_pages, float scale, int dtype,
+                          int64_t q_tok_stride, int64_t out_tok_stride, int* err,
+                          cudaStream_t stream);
+
+/*
  * MoE expert-slot copy, all banks in one launch (replaces the reference's fused
  * multi-bank copy, plasticinfer_fast_index_copy_multi_launch:
  * src/plastic_infer/kernel/fast_index_copy.py:190-244, kernel

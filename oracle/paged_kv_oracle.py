@@ -142,6 +142,39 @@ def paged_attention_decode(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarr
     return out
 
 
+def paged_attention_prefill(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray,
+                            block_table: list[int], kv_len: int, q_start: int, causal: bool,
+                            page_size: int, scale: float | None = None) -> np.ndarray:
+    """Prefill attention of one request: q [q_len, Hq, D] over its first kv_len tokens.
+
+    src/plastic_infer/exec/runner_paged.py:36-95 (_attn_paged): query i sits at position
+    q_start + i; causal -> it sees keys j < min(kv_len, q_start + i + 1). With q_start == 0
+    that is SDPA's is_causal on the gathered context (attention.py:151-190, top-left
+    aligned), with q_start > 0 the dense mask built at runner_paged.py:70-76; non-causal
+    sees all kv_len keys. GQA head h reads KV head h // G. float64 softmax.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    L, Hq, D = q.shape
+    if kv_len == 0:
+        return np.zeros((L, Hq, D), dtype=np.float32)
+    k, v = gather_paged_kv(k_pages, v_pages, block_table, page_size, kv_len)  # [kv, H, D]
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    scale = 1.0 / np.sqrt(D) if scale is None else scale
+    kh = np.repeat(k, G, axis=1).transpose(1, 0, 2)      # [Hq, kv, D]
+    vh = np.repeat(v, G, axis=1).transpose(1, 0, 2)
+    s = np.einsum("lhd,hjd->hlj", q, kh) * scale          # [Hq, L, kv]
+    j = np.arange(kv_len)[None, :]
+    lim = np.minimum(kv_len, q_start + np.arange(L) + 1)[:, None] if causal else np.full((L, 1), kv_len)
+    s = np.where(j < lim, s, -np.inf)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("hlj,hjd->lhd", p, vh).astype(np.float32)
+
+
 # ---------------------------------------------------------------------------
 # Decode prologue: QK-norm + RoPE of the step's q / k rows (then the slot write above)
 # ---------------------------------------------------------------------------

@@ -74,6 +74,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
          _i64, _i64, _vp, _vp],
     ),
+    # out, q, k_pool, v_pool, block_table, table_len, q_len, kv_len, q_start, causal, hq,
+    # hkv, head_dim, page_size, num_pages, scale, dtype, q_tok_stride, out_tok_stride, err,
+    # stream
+    "pi_paged_prefill_attn": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i64,
+         _f32, _i32, _i64, _i64, _vp, _vp],
+    ),
     # dst_ptrs, src_ptrs, feat_bytes, num_banks, dst_indices, src_indices, length,
     # num_indices, use_int32, err, stream
     "pi_expert_slot_copy": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _i64, _vp, _i32, _vp, _vp]),

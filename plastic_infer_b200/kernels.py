@@ -455,6 +455,89 @@ def page_scatter(staging: torch.Tensor, page_ids: torch.Tensor, pool: torch.Tens
 
 
 # ---------------------------------------------------------------------------
+# f3: paged prefill attention
+# ---------------------------------------------------------------------------
+
+PREFILL_GROUPS = (1, 2, 4, 8, 16)
+
+
+def prefill_supported(q: torch.Tensor, k_pool: torch.Tensor) -> bool:
+    """Whether pi_paged_prefill_attn covers this q / pool combination."""
+    if k_pool.dim() != 4 or q.dim() not in (3, 4):
+        return False
+    P, Hkv, S, D = k_pool.shape
+    Hq = q.shape[-2]
+    return (k_pool.dtype in (torch.bfloat16, torch.float16) and q.dtype == k_pool.dtype
+            and D in (64, 128) and S in (16, 32) and q.shape[-1] == D and Hq % Hkv == 0
+            and Hq // Hkv in PREFILL_GROUPS)
+
+
+def paged_prefill_attention(
+    q: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_table: torch.Tensor,
+    kv_len: int,
+    q_start: int = 0,
+    causal: bool = True,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    err: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Prefill attention of one request's q [q_len, Hq, D] (or [1, q_len, Hq, D]) over the
+    first kv_len tokens of its pages (block_table: int32 [n] page ids, device).
+
+    Query i sits at position q_start + i; with `causal` it sees keys j <= q_start + i
+    (the reference's is_causal when q_start == 0, its offset mask otherwise:
+    src/plastic_infer/exec/runner_paged.py:36-95). Returns [q_len, Hq, D] in the pool dtype
+    (the input's leading batch axis is kept when given).
+    """
+    P, Hkv, S, D = _check_pool(k_pool, "k_pool")
+    if v_pool.shape != k_pool.shape or v_pool.dtype != k_pool.dtype:
+        raise ValueError("k_pool and v_pool must have the same shape and dtype")
+    batched = q.dim() == 4
+    if batched:
+        if q.shape[0] != 1:
+            raise ValueError("prefill attends one request: q must be [1, q_len, Hq, D]")
+        q3 = q[0]
+    else:
+        q3 = q
+    if q3.dim() != 3 or q3.shape[2] != D:
+        raise ValueError(f"q must be [q_len, Hq, {D}]")
+    if not prefill_supported(q3, k_pool):
+        raise ValueError("shape or dtype not covered by the prefill kernel (bf16/f16, head_dim "
+                         "64/128, page 16/32, Hq/Hkv in 1/2/4/8/16)")
+    if block_table.dtype != torch.int32 or block_table.dim() != 1:
+        raise ValueError("block_table must be int32 [n]")
+    q_len, Hq = q3.shape[0], q3.shape[1]
+    if kv_len > block_table.numel() * S or kv_len < 0 or q_start < 0:
+        raise ValueError("kv_len must be within the block table's pages")
+    _require_cuda(q3, k_pool, v_pool, block_table)
+    if q3.stride(2) != 1 or q3.stride(1) != D:
+        q3 = q3.contiguous()
+    if out is None:
+        out3 = torch.empty((q_len, Hq, D), dtype=k_pool.dtype, device=q3.device)
+    else:
+        out3 = out[0] if out.dim() == 4 else out
+        if out3.shape != (q_len, Hq, D) or out3.dtype != k_pool.dtype or out3.stride(2) != 1 \
+                or out3.stride(1) != D:
+            raise ValueError("out must be [q_len, Hq, D] in the pool dtype with contiguous heads")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    block_table = block_table.contiguous()
+    _capi.call(
+        "pi_paged_prefill_attn",
+        out3.data_ptr(), q3.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        block_table.data_ptr(), block_table.numel(), q_len, int(kv_len), int(q_start),
+        1 if causal else 0, Hq, Hkv, D, S, P, float(scale), dtype_code(k_pool.dtype),
+        q3.stride(0), out3.stride(0), _err_ptr(err), _stream(),
+    )
+    if out is not None:
+        return out
+    return out3.unsqueeze(0) if batched else out3
+
+
+# ---------------------------------------------------------------------------
 # e: decode attention with the all-gather fused in (multi-GPU, peer stores)
 # ---------------------------------------------------------------------------
 

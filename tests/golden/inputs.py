@@ -54,6 +54,29 @@ PROLOGUE_CASES = [
 ]
 
 
+# Prefill cases for _attn_paged (one request, q_len new tokens after q_start):
+# q_start == 0 / non-causal go through its is_causal SDPA path, q_start > 0 through its
+# dense offset mask. fp32 (the reference's exact path).
+PREFILL_CASES = [
+    dict(name="pf_causal0", seed=301, q_len=37, kv_len=37, q_start=0, causal=True,
+         Hq=4, Hkv=2, D=64, S=16),
+    dict(name="pf_offset", seed=302, q_len=13, kv_len=33, q_start=20, causal=True,
+         Hq=8, Hkv=2, D=64, S=16),
+    dict(name="pf_noncausal", seed=303, q_len=9, kv_len=40, q_start=31, causal=False,
+         Hq=4, Hkv=4, D=64, S=16),
+    dict(name="pf_g8_d128", seed=304, q_len=11, kv_len=17, q_start=6, causal=True,
+         Hq=16, Hkv=2, D=128, S=16),
+]
+
+
+def prefill_inputs(case: dict) -> dict:
+    """q [q_len, Hq, D] and the context's K/V rows [kv_len, Hkv, D], float32 ~N(0,1)."""
+    rng = np.random.default_rng(case["seed"])
+    return dict(q=rng.standard_normal((case["q_len"], case["Hq"], case["D"]), dtype=np.float32),
+                k=rng.standard_normal((case["kv_len"], case["Hkv"], case["D"]), dtype=np.float32),
+                v=rng.standard_normal((case["kv_len"], case["Hkv"], case["D"]), dtype=np.float32))
+
+
 def prologue_inputs(case: dict) -> dict:
     """q [B,Hq,D], k / v [B,Hkv,D] float32 ~N(0,1); QK-norm weights ~1 + 0.1 N(0,1)."""
     rng = np.random.default_rng(case["seed"])

@@ -16,6 +16,8 @@ tests/golden/inputs.py, and writes small fixtures next to this file:
   c1_tiny.npz                 prefill_forward_paged + 32 decode_step_paged greedy steps (C1)
   prologue.npz                qk_norm + rope_positions (fp32 table of build_rope_cache) outputs
                               for every PROLOGUE_CASES entry
+  prefill.npz                 _attn_paged prefill outputs (is_causal, offset mask, non-causal)
+                              and the block tables the reference's allocator produced
 
 The fixtures are what the oracle is pinned against (tests/test_oracle_golden.py)
 and what the GPU parity tests compare with; the reference tree itself is never
@@ -41,8 +43,8 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 from tests.golden.inputs import (  # noqa: E402
-    ATTENTION_CASES, C1_DECODE_STEPS, C1_LOGIT_STEPS, C1_MODEL, PROLOGUE_CASES, attention_inputs,
-    c1_prompts, c1_weights, checksum, prologue_inputs, token_kv,
+    ATTENTION_CASES, C1_DECODE_STEPS, C1_LOGIT_STEPS, C1_MODEL, PREFILL_CASES, PROLOGUE_CASES,
+    attention_inputs, c1_prompts, c1_weights, checksum, prefill_inputs, prologue_inputs, token_kv,
 )
 from oracle.paged_kv_oracle import f32_to_bf16_bits  # noqa: E402
 
@@ -271,6 +273,29 @@ def gen_prologue(ref) -> None:
     np.savez_compressed(HERE / "prologue.npz", **out)
 
 
+def gen_prefill(ref) -> None:
+    """_attn_paged on a KVStore filled token by token with append_token (fp32, CPU)."""
+    KVConfig, KVStore, attn_paged = ref["KVConfig"], ref["KVStore"], ref["_attn_paged"]
+    out = {}
+    for case in PREFILL_CASES:
+        x = prefill_inputs(case)
+        S, Hkv, D, kv = case["S"], case["Hkv"], case["D"], case["kv_len"]
+        cfg = KVConfig(n_layers=1, n_kv_heads=Hkv, head_dim=D, page_size=S, pages_per_chunk=2,
+                       max_pages=-(-kv // S) + 3, dtype=torch.float32, device=torch.device("cpu"))
+        store = KVStore(cfg)
+        cache = store.new_request()
+        for t in range(kv):
+            cache.append_token(torch.from_numpy(x["k"][t])[None], torch.from_numpy(x["v"][t])[None])
+        q = torch.from_numpy(x["q"])[None]
+        o = attn_paged(q, cache, 0, store, kv_num_tokens=kv, causal=case["causal"],
+                       q_start_pos=case["q_start"])
+        n = case["name"]
+        out[f"{n}__out"] = o[0].numpy().copy()
+        out[f"{n}__table"] = np.asarray(cache.get_block_table_for_layer(0), dtype=np.int32)
+        out[f"{n}__checksum"] = np.float64(checksum(x["q"], x["k"], x["v"]))
+    np.savez_compressed(HERE / "prefill.npz", **out)
+
+
 def load_reference(src: str) -> dict:
     sys.path.insert(0, src)
     from plastic_infer.exec.attention import (
@@ -278,7 +303,7 @@ def load_reference(src: str) -> dict:
     )
     from plastic_infer.exec.runner import DenseWeights, ModelConfig
     from plastic_infer.exec.runner_paged import (
-        _write_kv_layer, decode_step_paged, make_kv_config, prefill_forward_paged,
+        _attn_paged, _write_kv_layer, decode_step_paged, make_kv_config, prefill_forward_paged,
     )
     from plastic_infer.kv.chunk import compute_prefix_hashes
     from plastic_infer.kv.kv_store import KVConfig, KVStore
@@ -291,7 +316,7 @@ def main() -> None:
     ap.add_argument("--ref", required=True, help="path to the reference's src/ directory")
     ap.add_argument("--only", nargs="*", default=None,
                     help="generate only these fixtures (index_copy, attention, store, "
-                         "chunk_keys, allocator, c1, prologue)")
+                         "chunk_keys, allocator, c1, prologue, prefill)")
     args = ap.parse_args()
     torch.manual_seed(0)
     ref = load_reference(args.ref)
@@ -303,6 +328,7 @@ def main() -> None:
         allocator=lambda: gen_allocator(ref),
         c1=lambda: gen_c1(ref),
         prologue=lambda: gen_prologue(ref),
+        prefill=lambda: gen_prefill(ref),
     )
     for name, gen in gens.items():
         if args.only is None or name in args.only:

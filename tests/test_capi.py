@@ -88,6 +88,17 @@ def test_host_validation_rejects_before_launch(lib: ctypes.CDLL) -> None:
     assert pro(fake, 1024, fake, fake, fake, 100, fake, fake, 256, _capi.PI_DTYPE_BF16, None,
                None, 1e-5, fake, fake, fake, 4, 8, 2, 128, 16, 64, _capi.PI_DTYPE_BF16, None,
                None) == _capi.PI_ERR_BAD_SHAPE
+    # paged prefill: head_dim 256 and fp32 unsupported; group 3 unsupported; kv_len beyond
+    # the block table; nothing to do
+    pf = lib.pi_paged_prefill_attn
+    args = lambda q_len, kv, hq, hkv, D, S, dt, tl: (  # noqa: E731
+        fake, fake, fake, fake, fake, tl, q_len, kv, 0, 1, hq, hkv, D, S, 64, 1.0, dt, hq * D,
+        hq * D, None, None)
+    assert pf(*args(4, 16, 8, 2, 256, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_ERR_UNSUPPORTED
+    assert pf(*args(4, 16, 8, 2, 128, 16, _capi.PI_DTYPE_F32, 1)) == _capi.PI_ERR_UNSUPPORTED
+    assert pf(*args(4, 16, 6, 2, 128, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_ERR_UNSUPPORTED
+    assert pf(*args(4, 17, 8, 2, 128, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_ERR_BAD_SHAPE
+    assert pf(*args(0, 16, 8, 2, 128, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_OK
     # expert-slot copy: too many banks; nothing to do; null pointers
     ec = lib.pi_expert_slot_copy
     assert ec(fake, fake, fake, 33, fake, fake, 4, None, 1, None, None) == _capi.PI_ERR_BAD_SHAPE

@@ -2,7 +2,8 @@
 
 tests/golden/make_golden.py ran the reference's own functions (append_token,
 _write_kv_layer, paged_attention_v1, sink_completed_chunks, load_prefix,
-compute_prefix_hashes, qk_norm + rope_positions) on seeded inputs; here the numpy
+compute_prefix_hashes, qk_norm + rope_positions, _attn_paged prefill) on seeded inputs;
+here the numpy
 restatement must reproduce every one of those results (bit-exact for copies, 1e-5 for
 fp32 attention and the fp32 decode prologue).
 """
@@ -17,7 +18,8 @@ import pytest
 
 from oracle import paged_kv_oracle as orc
 from tests.golden.inputs import (
-    ATTENTION_CASES, PROLOGUE_CASES, attention_inputs, checksum, prologue_inputs,
+    ATTENTION_CASES, PREFILL_CASES, PROLOGUE_CASES, attention_inputs, checksum, prefill_inputs,
+    prologue_inputs,
 )
 
 GOLD = pathlib.Path(__file__).resolve().parent / "golden"
@@ -133,3 +135,28 @@ def test_rope_inv_freq_is_the_reference_table_frequency(case: dict) -> None:
     g = np.load(GOLD / "prologue.npz")
     assert np.array_equal(rope_inv_freq(case["D"], case["base"]).numpy(),
                           g[case["name"] + "__inv_freq"])
+
+
+def prefill_pools(case: dict, x: dict, table: np.ndarray):
+    """Logical [P, H, D, S] pools holding the context's K/V rows at the table's pages."""
+    S, Hkv, D = case["S"], case["Hkv"], case["D"]
+    P = int(table.max()) + 1 if len(table) else 1
+    k = np.zeros((P, Hkv, D, S), dtype=np.float32)
+    v = np.zeros_like(k)
+    for t in range(case["kv_len"]):
+        k[table[t // S], :, :, t % S] = x["k"][t]
+        v[table[t // S], :, :, t % S] = x["v"][t]
+    return k, v
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES, ids=[c["name"] for c in PREFILL_CASES])
+def test_prefill_matches_reference(case: dict) -> None:
+    g = np.load(GOLD / "prefill.npz")
+    n = case["name"]
+    x = prefill_inputs(case)
+    assert checksum(x["q"], x["k"], x["v"]) == pytest.approx(float(g[n + "__checksum"]), rel=1e-12)
+    table = g[n + "__table"]
+    k, v = prefill_pools(case, x, table)
+    out = orc.paged_attention_prefill(x["q"], k, v, list(table), case["kv_len"], case["q_start"],
+                                      case["causal"], case["S"])
+    np.testing.assert_allclose(out, g[n + "__out"], rtol=1e-5, atol=1e-5)
