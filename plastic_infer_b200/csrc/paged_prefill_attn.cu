@@ -15,7 +15,9 @@
 // Q as the A operand held in registers for the whole KV loop, K^T fetched by ldmatrix
 // from the swizzled page tile; P V with P taken straight from the S accumulators and V
 // by ldmatrix.trans. Online softmax in base 2, fp32. The 4 warps consume one TMA ring of
-// NS page stages ("full" barrier: TMA bytes; "empty" barrier: 4 warp arrivals).
+// NS page stages (a "full" mbarrier per stage counts the TMA bytes). The CTA's page ids
+// are staged in shared memory once; whichever warp finishes a stage last (a shared
+// arrival counter) refills it at once, so no warp waits for another to issue loads.
 // Every wait is bounded; a failing warp marks the CTA and thread 0 drains in-flight
 // loads before the CTA exits.
 #include <cudaTypedefs.h>
@@ -35,6 +37,7 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRows = 16 * kWarps;  // query rows per CTA
 constexpr int kStages = 4;
+constexpr int kIdCache = 2048;  // page ids staged in shared memory (32k tokens at S = 16)
 constexpr unsigned kFull = 0xffffffffu;
 
 template <int D, int S>
@@ -52,10 +55,6 @@ struct Cfg {
 template <int S>
 __device__ __forceinline__ uint32_t tile_off(int t, int d) {
   return static_cast<uint32_t>((d >> 6) * (S * 128) + t * 128 + ((((d & 63) >> 3) ^ (t & 7)) << 4));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 struct PrefillParams {
@@ -82,6 +81,9 @@ __global__ void __launch_bounds__(kThreads)
                                               ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(tiles + kStages * C::kStageBytes);
   __shared__ int s_failed;
+  __shared__ int s_issued;           // pages issued so far (for the drain)
+  __shared__ int s_arrived[kStages];  // warps done with the stage's current page
+  __shared__ int s_tile[kIdCache];    // TMA tile row (page_id * Hkv + h) of page k
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -114,32 +116,35 @@ __global__ void __launch_bounds__(kThreads)
   for (int o = 16; o >= 1; o >>= 1) wmin = min(wmin, __shfl_xor_sync(kFull, wmin, o));
 
   const uint32_t full0 = smem_u32(bars);
-  const uint32_t empty0 = smem_u32(bars + kStages);
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, kWarps);
-    }
+    for (int s = 0; s < kStages; ++s) mbar_init(full0 + 8 * s, 1);
     fence_mbar_init();
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
     s_failed = 0;
+    s_issued = 0;
   }
-  __syncthreads();
+  if (tid < kStages) s_arrived[tid] = 0;
 
-  // Programmatic launch: q and the pools may be the previous kernel's output.
+  // Programmatic launch: q, the pools and the block table may be the previous kernel's
+  // output.
   pdl_wait();
   pdl_trigger();
 
-  const uint32_t tiles_u32 = smem_u32(tiles);
-  int issued = 0;  // thread 0 only
-  auto issue = [&](int k) {
+  auto tile_of = [&](int k) -> int {
     int pid = __ldg(p.block_table + k);
     if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
       record_error(p.err, PI_ERR_PAGE_RANGE);
       pid = 0;
     }
-    const int tile = pid * p.hkv + h;
+    return pid * p.hkv + h;
+  };
+  for (int i = tid; i < npages && i < kIdCache; i += kThreads) s_tile[i] = tile_of(i);
+  __syncthreads();
+
+  const uint32_t tiles_u32 = smem_u32(tiles);
+  auto issue = [&](int k) {
+    const int tile = k < kIdCache ? s_tile[k] : tile_of(k);
     const int stage = k % kStages;
     const uint32_t bar = full0 + 8 * stage;
     const uint32_t kdst = tiles_u32 + stage * C::kStageBytes;
@@ -153,7 +158,9 @@ __global__ void __launch_bounds__(kThreads)
     }
   };
   if (tid == 0) {
-    for (; issued < kStages && issued < npages; ++issued) issue(issued);
+    const int first = npages < kStages ? npages : kStages;
+    for (int k = 0; k < first; ++k) issue(k);
+    s_issued = first;
   }
 
   // Q rows as the MMA A operand for every k-step (rows past q_len are zero).
@@ -299,17 +306,19 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
 
+    // The last warp done with this stage refills it with page k + NS: this warp's reads of
+    // the stage precede its count (warp barrier + CTA-scope release); the last counter
+    // acquires every warp's, then hands the stage to the async proxy.
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * stage);
-    // thread 0 refills this stage with page k + NS once all four warps are done with it
-    if (tid == 0 && issued < npages) {
-      if (mbar_wait_bounded(empty0 + 8 * stage, static_cast<uint32_t>((k / kStages) & 1))) {
-        issue(issued);
-        ++issued;
-      } else {
-        record_error(p.err, PI_ERR_TIMEOUT);
-        failed = true;
-        break;
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&s_arrived[stage], 1) == kWarps - 1) {
+        __threadfence_block();
+        s_arrived[stage] = 0;
+        if (k + kStages < npages) {
+          issue(k + kStages);
+          atomicAdd(&s_issued, 1);
+        }
       }
     }
   }
@@ -337,6 +346,7 @@ __global__ void __launch_bounds__(kThreads)
   // flight; the last kStages issued pages are the only ones that can still be landing.
   __syncthreads();
   if (tid == 0 && s_failed) {
+    const int issued = s_issued;
     for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
       mbar_wait_bounded(full0 + 8 * (j % kStages), static_cast<uint32_t>((j / kStages) & 1));
   }
@@ -345,7 +355,7 @@ __global__ void __launch_bounds__(kThreads)
 template <typename T, int D, int S>
 int launch(const PrefillParams& p, const CUtensorMap& tk, const CUtensorMap& tv, cudaStream_t stream) {
   using C = Cfg<D, S>;
-  constexpr size_t smem = 1024 + static_cast<size_t>(kStages) * C::kStageBytes + 2 * kStages * 8;
+  constexpr size_t smem = 1024 + static_cast<size_t>(kStages) * C::kStageBytes + kStages * 8;
   auto kern = paged_prefill_kernel<T, D, S>;
   static bool configured[64] = {};  // per device: the dynamic shared memory limit is set
   int dev = 0;
