@@ -11,6 +11,19 @@ These are the batched additions behind the reference's single-request API:
   page_gather / page_scatter
                          pool <-> staging moves for the host store
                          (reference: src/plastic_infer/kv/kv_store.py:258-269, 311-321)
+  paged_decode_attention_gather
+                         decode attention of one KV-head shard with the all-gather of the
+                         per-rank outputs fused in (NVLink peer stores; multi-GPU)
+  decode_prologue        QK-norm + RoPE of a step's q/k rows and the K/V slot write, one
+                         launch (reference: attention.py:23-95 + _write_kv_layer)
+  paged_prefill_attention
+                         one request's prefill straight from the pool
+                         (reference: _attn_paged, src/plastic_infer/exec/runner_paged.py:36-95)
+  expert_slot_copy       MoE expert rows from pinned host banks into device slots, all banks
+                         in one launch (reference: fast_index_copy_multi_jit)
+  set_programmatic_launch
+                         programmatic dependent launch for the index-copy, prologue and
+                         attention kernels
 
 Pools are the *physical* tensors [num_pages, kv_heads, page_size, head_dim]. Every
 function launches on torch's current stream, as the reference's ctypes launch does
