@@ -57,6 +57,7 @@ constexpr int kMaxBatch = 4096;      // prefix table lives in shared memory
 constexpr int kMaxKvHeads = 64;      // arrival counters: kMaxBatch x kMaxKvHeads
 constexpr int kMaxCtasPerSm = 2;     // workspace is sized for this many
 constexpr int kHeadsPad = 8;         // n dimension of the MMAs (query heads per KV head)
+constexpr int64_t kL2PrefetchBytes = int64_t{48} << 20;  // pages warmed before the launch wait
 constexpr unsigned kFull = 0xffffffffu;
 
 struct FastParams {
@@ -146,54 +147,124 @@ struct RowDsts {
 template <typename T, int D>
 __device__ __noinline__ void merge_pieces(const RowDsts<T> dst, const float* ws_ml,
                                           const float* ws_o, int wa, int npieces, int role_a,
-                                          int G, int lane) {
-  // All heads at once: lanes split into G groups of `lph` lanes, lane = (head g,
-  // column chunk); every load of a phase is independent, so the merge costs two
-  // memory round trips whatever G and the piece count are.
+                                          int G, int lane, uint32_t stage_s, int stage_bytes) {
+  // The merge sits on the launch's critical path: the segment's last piece ends with
+  // the rest of the grid, and nothing else can cover its latency. So it is written
+  // for latency rather than for throughput:
+  // - all heads at once: lanes split into G groups of `lph` lanes, and lane (g, i)
+  //   owns the float4 columns i, i + lph, i + 2 lph, ... of head g, so every read of a
+  //   piece (global or shared) is contiguous across the group, and the output store of
+  //   one column group is one 8-byte store;
+  // - each batch's maximum first, so the pieces' weights are independent of each
+  //   other (no serial exp2 chain through a running maximum);
+  // - staged (stage_bytes > 0: the calling warp's page ring, idle at the end of its
+  //   range): cp.async copies a batch of pieces' (O, m, l) records into shared memory
+  //   at once, one L2 round trip for as many pieces as the ring holds (15 at G = 4,
+  //   D = 128, 4 stages);
+  // - otherwise (a merge in the middle of the range, page loads still in flight in the
+  //   ring) the loads go straight to registers.
   const int gp = G <= 1 ? 1 : (G <= 2 ? 2 : (G <= 4 ? 4 : 8));
   const int lph = (32 / gp) * 4 <= D ? 32 / gp : D / 4;  // lanes per head, >= 1 float4 each
   const int g = lane / lph;
+  const int li = lane % lph;
   const int n4 = D / (4 * lph);      // float4 per lane
-  const int d0 = (lane % lph) * 4 * n4;
-  if (g >= G) return;
   auto slot_of = [&](int j) { return static_cast<int64_t>(wa + j) * 2 + (j == 0 ? role_a : 0); };
   float M = -INFINITY;
-#pragma unroll 8
-  for (int j = 0; j < npieces; ++j) M = fmaxf(M, __ldcg(ws_ml + slot_of(j) * kHeadsPad * 2 + g * 2));
   float L = 0.f;
   float4 acc[D / 16];  // n4 <= D / 16 (G = 8)
 #pragma unroll
   for (int e = 0; e < D / 16; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
-  // Four pieces' loads in flight at once at D <= 128 (at D = 256 it would spill the page loop).
-  constexpr int kPieceUnroll = D <= 128 ? 4 : 1;
-#pragma unroll kPieceUnroll
-  for (int j = 0; j < npieces; ++j) {
-    const int64_t sl = slot_of(j);
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(ws_ml + sl * kHeadsPad * 2 + g * 2));
-    const float w = fast_exp2(ml.x - M);
-    L += w * ml.y;
-    const float4* src = reinterpret_cast<const float4*>(ws_o + sl * kHeadsPad * D + g * D + d0);
-#pragma unroll
-    for (int e = 0; e < D / 16; ++e) {
-      if (e < n4) {
-        const float4 v = __ldcg(src + e);
-        acc[e].x += w * v.x;
-        acc[e].y += w * v.y;
-        acc[e].z += w * v.z;
-        acc[e].w += w * v.w;
+  auto acc_add = [&](int e, float w, float4 v) {
+    acc[e].x += w * v.x;
+    acc[e].y += w * v.y;
+    acc[e].z += w * v.z;
+    acc[e].w += w * v.w;
+  };
+  // Every piece holds at least one context token, so its max is finite; the guards
+  // only keep two -inf maxima (possible only with -inf scores) from making a NaN.
+  auto weight = [](float m, float ref) { return m == ref ? 1.f : fast_exp2(m - ref); };
+  // One piece's record in the stage: O of its G heads [G][D] fp32, then (m, l) per head.
+  const int obytes = G * D * 4;
+  const int rec = obytes + ((G * 8 + 15) & ~15);
+  const int cap = stage_bytes / rec;
+  if (cap > 0) {
+    const int cpr = rec / 16;       // 16-byte chunks per record
+    const int co = obytes / 16;     // ... of which O
+    const uint8_t* sp = static_cast<const uint8_t*>(__cvta_shared_to_generic(stage_s));
+    for (int j0 = 0; j0 < npieces; j0 += cap) {
+      const int n = min(cap, npieces - j0);
+      for (int q = 0; q < n; ++q) {
+        const int64_t sl = slot_of(j0 + q);
+        const char* os = reinterpret_cast<const char*>(ws_o + sl * kHeadsPad * D);
+        const char* ms = reinterpret_cast<const char*>(ws_ml + sl * kHeadsPad * 2) - obytes;
+        const uint32_t dq = stage_s + static_cast<uint32_t>(q * rec);
+        for (int w = lane; w < cpr; w += 32) cp_async_16(dq + w * 16, (w < co ? os : ms) + w * 16);
       }
+      cp_async_wait_all();
+      __syncwarp();
+      if (g < G) {
+        float mb = M;
+        for (int q = 0; q < n; ++q)
+          mb = fmaxf(mb, *reinterpret_cast<const float*>(sp + q * rec + obytes + g * 8));
+        // rescale what earlier batches accumulated
+        const float a = weight(M, mb);
+        M = mb;
+        L *= a;
+#pragma unroll
+        for (int e = 0; e < D / 16; ++e) {
+          acc[e].x *= a;
+          acc[e].y *= a;
+          acc[e].z *= a;
+          acc[e].w *= a;
+        }
+        for (int q = 0; q < n; ++q) {
+          const uint8_t* r = sp + q * rec;
+          const float2 ml = *reinterpret_cast<const float2*>(r + obytes + g * 8);
+          const float w = weight(ml.x, M);
+          L += w * ml.y;
+          const float4* v = reinterpret_cast<const float4*>(r) + g * (D / 4) + li;
+#pragma unroll
+          for (int e = 0; e < D / 16; ++e)
+            if (e < n4) acc_add(e, w, v[e * lph]);
+        }
+      }
+      __syncwarp();
+    }
+  } else if (g < G) {
+#pragma unroll 8
+    for (int j = 0; j < npieces; ++j) M = fmaxf(M, __ldcg(ws_ml + slot_of(j) * kHeadsPad * 2 + g * 2));
+    // (at D = 256 more than one piece in flight would spill the page loop)
+    constexpr int kPieceUnroll = D <= 128 ? 4 : 1;
+#pragma unroll kPieceUnroll
+    for (int j = 0; j < npieces; ++j) {
+      const int64_t sl = slot_of(j);
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(ws_ml + sl * kHeadsPad * 2 + g * 2));
+      const float w = weight(ml.x, M);
+      L += w * ml.y;
+      const float4* src = reinterpret_cast<const float4*>(ws_o + sl * kHeadsPad * D + g * D) + li;
+#pragma unroll
+      for (int e = 0; e < D / 16; ++e)
+        if (e < n4) acc_add(e, w, __ldcg(src + e * lph));
     }
   }
+  if (g >= G) return;
   const float inv = L > 0.f ? 1.f / L : 0.f;
   for (int k = 0; k < dst.n; ++k) {
+    T* row = dst.p[k] + g * D;
+    const bool vec = (reinterpret_cast<uintptr_t>(row) & 7) == 0;
 #pragma unroll
     for (int e = 0; e < D / 16; ++e) {
       if (e < n4) {
-        T* o = dst.p[k] + g * D + d0 + 4 * e;
-        o[0] = from_f32<T>(acc[e].x * inv);
-        o[1] = from_f32<T>(acc[e].y * inv);
-        o[2] = from_f32<T>(acc[e].z * inv);
-        o[3] = from_f32<T>(acc[e].w * inv);
+        T* o = row + 4 * (li + e * lph);
+        const float4 x = make_float4(acc[e].x * inv, acc[e].y * inv, acc[e].z * inv, acc[e].w * inv);
+        if (vec) {
+          *reinterpret_cast<uint2*>(o) = make_uint2(MmaOp<T>::pack(x.x, x.y), MmaOp<T>::pack(x.z, x.w));
+        } else {
+          o[0] = from_f32<T>(x.x);
+          o[1] = from_f32<T>(x.y);
+          o[2] = from_f32<T>(x.z);
+          o[3] = from_f32<T>(x.w);
+        }
       }
     }
   }
@@ -412,6 +483,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   int id_cur = load_ids(lo);
   int id_nxt = load_ids(lo + 32);
 
+  // Warm L2 with this warp's first pages (lane j: page lo + j) while the previous kernel
+  // on the stream may still be running. The CTAs of a programmatic launch become
+  // resident as the previous grid's CTAs retire and then wait below for its tail, with
+  // HBM mostly idle. A prefetch moves nothing into this CTA, and L2 is where every
+  // write to device memory lands, so whatever the previous kernel still writes to these
+  // pages is what the loads after the wait read. The grid prefetches at most
+  // kL2PrefetchBytes, well inside L2, so the pages are still there when used.
+  if (active) {
+    const int64_t budget = kL2PrefetchBytes / (static_cast<int64_t>(NW) * C::kStageBytes);
+    const int64_t npf = min(min(hi - lo, budget), static_cast<int64_t>(32));
+    if (lane < npf) {
+#pragma unroll
+      for (int j = 0; j < C::kBoxes; ++j) {
+        tma_prefetch_l2_2d(&tmap_k, 64 * j, id_cur * S);
+        tma_prefetch_l2_2d(&tmap_v, 64 * j, id_cur * S);
+      }
+    }
+  }
+
   // Everything above reads only ctx_lens and block_tables. Under a programmatic launch
   // the previous kernel on the stream may still be running up to here; from here on
   // its results (q, the pools, the launch counter) are complete and visible.
@@ -585,9 +675,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (old != npieces - 1) return;
     __threadfence();
     const int role_a = (total * wa / NWe == seg_start) ? 0 : 1;
+    // At the end of the range every page load has been consumed: the ring is free.
+    const bool ring_idle = piece_end == hi;
     merge_pieces<T, D>(row_dsts(static_cast<int64_t>(cb) * p.out_stride +
                                 static_cast<int64_t>(ch) * G * D),
-                       p.ws_ml, p.ws_o, wa, npieces, role_a, G, lane);
+                       p.ws_ml, p.ws_o, wa, npieces, role_a, G, lane, tiles_u32,
+                       ring_idle ? NS * C::kStageBytes : 0);
     if (lane == 0) p.ws_cnt[cb * Hkv + ch] = 0;
   };
 
