@@ -277,6 +277,59 @@ int pi_paged_prefill_attn(void* out, const void* q, const void* k_pool, const vo
                           cudaStream_t stream);
 
 /*
+ * One span of a KV sequence for pi_host_stream_attn: `len` tokens whose K element
+ * (kv head h, token t, dim d) is k[h * head_stride + t * tok_stride + d * dim_stride]
+ * (V the same with v). k and v point to device memory or to page-locked host memory
+ * (cudaHostAlloc / cudaHostRegister), which the kernel reads in place through its
+ * mapped device alias. Strides are in elements and non-negative.
+ */
+typedef struct pi_kv_span {
+  const void* k;
+  const void* v;
+  int64_t len;
+  int64_t head_stride;
+  int64_t tok_stride;
+  int64_t dim_stride;
+} pi_kv_span_t;
+
+#define PI_HS_MAX_SPANS 512
+
+/*
+ * Attention of one request over a KV sequence split into spans (replaces
+ * host_stream_attention_v1, src/plastic_infer/exec/attention.py:193-250: host chunks
+ * [H_kv, D, C] oldest first, then the resident tail [1, R, H_kv, D], concatenated,
+ * GQA-expanded and fed to SDPA). The spans are concatenated in order into positions
+ * [0, kv_len); host spans cross the host link once and are never staged.
+ *   out[i, h, :] = softmax_j(scale * q[i, h, :] . K_{h/G}[j]) V_{h/G}[j]
+ * over every j when causal == 0, else over j <= q_start + i (the reference's offset
+ * mask; with q_start == 0 and q_len == kv_len this is SDPA's is_causal). Rows with no
+ * visible key are zero.
+ *   q, out   device, [q_len, num_q_heads, head_dim], token strides q_tok_stride /
+ *            out_tok_stride elements, heads and dims contiguous
+ *   spans    HOST array of num_spans <= PI_HS_MAX_SPANS descriptors, read during the
+ *            call; a span whose memory has no device alias (pageable host memory)
+ *            returns PI_ERR_UNSUPPORTED
+ *   workspace  device scratch of pi_host_stream_attn_workspace_size(...) bytes,
+ *            256-byte aligned (none needed when that size is 0)
+ *   flags    0, or PI_HS_SPANS_CHECKED: the caller has established that every span
+ *            is device memory or page-locked host memory, and the library then skips
+ *            its per-span pointer queries (about a microsecond each) and uses host
+ *            addresses as device addresses, as unified addressing maps pinned memory
+ *            (registered memory only where the device reports it can use host pointers)
+ * dtype f32, bf16 or f16 for q, out and every span; head_dim a multiple of 8, <= 256;
+ * fp32 arithmetic. Two launches (splits, then their merge) when the sequence is long
+ * enough to be split, else one.
+ */
+size_t pi_host_stream_attn_workspace_size(int q_len, int num_q_heads, int num_kv_heads,
+                                          int head_dim, int64_t kv_len);
+#define PI_HS_SPANS_CHECKED 1
+int pi_host_stream_attn(void* out, const void* q, int64_t q_tok_stride, int64_t out_tok_stride,
+                        const pi_kv_span_t* spans, int num_spans, int q_len, int64_t q_start,
+                        int causal, int num_q_heads, int num_kv_heads, int head_dim, float scale,
+                        int dtype, void* workspace, size_t workspace_bytes, int flags, int* err,
+                        cudaStream_t stream);
+
+/*
  * MoE expert-slot copy, all banks in one launch (replaces the reference's fused
  * multi-bank copy, plasticinfer_fast_index_copy_multi_launch:
  * src/plastic_infer/kernel/fast_index_copy.py:190-244, kernel

@@ -175,6 +175,42 @@ def paged_attention_prefill(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndar
     return np.einsum("hlj,hjd->lhd", p, vh).astype(np.float32)
 
 
+def host_stream_attention(q: np.ndarray, host_chunks: list[tuple[np.ndarray, np.ndarray]],
+                          resident_k: np.ndarray, resident_v: np.ndarray, q_start: int = 0,
+                          causal: bool = True, scale: float | None = None) -> np.ndarray:
+    """Attention over host chunks plus a resident tail (one request).
+
+    src/plastic_infer/exec/attention.py:193-250 (host_stream_attention_v1): the chunks
+    ([H_kv, D, C] each, oldest first) and the tail ([1, R, H_kv, D]) are concatenated
+    into [1, kv_len, H_kv, D]; query row i of q [1, q_len, Hq, D] sits at position
+    q_start + i. causal -> it sees keys j <= q_start + i (the dense mask of :236-243, and
+    SDPA's is_causal when q_start == 0 and q_len == kv_len, which is the same set);
+    non-causal sees every key. GQA head h reads KV head h // G. float64 softmax; rows
+    with no visible key (kv_len == 0) are zero.
+    """
+    q = np.asarray(q, dtype=np.float64)[0]                       # [L, Hq, D]
+    parts_k = [np.asarray(kc, dtype=np.float64).transpose(2, 0, 1) for kc, _ in host_chunks]
+    parts_v = [np.asarray(vc, dtype=np.float64).transpose(2, 0, 1) for _, vc in host_chunks]
+    k = np.concatenate(parts_k + [np.asarray(resident_k, dtype=np.float64)[0]], axis=0)
+    v = np.concatenate(parts_v + [np.asarray(resident_v, dtype=np.float64)[0]], axis=0)
+    L, Hq, D = q.shape
+    kv_len, Hkv = k.shape[0], k.shape[1]
+    if kv_len == 0:
+        return np.zeros((1, L, Hq, D), dtype=np.float32)
+    G = Hq // Hkv
+    scale = 1.0 / np.sqrt(D) if scale is None else scale
+    kh = np.repeat(k, G, axis=1).transpose(1, 0, 2)              # [Hq, kv, D]
+    vh = np.repeat(v, G, axis=1).transpose(1, 0, 2)
+    s = np.einsum("lhd,hjd->hlj", q, kh) * scale                 # [Hq, L, kv]
+    if causal:
+        j = np.arange(kv_len)[None, :]
+        s = np.where(j <= q_start + np.arange(L)[:, None], s, -np.inf)
+    s = s - s.max(axis=-1, keepdims=True)
+    p_ = np.exp(s)
+    p_ /= p_.sum(axis=-1, keepdims=True)
+    return np.einsum("hlj,hjd->lhd", p_, vh)[None].astype(np.float32)
+
+
 # ---------------------------------------------------------------------------
 # Decode prologue: QK-norm + RoPE of the step's q / k rows (then the slot write above)
 # ---------------------------------------------------------------------------

@@ -34,7 +34,7 @@ PI_DTYPE_F32 = 0
 PI_DTYPE_BF16 = 1
 PI_DTYPE_F16 = 2
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int
@@ -93,6 +93,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i32, _vp, _vp, _f32, _vp, _vp, _vp,
          _i32, _i32, _i32, _i32, _i32, _i64, _i32, _vp, _vp],
     ),
+    # q_len, num_q_heads, num_kv_heads, head_dim, kv_len
+    "pi_host_stream_attn_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i64]),
+    # out, q, q_tok_stride, out_tok_stride, spans (host array), num_spans, q_len, q_start,
+    # causal, hq, hkv, head_dim, scale, dtype, workspace, workspace_bytes, flags, err, stream
+    "pi_host_stream_attn": (
+        _i32,
+        [_vp, _vp, _i64, _i64, _vp, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _f32, _i32, _vp,
+         _sz, _i32, _vp, _vp],
+    ),
     "pi_paged_kv_gather": (_i32, [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _vp, _vp]),
     "pi_page_gather": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _i32, _i64, _vp, _vp]),
     "pi_page_scatter": (_i32, [_vp, _vp, _vp, _i64, _i32, _i64, _i32, _i64, _vp, _vp]),
@@ -112,6 +121,23 @@ class PeerGather(ctypes.Structure):
         ("rank_stride", ctypes.c_int64),
         ("epoch", ctypes.c_uint),
         ("launch_counter", ctypes.c_void_p),
+    ]
+
+
+HS_MAX_SPANS = 512  # PI_HS_MAX_SPANS
+HS_SPANS_CHECKED = 1  # PI_HS_SPANS_CHECKED
+
+
+class KvSpan(ctypes.Structure):
+    """pi_kv_span_t (include/plastic_kv.h)."""
+
+    _fields_ = [
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("len", ctypes.c_int64),
+        ("head_stride", ctypes.c_int64),
+        ("tok_stride", ctypes.c_int64),
+        ("dim_stride", ctypes.c_int64),
     ]
 
 

@@ -27,7 +27,7 @@ bool programmatic_launch() { return g_programmatic.load(std::memory_order_relaxe
 
 }  // namespace pi
 
-extern "C" int pi_abi_version(void) { return 2; }
+extern "C" int pi_abi_version(void) { return 3; }
 
 extern "C" int pi_set_programmatic_launch(int enable) {
   pi::g_programmatic.store(enable ? 1 : 0, std::memory_order_relaxed);

@@ -9,6 +9,9 @@ Drop-in for src/plastic_infer/exec/attention.py:
                          over the pages); for prefill (Sq > 1) the reference algorithm
                          (gather + SDPA) over the kernel gather. Paged prefill is not
                          part of the decode hot path.
+* `host_stream_attention_v1` -> pi_host_stream_attn: one pass over the host chunks
+                         (pinned ones read in place) and the resident tail, instead of
+                         concatenating them and running SDPA (attention.py:193-250).
 * RoPE / RMSNorm / QK-norm keep the reference math (attention.py:23-95); they are
   used by the runners, not by the KV path.
 
@@ -142,29 +145,32 @@ def host_stream_attention_v1(q: torch.Tensor, host_chunks: list[tuple[torch.Tens
                              resident_k: torch.Tensor, resident_v: torch.Tensor,
                              q_start_pos: int = 0, causal: bool = True) -> torch.Tensor:
     """Attention over host chunks ([H_kv, D, C] each, oldest first) plus a resident
-    tail ([1, R, H_kv, D]); reference semantics (attention.py:193-250).
+    tail ([1, R, H_kv, D]); the reference's semantics (attention.py:193-250) computed by
+    the flash-incremental kernel its docstring anticipates (pi_host_stream_attn).
 
-    The chunks are brought to the query's device and concatenated there (the
-    reference concatenates wherever the tensors live).
+    Nothing is concatenated: each chunk and the tail is one span of the kernel's KV
+    sequence. Chunks in page-locked host memory (the host KV store's buffers) are read
+    in place over the host link; pageable or other-dtype chunks are first copied to the
+    query's GPU in q's dtype. Returns [1, q_len, Hq, D].
     """
-    dev = q.device
-    k_parts = [kc.to(dev, non_blocking=True).permute(2, 0, 1) for kc, _ in host_chunks]
-    v_parts = [vc.to(dev, non_blocking=True).permute(2, 0, 1) for _, vc in host_chunks]
-    k_full = torch.cat(k_parts + [resident_k[0]], dim=0).unsqueeze(0)
-    v_full = torch.cat(v_parts + [resident_v[0]], dim=0).unsqueeze(0)
-    q_len, kv_len = q.shape[1], k_full.shape[1]
-    q_t, k_t, v_t = q.transpose(1, 2), k_full.transpose(1, 2), v_full.transpose(1, 2)
-    Hq, Hkv = q_t.shape[1], k_t.shape[1]
-    if Hq != Hkv:
-        assert Hq % Hkv == 0
-        k_t = k_t.repeat_interleave(Hq // Hkv, dim=1)
-        v_t = v_t.repeat_interleave(Hq // Hkv, dim=1)
-    if causal and (q_start_pos > 0 or q_len != kv_len):
-        q_pos = torch.arange(q_start_pos, q_start_pos + q_len, device=dev)
-        kv_pos = torch.arange(kv_len, device=dev)
-        mask = torch.zeros(q_len, kv_len, dtype=q.dtype, device=dev)
-        mask = mask.masked_fill(kv_pos[None, :] > q_pos[:, None], float("-inf"))
-        out = F.scaled_dot_product_attention(q_t, k_t, v_t, attn_mask=mask[None, None])
-    else:
-        out = F.scaled_dot_product_attention(q_t, k_t, v_t, is_causal=causal)
-    return out.transpose(1, 2)
+    kernels._require_cuda(q)
+    dev, dt = q.device, q.dtype
+
+    def place(t: torch.Tensor) -> torch.Tensor:
+        if t.dtype != dt or (t.is_cuda and t.device != dev) or (not t.is_cuda and not t.is_pinned()):
+            return t.to(dev, dt)
+        return t
+
+    def pair(k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        k, v = place(k), place(v)
+        if k.stride() != v.stride():  # the kernel reads K and V of a span with one stride set
+            k, v = k.to(dev).contiguous(), v.to(dev).contiguous()
+        return k, v
+
+    spans = []
+    for kc, vc in host_chunks:
+        kc, vc = pair(kc, vc)
+        spans.append((kc.permute(0, 2, 1), vc.permute(0, 2, 1)))   # [H_kv, C, D]
+    rk, rv = pair(resident_k[0], resident_v[0])                     # [R, H_kv, D]
+    spans.append((rk.permute(1, 0, 2), rv.permute(1, 0, 2)))       # [H_kv, R, D]
+    return kernels.host_stream_attention(q, spans, q_start=q_start_pos, causal=causal)

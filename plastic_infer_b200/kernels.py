@@ -21,6 +21,9 @@ These are the batched additions behind the reference's single-request API:
                          (reference: _attn_paged, src/plastic_infer/exec/runner_paged.py:36-95)
   expert_slot_copy       MoE expert rows from pinned host banks into device slots, all banks
                          in one launch (reference: fast_index_copy_multi_jit)
+  host_stream_attention  one request's attention over host-resident chunks (pinned, read in
+                         place) plus a device tail (reference: host_stream_attention_v1,
+                         src/plastic_infer/exec/attention.py:193-250)
   set_programmatic_launch
                          programmatic dependent launch for the index-copy, prologue and
                          attention kernels
@@ -28,7 +31,8 @@ These are the batched additions behind the reference's single-request API:
 Pools are the *physical* tensors [num_pages, kv_heads, page_size, head_dim]. Every
 function launches on torch's current stream, as the reference's ctypes launch does
 (src/plastic_infer/kernel/fast_index_copy.py:185), and raises `KernelError` on a
-non-zero status. Inputs must be CUDA tensors; there is no CPU path.
+non-zero status. Inputs must be CUDA tensors (host_stream_attention also reads
+page-locked host tensors in place); there is no CPU path.
 """
 
 from __future__ import annotations
@@ -37,6 +41,7 @@ import ctypes
 import math
 import threading
 
+import numpy as np
 import torch
 
 from . import _capi
@@ -545,6 +550,131 @@ def paged_prefill_attention(
         1 if causal else 0, Hq, Hkv, D, S, P, float(scale), dtype_code(k_pool.dtype),
         q3.stride(0), out3.stride(0), _err_ptr(err), _stream(),
     )
+    if out is not None:
+        return out
+    return out3.unsqueeze(0) if batched else out3
+
+
+# ---------------------------------------------------------------------------
+# f2: attention over host-resident chunks + a device tail, read in place
+# ---------------------------------------------------------------------------
+
+_keep_lock = threading.Lock()
+_keep: list[tuple[torch.cuda.Event, tuple]] = []
+_hs_ws: dict[int, Workspace] = {}
+
+
+def _keep_until_done(tensors: list[torch.Tensor]) -> None:
+    """Hold host tensors a launch reads in place until the launch has run: torch cannot
+    see a kernel's reads of pinned memory, and would otherwise recycle the pages."""
+    if not tensors or torch.cuda.is_current_stream_capturing():
+        return
+    ev = torch.cuda.Event()
+    ev.record()
+    with _keep_lock:
+        _keep[:] = [(e, t) for e, t in _keep if not e.query()]
+        _keep.append((ev, tuple(tensors)))
+
+
+def host_stream_attention(
+    q: torch.Tensor,
+    kv_spans,
+    q_start: int = 0,
+    causal: bool = True,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    workspace: Workspace | None = None,
+    err: torch.Tensor | None = None,
+    num_kv_heads: int | None = None,
+) -> torch.Tensor:
+    """Attention of one request over a KV sequence given as spans, on the host or the GPU.
+
+    q is [q_len, Hq, D] (or [1, q_len, Hq, D]) on the GPU; query i sits at position
+    q_start + i. kv_spans is a sequence of (k, v) views shaped [H_kv, T, D] (any strides;
+    k and v alike) that concatenate, in order, into the request's keys and values. A span
+    lives on the query's GPU or in page-locked host memory, which the kernel reads in
+    place over the host link: host chunks are never staged or materialised. With
+    `causal`, query i sees keys j <= q_start + i; otherwise every key. Returns
+    [q_len, Hq, D] in q's dtype (the leading batch axis is kept when given).
+
+    The pinned spans stay referenced until the launch has run. Under CUDA-graph capture
+    the caller keeps them alive for the graph's lifetime.
+    """
+    batched = q.dim() == 4
+    if batched:
+        if q.shape[0] != 1:
+            raise ValueError("host-stream attention attends one request: q must be [1, q_len, Hq, D]")
+        q3 = q[0]
+    else:
+        q3 = q
+    if q3.dim() != 3:
+        raise ValueError("q must be [q_len, Hq, D]")
+    _require_cuda(q3)
+    q_len, Hq, D = q3.shape
+    if q_start < 0:
+        raise ValueError("q_start must be >= 0")
+    if q3.stride(2) != 1 or q3.stride(1) != D:
+        q3 = q3.contiguous()
+    code = dtype_code(q3.dtype)
+    kv_spans = list(kv_spans)
+    if len(kv_spans) > _capi.HS_MAX_SPANS:
+        raise ValueError(f"at most {_capi.HS_MAX_SPANS} spans per call")
+    rows: list[tuple[int, int, int, int, int, int]] = []
+    hkv = num_kv_heads
+    kv_len = 0
+    host: list[torch.Tensor] = []
+    for i, (k, v) in enumerate(kv_spans):
+        if k.dim() != 3 or k.shape != v.shape or k.stride() != v.stride():
+            raise ValueError("each span is a (k, v) pair of [H_kv, T, D] views with equal strides")
+        if k.shape[2] != D:
+            raise ValueError(f"span {i} has head_dim {k.shape[2]}, q has {D}")
+        if hkv is None:
+            hkv = k.shape[0]
+        elif k.shape[0] != hkv:
+            raise ValueError("every span must have the same number of KV heads")
+        if k.dtype != q3.dtype or v.dtype != q3.dtype:
+            raise TypeError(f"span {i} is {k.dtype}; q is {q3.dtype}")
+        if k.is_cuda or v.is_cuda:
+            if k.device != q3.device or v.device != q3.device:
+                raise ValueError(f"span {i} is on {k.device}, q on {q3.device}")
+        else:
+            if not (k.is_pinned() and v.is_pinned()):
+                raise ValueError(f"host span {i} must be in page-locked memory (Tensor.pin_memory())")
+            host += [k, v]
+        rows.append((k.data_ptr(), v.data_ptr(), k.shape[1], k.stride(0), k.stride(1), k.stride(2)))
+        kv_len += k.shape[1]
+    if hkv is None:
+        hkv = Hq  # no keys at all: every row is zero
+    if Hq % hkv:
+        raise ValueError(f"Hq={Hq} is not a multiple of H_kv={hkv}")
+    if out is None:
+        out3 = torch.empty((q_len, Hq, D), dtype=q3.dtype, device=q3.device)
+    else:
+        out3 = out[0] if out.dim() == 4 else out
+        if out3.shape != (q_len, Hq, D) or out3.dtype != q3.dtype or out3.stride(2) != 1 \
+                or out3.stride(1) != D:
+            raise ValueError("out must be [q_len, Hq, D] in q's dtype with contiguous heads")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    nbytes = int(_capi.load().pi_host_stream_attn_workspace_size(q_len, Hq, hkv, D, kv_len))
+    ws_ptr = None
+    if nbytes:
+        if workspace is None:
+            idx = q3.device.index
+            with _ws_lock:
+                workspace = _hs_ws.get(idx)
+                if workspace is None:
+                    workspace = _hs_ws[idx] = Workspace(q3.device)
+        ws_ptr = workspace.get(nbytes).data_ptr()
+    # pi_kv_span_t[]: six 64-bit fields per span (two addresses, length, three strides)
+    table = np.array(rows if rows else [(0, 0, 0, 0, 0, 1)], dtype=np.uint64)
+    _capi.call(
+        "pi_host_stream_attn",
+        out3.data_ptr(), q3.data_ptr(), q3.stride(0), out3.stride(0), table.ctypes.data,
+        len(kv_spans), q_len, int(q_start), 1 if causal else 0, Hq, hkv, D, float(scale), code,
+        ws_ptr, nbytes, _capi.HS_SPANS_CHECKED, _err_ptr(err), _stream(),
+    )
+    _keep_until_done(host)
     if out is not None:
         return out
     return out3.unsqueeze(0) if batched else out3

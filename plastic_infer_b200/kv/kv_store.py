@@ -110,6 +110,9 @@ class KVRequestCache:
         self._length = 0
         self.chunk_keys: list[ChunkKey] = []
         self._final_hash: Optional[bytes] = None
+        # Leading complete chunks whose device pages evict_chunks released: their K/V
+        # live only in the host store, and their block-table entries are -1.
+        self.evicted_chunks = 0
 
     @property
     def length(self) -> int:
@@ -194,6 +197,8 @@ class KVStore:
         self._host_lru: OrderedDict[bytes, None] = OrderedDict()
         self._max_host_chunks = config.max_host_chunks
         self._prefix_index: dict[bytes, ChunkKey] = {}
+        # host chunks that a live request has evicted from the device: not LRU-evictable
+        self._host_pins: dict[bytes, int] = {}
         c = config
         on_cuda = self.gpu.device.type == "cuda"
         self._chunk_pool = _PinnedChunkPool(
@@ -207,7 +212,10 @@ class KVStore:
         return KVRequestCache(self, request_id=request_id)
 
     def free_request(self, cache: KVRequestCache) -> None:
-        self.gpu.allocator.free_many(list(cache.block_table.all_page_ids()))
+        self.gpu.allocator.free_many([p for p in cache.block_table.all_page_ids() if p >= 0])
+        for c in range(min(cache.evicted_chunks, len(cache.chunk_keys))):
+            self._unpin_host(cache.chunk_keys[c].full_key)
+        cache.evicted_chunks = 0
 
     # -- sinking (device -> host) -------------------------------------------------
 
@@ -238,8 +246,11 @@ class KVStore:
             if full_key in self._host_cache:
                 self._touch_host(full_key)
                 continue
+            if chunk_idx < cache.evicted_chunks:
+                continue  # its device pages are gone: nothing left to copy
             while len(self._host_cache) >= self._max_host_chunks:
-                self._evict_host_lru()
+                if not self._evict_host_lru():
+                    break  # every cached chunk is held by a live request
             todo.append((chunk_idx, key))
             # Reserve the LRU slot now so later chunks of this call evict correctly.
             self._host_cache[full_key] = (None, None)  # type: ignore[assignment]
@@ -344,29 +355,84 @@ class KVStore:
 
     def evict_chunks(self, need_pages: int,
                      protected_request: Optional[KVRequestCache] = None) -> int:
-        """Free pages of the oldest complete chunks of `protected_request`.
+        """Free the device pages of the oldest complete chunks of `protected_request`.
 
-        Mirrors the reference v1 policy exactly (src/plastic_infer/kv/kv_store.py:340-386),
-        including its documented quirk: freed pages stay in the request's block
-        table (stale entries), and the newest complete chunk is kept.
+        The reference's v1 policy (src/plastic_infer/kv/kv_store.py:340-386): oldest
+        chunk first, the newest complete chunk is always kept, stop once `need_pages`
+        pages are freed; returns the pages freed (0 without a protected request).
+
+        Fixed here: the reference leaves freed pages in the request's block table
+        (kv_store.py:380-383), so a second call frees them again (the allocator's
+        double-free assertion) and attention would read pages that now belong to
+        another request. Here an evicted chunk's block-table entries become -1, the
+        request counts its leading evicted chunks (`evicted_chunks`) and a later call
+        continues after them, and the chunk's host copy (if it was sunk) is held in
+        the host LRU while the request lives. Attention over such a request reads the
+        host copies in place: host_stream_attention_v1(q, *store.host_stream_chunks(
+        cache, layer), ...). Evicting a chunk that was never sunk loses its K/V, as in
+        the reference; host_stream_chunks then raises.
         """
         if protected_request is None:
             return 0
         cfg = self.config
+        cache = protected_request
         freed = 0
-        for chunk_idx in range(protected_request.num_complete_chunks() - 1):
-            if freed >= need_pages:
-                break
-            start = chunk_idx * cfg.pages_per_chunk
+        n_full = cache.num_complete_chunks()
+        while cache.evicted_chunks < n_full - 1 and freed < need_pages:
+            c = cache.evicted_chunks
+            start = c * cfg.pages_per_chunk
             pages: list[int] = []
             for layer in range(cfg.n_layers):
+                row = cache.block_table.pages[layer]
                 for j in range(cfg.pages_per_chunk):
                     lp = start + j
-                    if lp < protected_request.block_table.num_logical_pages(layer):
-                        pages.append(protected_request.block_table.get_page(layer, lp))
+                    if lp < len(row) and row[lp] >= 0:
+                        pages.append(row[lp])
+                        row[lp] = -1
             self.gpu.allocator.free_many(pages)
             freed += len(pages)
+            if c < len(cache.chunk_keys):
+                self._pin_host(cache.chunk_keys[c].full_key)
+            cache.evicted_chunks += 1
         return freed
+
+    def host_stream_chunks(self, cache: KVRequestCache, layer: int
+                           ) -> tuple[list[tuple[torch.Tensor, torch.Tensor]], torch.Tensor, torch.Tensor]:
+        """The KV of one layer of `cache` as host_stream_attention_v1 takes it.
+
+        Returns (host_chunks, resident_k, resident_v). host_chunks holds the host copies
+        of the request's evicted chunks, oldest first, as [H_kv, D, C] views of the
+        pinned chunk buffers: the kernel reads them in place, nothing is copied back.
+        resident_k / resident_v [1, R, H_kv, D] are the tokens still in the device pool,
+        gathered in one launch each.
+        """
+        cfg = self.config
+        chunks: list[tuple[torch.Tensor, torch.Tensor]] = []
+        for c in range(cache.evicted_chunks):
+            key = cache.chunk_keys[c].full_key if c < len(cache.chunk_keys) else None
+            kv = self._host_cache.get(key) if key is not None else None
+            if kv is None or kv[0] is None:
+                raise RuntimeError(f"chunk {c} left the device pool without a host copy")
+            chunks.append((kv[0][layer], kv[1][layer]))
+        start = cache.evicted_chunks * cfg.pages_per_chunk
+        table = cache.block_table.pages[layer][start:]
+        n_tail = cache.length - cache.evicted_chunks * cfg.tokens_per_chunk
+        dev = self.gpu.device
+        bt = torch.tensor(table if table else [0], dtype=torch.int32, device=dev)
+        rk = kernels.paged_kv_gather(self.gpu.k_phys, bt, n_tail).unsqueeze(0)
+        rv = kernels.paged_kv_gather(self.gpu.v_phys, bt, n_tail).unsqueeze(0)
+        return chunks, rk, rv
+
+    def _pin_host(self, full_key: bytes) -> None:
+        if full_key in self._host_cache:
+            self._host_pins[full_key] = self._host_pins.get(full_key, 0) + 1
+
+    def _unpin_host(self, full_key: bytes) -> None:
+        n = self._host_pins.get(full_key, 0)
+        if n <= 1:
+            self._host_pins.pop(full_key, None)
+        else:
+            self._host_pins[full_key] = n - 1
 
     # -- host LRU -------------------------------------------------------------------
 
@@ -375,16 +441,20 @@ class KVStore:
             del self._host_lru[full_key]
         self._host_lru[full_key] = None
 
-    def _evict_host_lru(self) -> None:
-        if not self._host_lru:
-            return
-        oldest, _ = self._host_lru.popitem(last=False)
+    def _evict_host_lru(self) -> bool:
+        """Drop the least recently used host chunk that no live request holds; False
+        when there is none."""
+        oldest = next((k for k in self._host_lru if k not in self._host_pins), None)
+        if oldest is None:
+            return False
+        del self._host_lru[oldest]
         del self._host_cache[oldest]
         self._prefix_index.pop(oldest, None)
         phys = self._host_phys.pop(oldest, None)
         if phys is not None:
             self._chunk_pool.give(phys[0])
             self._chunk_pool.give(phys[1])
+        return True
 
     @property
     def host_cache_size(self) -> int:

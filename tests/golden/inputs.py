@@ -69,6 +69,44 @@ PREFILL_CASES = [
 ]
 
 
+# host_stream_attention_v1 cases: a contiguous KV of `total` tokens split into host
+# chunks of `chunk` tokens ([H_kv, D, C], the reference's host layout) covering the first
+# `host` tokens, plus the resident tail. The first four follow the shapes of the
+# reference's own tests of the op; the rest are model-sized. fp32 ~ 0.3 N(0, 1).
+HOST_STREAM_CASES = [
+    dict(name="hs_tail_prefill", seed=401, total=10, host=6, chunk=3, q_len=2, q_start=10,
+         causal=True, Hq=4, Hkv=2, D=16),
+    dict(name="hs_decode", seed=402, total=8, host=5, chunk=4, q_len=1, q_start=8,
+         causal=True, Hq=4, Hkv=2, D=16),
+    dict(name="hs_offset_suffix", seed=403, total=8, host=4, chunk=2, q_len=2, q_start=5,
+         causal=True, Hq=4, Hkv=2, D=16),
+    dict(name="hs_all_resident", seed=404, total=6, host=0, chunk=3, q_len=6, q_start=0,
+         causal=True, Hq=4, Hkv=2, D=16),
+    dict(name="hs_8b_decode", seed=405, total=700, host=640, chunk=64, q_len=1, q_start=700,
+         causal=True, Hq=32, Hkv=8, D=128),
+    dict(name="hs_moe_suffix", seed=406, total=300, host=256, chunk=128, q_len=5, q_start=295,
+         causal=True, Hq=32, Hkv=4, D=128),
+    dict(name="hs_noncausal", seed=407, total=90, host=60, chunk=20, q_len=3, q_start=0,
+         causal=False, Hq=8, Hkv=8, D=64),
+]
+
+
+def host_stream_inputs(case: dict) -> dict:
+    """q [1, q_len, Hq, D]; host chunks (k_c, v_c) [H_kv, D, C]; resident [1, R, H_kv, D]."""
+    rng = np.random.default_rng(case["seed"])
+    Hkv, D = case["Hkv"], case["D"]
+    k_full = (0.3 * rng.standard_normal((1, case["total"], Hkv, D))).astype(np.float32)
+    v_full = (0.3 * rng.standard_normal((1, case["total"], Hkv, D))).astype(np.float32)
+    q = (0.3 * rng.standard_normal((1, case["q_len"], case["Hq"], D))).astype(np.float32)
+    chunks = []
+    for s in range(0, case["host"], case["chunk"]):
+        e = min(s + case["chunk"], case["host"])
+        chunks.append((np.ascontiguousarray(k_full[0, s:e].transpose(1, 2, 0)),
+                       np.ascontiguousarray(v_full[0, s:e].transpose(1, 2, 0))))
+    return dict(q=q, chunks=chunks, rk=np.ascontiguousarray(k_full[:, case["host"]:]),
+                rv=np.ascontiguousarray(v_full[:, case["host"]:]), k_full=k_full, v_full=v_full)
+
+
 def prefill_inputs(case: dict) -> dict:
     """q [q_len, Hq, D] and the context's K/V rows [kv_len, Hkv, D], float32 ~N(0,1)."""
     rng = np.random.default_rng(case["seed"])

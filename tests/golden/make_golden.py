@@ -43,8 +43,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 from tests.golden.inputs import (  # noqa: E402
-    ATTENTION_CASES, C1_DECODE_STEPS, C1_LOGIT_STEPS, C1_MODEL, PREFILL_CASES, PROLOGUE_CASES,
-    attention_inputs, c1_prompts, c1_weights, checksum, prefill_inputs, prologue_inputs, token_kv,
+    ATTENTION_CASES, C1_DECODE_STEPS, C1_LOGIT_STEPS, C1_MODEL, HOST_STREAM_CASES, PREFILL_CASES,
+    PROLOGUE_CASES, attention_inputs, c1_prompts, c1_weights, checksum, host_stream_inputs,
+    prefill_inputs, prologue_inputs, token_kv,
 )
 from oracle.paged_kv_oracle import f32_to_bf16_bits  # noqa: E402
 
@@ -296,10 +297,25 @@ def gen_prefill(ref) -> None:
     np.savez_compressed(HERE / "prefill.npz", **out)
 
 
+def gen_host_stream(ref) -> None:
+    """host_stream_attention_v1 on CPU fp32 tensors, host chunks in the reference layout."""
+    hs = ref["host_stream_attention_v1"]
+    out = {}
+    for case in HOST_STREAM_CASES:
+        x = host_stream_inputs(case)
+        chunks = [(torch.from_numpy(kc), torch.from_numpy(vc)) for kc, vc in x["chunks"]]
+        o = hs(torch.from_numpy(x["q"]), chunks, torch.from_numpy(x["rk"]),
+               torch.from_numpy(x["rv"]), q_start_pos=case["q_start"], causal=case["causal"])
+        n = case["name"]
+        out[f"{n}__out"] = o.numpy().copy()
+        out[f"{n}__checksum"] = np.float64(checksum(x["q"], x["k_full"], x["v_full"]))
+    np.savez_compressed(HERE / "host_stream.npz", **out)
+
+
 def load_reference(src: str) -> dict:
     sys.path.insert(0, src)
     from plastic_infer.exec.attention import (
-        build_rope_cache, paged_attention_v1, qk_norm, rope_positions,
+        build_rope_cache, host_stream_attention_v1, paged_attention_v1, qk_norm, rope_positions,
     )
     from plastic_infer.exec.runner import DenseWeights, ModelConfig
     from plastic_infer.exec.runner_paged import (
@@ -316,7 +332,7 @@ def main() -> None:
     ap.add_argument("--ref", required=True, help="path to the reference's src/ directory")
     ap.add_argument("--only", nargs="*", default=None,
                     help="generate only these fixtures (index_copy, attention, store, "
-                         "chunk_keys, allocator, c1, prologue, prefill)")
+                         "chunk_keys, allocator, c1, prologue, prefill, host_stream)")
     args = ap.parse_args()
     torch.manual_seed(0)
     ref = load_reference(args.ref)
@@ -329,6 +345,7 @@ def main() -> None:
         c1=lambda: gen_c1(ref),
         prologue=lambda: gen_prologue(ref),
         prefill=lambda: gen_prefill(ref),
+        host_stream=lambda: gen_host_stream(ref),
     )
     for name, gen in gens.items():
         if args.only is None or name in args.only:

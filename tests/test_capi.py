@@ -106,6 +106,23 @@ def test_host_validation_rejects_before_launch(lib: ctypes.CDLL) -> None:
     assert ec(None, fake, fake, 2, fake, fake, 4, None, 1, None, None) == _capi.PI_ERR_NULL_POINTER
     # arrival counters (4096 requests x 64 KV heads) + the grid-completion counter block
     assert lib.pi_paged_decode_attn_ws_zero_bytes() == 4096 * 64 * 4 + 256
+    # host-stream attention: dtype, head_dim, head ratio, span count, nothing to do, nulls
+    hs = lib.pi_host_stream_attn
+    sp = (_capi.KvSpan * 1)(_capi.KvSpan(fake, fake, 4, 512, 64, 1))
+    spp = ctypes.addressof(sp)
+    hargs = lambda q_len, hq, hkv, D, dt, n=1, spans=spp, out=fake: (  # noqa: E731
+        out, fake, hq * D, hq * D, spans, n, q_len, 0, 1, hq, hkv, D, 1.0, dt, None, 0, 0, None,
+        None)
+    assert hs(*hargs(1, 8, 2, 128, 7)) == _capi.PI_ERR_UNSUPPORTED
+    assert hs(*hargs(1, 8, 2, 12, _capi.PI_DTYPE_BF16)) == _capi.PI_ERR_UNSUPPORTED
+    assert hs(*hargs(1, 8, 2, 512, _capi.PI_DTYPE_BF16)) == _capi.PI_ERR_UNSUPPORTED
+    assert hs(*hargs(1, 6, 4, 128, _capi.PI_DTYPE_BF16)) == _capi.PI_ERR_BAD_SHAPE
+    assert hs(*hargs(1, 8, 2, 128, _capi.PI_DTYPE_BF16, n=_capi.HS_MAX_SPANS + 1)) == \
+        _capi.PI_ERR_UNSUPPORTED
+    assert hs(*hargs(0, 8, 2, 128, _capi.PI_DTYPE_F32)) == _capi.PI_OK
+    assert hs(*hargs(1, 8, 2, 128, _capi.PI_DTYPE_F32, spans=None)) == _capi.PI_ERR_NULL_POINTER
+    assert hs(*hargs(1, 8, 2, 128, _capi.PI_DTYPE_F32, out=None)) == _capi.PI_ERR_NULL_POINTER
+    assert ctypes.sizeof(_capi.KvSpan) == 48
 
 
 def test_kernels_refuse_cpu_tensors() -> None:

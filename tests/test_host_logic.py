@@ -141,11 +141,39 @@ def test_store_eviction_policy_matches_reference() -> None:
     assert freed == 4                      # one chunk = 2 layers x 2 pages
     assert store.gpu.allocator.used_pages == used - freed
     assert store.evict_chunks(need_pages=1) == 0  # no protected request -> no-op
-    # The reference leaves freed pages in the block table (kv_store.py:380-383), so
-    # a second eviction walks chunk 0 again and trips the double-free assertion;
-    # the reference raises the same AssertionError("page 0 not in use").
-    with pytest.raises(AssertionError, match="page 0 not in use"):
-        store.evict_chunks(need_pages=100, protected_request=cache)
+    # The reference leaves the freed pages in the block table (kv_store.py:380-383), so
+    # its second eviction walks chunk 0 again and trips the allocator's double-free
+    # assertion ("page 0 not in use"). Fixed: the evicted entries are -1 and the next
+    # call continues with chunk 1; the newest complete chunk (3) is still kept.
+    assert cache.evicted_chunks == 1
+    assert cache.get_block_table_for_layer(0)[:2] == [-1, -1]
+    assert cache.get_block_table_for_layer(1)[:2] == [-1, -1]
+    assert store.evict_chunks(need_pages=100, protected_request=cache) == 8
+    assert cache.evicted_chunks == 3
+    assert store.gpu.allocator.used_pages == used - 12
+    assert store.evict_chunks(need_pages=100, protected_request=cache) == 0
+    assert all(p >= 0 for p in cache.get_block_table_for_layer(0)[6:])
+    store.free_request(cache)              # frees only the pages still held
+    assert store.gpu.allocator.used_pages == 0
+
+
+def test_evicted_chunk_host_copies_are_held_while_the_request_lives() -> None:
+    # evicted chunks' host copies are the only copy left: the host LRU must skip them
+    store = _cpu_store()
+    cache = store.new_request()
+    cache.reserve_tokens(8 * 3)
+    cache.set_token_ids(list(range(24)))
+    k0 = cache.chunk_keys[0].full_key
+    store._host_cache[k0] = (None, None)  # as if sunk (the data move itself needs a GPU)
+    store._touch_host(k0)
+    store.evict_chunks(need_pages=1, protected_request=cache)
+    assert store._host_pins == {k0: 1}
+    assert store._evict_host_lru() is False    # the only cached chunk is held
+    assert k0 in store._host_cache
+    store.free_request(cache)
+    assert store._host_pins == {}
+    assert store._evict_host_lru() is True
+    assert k0 not in store._host_cache
 
 
 def test_data_moves_need_cuda() -> None:

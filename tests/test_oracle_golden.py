@@ -18,8 +18,8 @@ import pytest
 
 from oracle import paged_kv_oracle as orc
 from tests.golden.inputs import (
-    ATTENTION_CASES, PREFILL_CASES, PROLOGUE_CASES, attention_inputs, checksum, prefill_inputs,
-    prologue_inputs,
+    ATTENTION_CASES, HOST_STREAM_CASES, PREFILL_CASES, PROLOGUE_CASES, attention_inputs, checksum,
+    host_stream_inputs, prefill_inputs, prologue_inputs,
 )
 
 GOLD = pathlib.Path(__file__).resolve().parent / "golden"
@@ -160,3 +160,27 @@ def test_prefill_matches_reference(case: dict) -> None:
     out = orc.paged_attention_prefill(x["q"], k, v, list(table), case["kv_len"], case["q_start"],
                                       case["causal"], case["S"])
     np.testing.assert_allclose(out, g[n + "__out"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("case", HOST_STREAM_CASES, ids=[c["name"] for c in HOST_STREAM_CASES])
+def test_host_stream_matches_reference(case: dict) -> None:
+    # host_stream_attention_v1 run by the reference on the same chunks (CPU fp32)
+    g = np.load(GOLD / "host_stream.npz")
+    n = case["name"]
+    x = host_stream_inputs(case)
+    assert checksum(x["q"], x["k_full"], x["v_full"]) == pytest.approx(
+        float(g[n + "__checksum"]), rel=1e-12)
+    out = orc.host_stream_attention(x["q"], x["chunks"], x["rk"], x["rv"], case["q_start"],
+                                    case["causal"])
+    np.testing.assert_allclose(out, g[n + "__out"], rtol=1e-5, atol=1e-6)
+
+
+def test_host_stream_oracle_is_contiguous_attention() -> None:
+    # the chunk split is invisible: one contiguous span gives the same rows
+    case = HOST_STREAM_CASES[4]
+    x = host_stream_inputs(case)
+    whole = orc.host_stream_attention(x["q"], [], x["k_full"], x["v_full"], case["q_start"],
+                                      case["causal"])
+    split = orc.host_stream_attention(x["q"], x["chunks"], x["rk"], x["rv"], case["q_start"],
+                                      case["causal"])
+    np.testing.assert_allclose(split, whole, rtol=1e-6, atol=1e-7)
