@@ -517,6 +517,81 @@ def bench_prefill(dev: torch.device, peaks: dict) -> dict:
     return res
 
 
+def bench_host_stream(dev: torch.device) -> dict:
+    """Host-stream decode attention at the C5 shape: 8 requests x 32768
+    tokens, Qwen3-8B heads (32 q / 8 KV, head_dim 128), bf16. Each request's first 75% of
+    tokens sit in pinned host chunks of 256 tokens ([H_kv, T, D], the KV store's chunk
+    layout), the last 25% on the device. One step = one layer's decode attention of all
+    8 requests.
+
+    Ours reads the host chunks in place (pi_host_stream_attn). The reference's algorithm
+    (host_stream_attention_v1: concatenate chunks + tail, repeat_interleave, SDPA) needs
+    the chunks on the device first; it is timed with that host->device copy included
+    (pinned, one cudaMemcpyAsync per chunk), on the same GPU. The bound is the host link:
+    achieved = host bytes / time, against a pinned 1 GiB host->device copy measured here.
+    """
+    import torch.nn.functional as F
+
+    from plastic_infer_b200 import kernels
+
+    B, kv, Hq, Hkv, D, C = 8, 32768, 32, 8, 128, 256
+    host_tok = kv * 3 // 4
+    n_chunks = host_tok // C
+    g = torch.Generator().manual_seed(51)
+    h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    d.copy_(h)
+    torch.cuda.synchronize()
+    link = (1 << 30) / (time_region(lambda: d.copy_(h, non_blocking=True), 3,
+                                    torch.cuda.current_stream()) / 3 * 1e-3) / 1e9
+    del h, d
+    reqs = []
+    for _ in range(B):
+        kh = torch.randn((n_chunks, Hkv, C, D), generator=g).to(torch.bfloat16).pin_memory()
+        vh = torch.randn((n_chunks, Hkv, C, D), generator=g).to(torch.bfloat16).pin_memory()
+        kt = torch.randn((kv - host_tok, Hkv, D), device=dev, dtype=torch.bfloat16)
+        vt = torch.randn((kv - host_tok, Hkv, D), device=dev, dtype=torch.bfloat16)
+        q = torch.randn((1, Hq, D), device=dev, dtype=torch.bfloat16)
+        spans = [(kh[i], vh[i]) for i in range(n_chunks)] + [(kt.permute(1, 0, 2), vt.permute(1, 0, 2))]
+        reqs.append((kh, vh, kt, vt, q, spans))
+    host_bytes = B * 2 * host_tok * Hkv * D * 2
+    dev_bytes = B * 2 * (kv - host_tok) * Hkv * D * 2
+    out = torch.empty((B, 1, Hq, D), device=dev, dtype=torch.bfloat16)
+
+    def ours():
+        for i, (_, _, _, _, q, spans) in enumerate(reqs):
+            kernels.host_stream_attention(q, spans, q_start=kv - 1, out=out[i])
+
+    stage_k = torch.empty((n_chunks, Hkv, C, D), device=dev, dtype=torch.bfloat16)
+    stage_v = torch.empty_like(stage_k)
+
+    def reference():
+        for i, (kh, vh, kt, vt, q, _) in enumerate(reqs):
+            for c in range(n_chunks):
+                stage_k[c].copy_(kh[c], non_blocking=True)
+                stage_v[c].copy_(vh[c], non_blocking=True)
+            k = torch.cat([stage_k.permute(0, 2, 1, 3).reshape(-1, Hkv, D), kt])   # [kv, H, D]
+            v = torch.cat([stage_v.permute(0, 2, 1, 3).reshape(-1, Hkv, D), vt])
+            kt_ = k.transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)[None]
+            vt_ = v.transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)[None]
+            out[i] = F.scaled_dot_product_attention(q.transpose(0, 1)[None], kt_, vt_)[0].transpose(0, 1)
+
+    res = dict(workload=f"C5 host-stream decode: {B} requests x {kv} tokens, {n_chunks} pinned "
+                        f"host chunks of {C} tokens + {kv - host_tok}-token device tail per request, "
+                        f"{Hq}q/{Hkv}kv heads, head_dim {D}, bf16; one layer",
+               host_gb=round(host_bytes / 1e9, 3), device_gb=round(dev_bytes / 1e9, 3),
+               link_gbs=round(link, 1))
+    for label, fn in (("ours", ours), ("reference_algorithm", reference)):
+        fn()
+        torch.cuda.synchronize()
+        reps = 3
+        us = time_region(fn, reps, torch.cuda.current_stream()) / reps * 1e3
+        res[label] = dict(us_per_layer=round(us, 1), host_gbs=round(host_bytes / (us * 1e-6) / 1e9, 1),
+                          frac_of_link=round(host_bytes / (us * 1e-6) / 1e9 / link, 3))
+    res["speedup"] = round(res["reference_algorithm"]["us_per_layer"] / res["ours"]["us_per_layer"], 2)
+    return res
+
+
 class CpuSample:
     """The C3 KV path of `requests` requests on the CPU (the oracle, a numpy port of the
     reference's _write_kv_layer + paged_attention_v1), built once and run per layer.
@@ -811,6 +886,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if args.c2_only:
         run_c2_only(args, dev)
         return
+    if args.host_stream_only:
+        print(json.dumps(dict(host_stream=bench_host_stream(dev))), flush=True)
+        return
     if args.prefill_only:
         print(json.dumps(dict(prefill=bench_prefill(dev, measured_peaks()))), flush=True)
         return
@@ -1092,6 +1170,8 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="ncu mode: warm-up + timed steps as plain launches, no extra parts")
     ap.add_argument("--c2-only", action="store_true", help="run only the C2 index-copy microbench")
+    ap.add_argument("--host-stream-only", action="store_true",
+                    help="print only the host-stream attention microbench (C5 shape)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the paged prefill attention microbench")
     ap.add_argument("--expert-copy-only", action="store_true",
