@@ -134,3 +134,12 @@ def test_kernels_refuse_cpu_tensors() -> None:
     new = torch.zeros(1, 2, 64, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         kernels.kv_index_copy(pool, pool, new, new, torch.zeros(1, dtype=torch.int64))
+    # host-stream attention: the query must be on the GPU (host chunks may not be)
+    from plastic_infer_b200.exec.attention import host_stream_attention_v1
+
+    q = torch.zeros(1, 1, 4, 64)
+    chunk = (torch.zeros(2, 64, 8), torch.zeros(2, 64, 8))
+    with pytest.raises(ValueError, match="CUDA"):
+        kernels.host_stream_attention(q[0], [(chunk[0].permute(0, 2, 1), chunk[1].permute(0, 2, 1))])
+    with pytest.raises(ValueError, match="CUDA"):
+        host_stream_attention_v1(q, [chunk], torch.zeros(1, 0, 2, 64), torch.zeros(1, 0, 2, 64))

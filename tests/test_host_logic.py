@@ -186,3 +186,15 @@ def test_data_moves_need_cuda() -> None:
     cache.set_token_ids(list(range(8)))
     with pytest.raises(RuntimeError):
         store.sink_completed_chunks(cache)
+
+
+def test_streaming_an_unsunk_evicted_chunk_raises() -> None:
+    # the reference frees a chunk whether or not it was sunk; its K/V are then gone, and
+    # attending the request from the host store must say so instead of reading nothing
+    store = _cpu_store()
+    cache = store.new_request()
+    cache.reserve_tokens(8 * 3)
+    cache.set_token_ids(list(range(24)))
+    assert store.evict_chunks(need_pages=1, protected_request=cache) == 4
+    with pytest.raises(RuntimeError, match="without a host copy"):
+        store.host_stream_chunks(cache, 0)
