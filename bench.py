@@ -640,7 +640,8 @@ class CpuSample:
         scale = (self.ctx.sum() / self.sub.sum()) * (cfg["layers"] / layers)
         step_s = dt * scale
         return dict(value=round(cfg["batch"] / step_s, 3), unit="tok/s",
-                    cores=_blas_threads(), kind="port",
+                    cores=_blas_threads(), host_cpus=os.cpu_count(), cpu_model=_cpu_model(),
+                    kind="port",
                     sample=f"{layers} layer(s) x {len(self.sub)} of {cfg['batch']} requests "
                            f"({int(self.sub.sum())} of {int(self.ctx.sum())} context tokens per "
                            f"layer), fp32 numpy oracle, scaled x{scale:.2f} to one "
@@ -650,6 +651,18 @@ class CpuSample:
 def cpu_baseline_sample(cfg: dict, target_s: float = 12.0) -> dict:
     """Oracle on a bounded sample (all requests, ~target_s of CPU work), scaled to a step."""
     return CpuSample(cfg).measure(target_s)
+
+
+def _cpu_model() -> str:
+    """The host CPU's model name (Linux /proc/cpuinfo), or "unknown"."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def _blas_threads() -> int:
