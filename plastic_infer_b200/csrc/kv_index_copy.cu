@@ -84,16 +84,17 @@ __global__ void __launch_bounds__(256) kv_index_copy_kernel(
     const int64_t next_slot = tn < n_tokens ? __ldg(slot_mapping + tn) : -1;
     const int64_t s = slot;
     slot = next_slot;
-    if (s < 0) continue;  // padding
-    if (s >= num_slots) {
-      if (lane == 0) record_error(err, PI_ERR_SLOT_RANGE);
-      continue;
-    }
-    const int64_t page = s / page_size;
-    const int64_t off = s - page * page_size;
-    const int64_t dst_base = page * page_stride + off * row_bytes;
+    // The source rows do not depend on the slot, so their loads go out before the slot
+    // is examined and its round trip overlaps them (rows of a padding token exist too;
+    // their loads are simply not stored). Only the store address waits for the slot.
+    const bool store = s >= 0 && s < num_slots;
     const char* ks = k_new + t * src_token_stride_bytes;
     const char* vs = v_new + t * src_token_stride_bytes;
+    // destination of this token's row group (valid only when `store`)
+    auto dst_base = [&]() {
+      const int64_t page = s / page_size;
+      return page * page_stride + (s - page * page_size) * row_bytes;
+    };
 
     if constexpr (kFixedLanes) {
       // 32 % vec_per_row == 0: lane `lane` always copies vector w of rows r0, r0 +
@@ -111,49 +112,53 @@ __global__ void __launch_bounds__(256) kv_index_copy_kernel(
             vals[j] = load_stream<VEC>((is_v ? vs : ks) + static_cast<int64_t>(h) * row_bytes + w0);
           }
         }
+        if (!store) break;
+        const int64_t db = dst_base();
 #pragma unroll
         for (int j = 0; j < kMaxRows; ++j) {
           const int r = rbase + r0 + j * rows_per_pass;
           if (r < 2 * kv_heads) {
             const bool is_v = r >= kv_heads;
             const int h = is_v ? r - kv_heads : r;
-            *reinterpret_cast<V*>((is_v ? v_pool : k_pool) + dst_base + h * head_stride + w0) =
-                vals[j];
+            *reinterpret_cast<V*>((is_v ? v_pool : k_pool) + db + h * head_stride + w0) = vals[j];
           }
         }
       }
-      continue;
-    }
-
-    // General shapes: all loads of a batch of kPerLane vectors per lane are issued
-    // before any store, so a warp keeps up to 32 * kPerLane * VEC bytes in flight.
-    for (int base = 0; base < total; base += 32 * kPerLane) {
-      V vals[kPerLane];
+    } else {
+      // General shapes: all loads of a batch of kPerLane vectors per lane are issued
+      // before any store, so a warp keeps up to 32 * kPerLane * VEC bytes in flight.
+      for (int base = 0; base < total; base += 32 * kPerLane) {
+        V vals[kPerLane];
 #pragma unroll
-      for (int j = 0; j < kPerLane; ++j) {
-        const int c = base + j * 32 + lane;
-        if (c < total) {
-          const bool is_v = c >= vec_per_tensor;
-          const int cc = is_v ? c - vec_per_tensor : c;
-          const int h = cc / vec_per_row;
-          const int w = cc - h * vec_per_row;
-          vals[j] = load_stream<VEC>((is_v ? vs : ks) + static_cast<int64_t>(h) * row_bytes +
-                                     static_cast<int64_t>(w) * VEC);
+        for (int j = 0; j < kPerLane; ++j) {
+          const int c = base + j * 32 + lane;
+          if (c < total) {
+            const bool is_v = c >= vec_per_tensor;
+            const int cc = is_v ? c - vec_per_tensor : c;
+            const int h = cc / vec_per_row;
+            const int w = cc - h * vec_per_row;
+            vals[j] = load_stream<VEC>((is_v ? vs : ks) + static_cast<int64_t>(h) * row_bytes +
+                                       static_cast<int64_t>(w) * VEC);
+          }
+        }
+        if (!store) break;
+        const int64_t db = dst_base();
+#pragma unroll
+        for (int j = 0; j < kPerLane; ++j) {
+          const int c = base + j * 32 + lane;
+          if (c < total) {
+            const bool is_v = c >= vec_per_tensor;
+            const int cc = is_v ? c - vec_per_tensor : c;
+            const int h = cc / vec_per_row;
+            const int w = cc - h * vec_per_row;
+            *reinterpret_cast<V*>((is_v ? v_pool : k_pool) + db + h * head_stride +
+                                  static_cast<int64_t>(w) * VEC) = vals[j];
+          }
         }
       }
-#pragma unroll
-      for (int j = 0; j < kPerLane; ++j) {
-        const int c = base + j * 32 + lane;
-        if (c < total) {
-          const bool is_v = c >= vec_per_tensor;
-          const int cc = is_v ? c - vec_per_tensor : c;
-          const int h = cc / vec_per_row;
-          const int w = cc - h * vec_per_row;
-          *reinterpret_cast<V*>((is_v ? v_pool : k_pool) + dst_base + h * head_stride +
-                                static_cast<int64_t>(w) * VEC) = vals[j];
-        }
-      }
     }
+    // a negative slot is padding; one past the pool is an error (the write is skipped)
+    if (s >= num_slots && lane == 0) record_error(err, PI_ERR_SLOT_RANGE);
   }
 }
 
