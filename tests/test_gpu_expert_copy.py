@@ -1,4 +1,4 @@
-"""GPU parity of the MoE expert-slot copy (pi_expert_slot_copy, SURVEY row f4).
+"""GPU parity of the MoE expert-slot copy (pi_expert_slot_copy).
 
 Rows move from pinned host banks (read through their device alias) into device slot
 caches, for every bank in one launch. The result must equal, byte for byte:

@@ -1,4 +1,4 @@
-"""GPU parity of host-stream attention (pi_host_stream_attn, SURVEY row f2).
+"""GPU parity of host-stream attention (pi_host_stream_attn).
 
 One request attends over host chunks read in place (page-locked) plus a device tail,
 in one pass: the reference's host_stream_attention_v1 (src/plastic_infer/exec/

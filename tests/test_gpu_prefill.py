@@ -1,4 +1,4 @@
-"""GPU parity of paged prefill attention (pi_paged_prefill_attn, SURVEY row f3).
+"""GPU parity of paged prefill attention (pi_paged_prefill_attn).
 
 One request's q_len new tokens attend, straight from the page pool, to the first kv_len
 tokens of their pages: causally from position q_start (the reference's is_causal path

@@ -1,4 +1,4 @@
-"""GPU parity of the fused decode prologue (pi_decode_prologue, SURVEY row f1).
+"""GPU parity of the fused decode prologue (pi_decode_prologue).
 
 One launch applies QK-norm (optional) and RoPE to the step's q and k rows and writes the
 new K/V rows at their slots. Checked against:
