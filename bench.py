@@ -1200,7 +1200,7 @@ def main() -> None:
                          "then computes its work split only after the previous kernel ends)")
     ap.add_argument("--fused", action="store_true",
                     help="one fused append+attention launch per layer instead of index-copy "
-                         "then attention (measured slower today: 202.9 vs 197.5 us per layer)")
+                         "then attention (measured slower: 202.9 vs 197.5 us per layer, 4-stage ring)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
