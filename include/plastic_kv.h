@@ -78,6 +78,24 @@ int pi_abi_version(void);
  */
 int pi_set_programmatic_launch(int enable);
 
+/*
+ * Page-ring depth of plain pi_paged_decode_attn launches (no reference counterpart).
+ * The TMA kernel keeps a ring of page stages per warp. By default (AUTO) a launch
+ * whose bound on the work (batch x bt_stride x num_kv_heads) is large uses a
+ * two-stage ring with two CTAs per SM, and every other launch a deep ring (4
+ * stages at head_dim <= 128) with one CTA per SM. DEEP and SHALLOW force one of the
+ * two for every plain launch the fast path takes (SHALLOW only where two CTAs fit on
+ * an SM), so either instance can be run and checked at any size. Results agree
+ * within the attention tolerance; they are not bit-identical because the work split
+ * differs. Launches with the fused append or the peer all-gather always use the deep
+ * ring. Applies to launches made after the call, in every thread. Returns PI_OK, or
+ * PI_ERR_BAD_SHAPE for an unknown mode.
+ */
+#define PI_ATTN_RING_AUTO 0
+#define PI_ATTN_RING_DEEP 1
+#define PI_ATTN_RING_SHALLOW 2
+int pi_set_decode_attn_ring(int mode);
+
 /* Static description of a status code. Never NULL. */
 const char* pi_error_string(int code);
 
@@ -86,6 +104,13 @@ const char* pi_error_string(int code);
  *   k_pool[s / page_size, h, s % page_size, :] = k_new[i, h, :]   (all h)
  *   v_pool[...]                                = v_new[i, h, :]
  * A negative slot is padding and is skipped. Bit-exact element copy.
+ *
+ * Duplicate slots: when two tokens of one launch name the same non-negative slot,
+ * every 16-byte piece of that slot's rows ends up holding the bytes of one of them,
+ * but which one is unspecified (and may differ from piece to piece). The
+ * reference's per-token loop keeps the last token's row; a caller that relies on
+ * that must not pass duplicates in one launch (split the batch, or drop all but the
+ * last occurrence). Slots that differ never interfere.
  *
  * Replaces the per-token Python loop of _write_kv_layer
  * (src/plastic_infer/exec/runner_paged.py:123-129) and the per-layer write of
@@ -115,6 +140,17 @@ int pi_kv_index_copy(void* k_pool, void* v_pool, const void* k_new, const void* 
 size_t pi_paged_decode_attn_workspace_bytes(int batch, int num_q_heads, int num_kv_heads,
                                             int head_dim);
 size_t pi_paged_decode_attn_ws_zero_bytes(void);
+
+/*
+ * Page-ring stages a plain pi_paged_decode_attn launch of this shape would use on
+ * the current device under the current pi_set_decode_attn_ring mode (no reference
+ * counterpart): 2 for the shallow ring with two CTAs per SM, the deep ring's depth
+ * otherwise, or 0 when the shape takes the generic SIMT path. Pointer alignment is
+ * not considered (misaligned pools or q also send a launch to the SIMT path).
+ */
+int pi_paged_decode_attn_ring_stages(int batch, int64_t bt_stride, int num_q_heads,
+                                     int num_kv_heads, int head_dim, int page_size,
+                                     int64_t num_pages, int dtype);
 
 /*
  * Batched paged GQA decode attention, one query token per request:
@@ -233,9 +269,12 @@ int pi_paged_decode_attn_gather(void* out, const void* q, const void* k_pool, co
  * the process exits. The function calls no cudaMalloc / cudaFree and no
  * allocating library routine.
  *
- *   - A request whose scratch need (pi_paged_decode_attn_workspace_bytes) exceeds
- *     PI_NOALLOC_SCRATCH_BYTES is rejected with PI_ERR_SCRATCH_LIMIT before any
- *     launch (e.g. head_dim 256, or head_dim 128 on a GPU with more than 148 SMs).
+ *   - A request that takes the TMA fast path and whose scratch need
+ *     (pi_paged_decode_attn_workspace_bytes) exceeds PI_NOALLOC_SCRATCH_BYTES is
+ *     rejected with PI_ERR_SCRATCH_LIMIT before any launch (e.g. head_dim 256, or
+ *     head_dim 128 on a GPU with more than 148 SMs). Shapes served by the generic
+ *     SIMT path (fp32 pools, other head_dim or page sizes, G > 8) use no scratch and
+ *     are never rejected for it.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current and caches it; make that
  *     first call before any stream capture on the device.

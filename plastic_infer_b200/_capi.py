@@ -30,6 +30,10 @@ PI_ERR_TIMEOUT = 9
 PI_ERR_SCRATCH_LIMIT = 10
 NOALLOC_SCRATCH_BYTES = 12 << 20  # PI_NOALLOC_SCRATCH_BYTES in include/plastic_kv.h
 
+PI_ATTN_RING_AUTO = 0
+PI_ATTN_RING_DEEP = 1
+PI_ATTN_RING_SHALLOW = 2
+
 PI_DTYPE_F32 = 0
 PI_DTYPE_BF16 = 1
 PI_DTYPE_F16 = 2
@@ -45,6 +49,7 @@ _f32 = ctypes.c_float
 # name -> (restype, argtypes); the one table of what the header declares.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pi_set_programmatic_launch": (_i32, [_i32]),
+    "pi_set_decode_attn_ring": (_i32, [_i32]),
     "pi_abi_version": (_i32, []),
     "pi_error_string": (ctypes.c_char_p, [_i32]),
     "pi_kv_index_copy": (
@@ -53,6 +58,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "pi_paged_decode_attn_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32]),
     "pi_paged_decode_attn_ws_zero_bytes": (_sz, []),
+    # batch, bt_stride, hq, hkv, head_dim, page_size, num_pages, dtype
+    "pi_paged_decode_attn_ring_stages": (_i32, [_i32, _i64, _i32, _i32, _i32, _i32, _i64, _i32]),
     "pi_paged_decode_attn": (
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,

@@ -21,9 +21,12 @@ int device_sm_count() {
 
 namespace {
 std::atomic<int> g_programmatic{0};
+std::atomic<int> g_attn_ring{PI_ATTN_RING_AUTO};
 }  // namespace
 
 bool programmatic_launch() { return g_programmatic.load(std::memory_order_relaxed) != 0; }
+
+int decode_attn_ring() { return g_attn_ring.load(std::memory_order_relaxed); }
 
 }  // namespace pi
 
@@ -31,6 +34,13 @@ extern "C" int pi_abi_version(void) { return 3; }
 
 extern "C" int pi_set_programmatic_launch(int enable) {
   pi::g_programmatic.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return PI_OK;
+}
+
+extern "C" int pi_set_decode_attn_ring(int mode) {
+  if (mode != PI_ATTN_RING_AUTO && mode != PI_ATTN_RING_DEEP && mode != PI_ATTN_RING_SHALLOW)
+    return PI_ERR_BAD_SHAPE;
+  pi::g_attn_ring.store(mode, std::memory_order_relaxed);
   return PI_OK;
 }
 

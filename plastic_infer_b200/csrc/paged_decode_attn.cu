@@ -1168,19 +1168,46 @@ int launch_fast_ns(const FastParams& fp, const void* k_pool, const void* v_pool,
 // segment into twice the pieces, and on a 1-KV-head shard the extra merges cost 10-15%.
 // The host bounds the work by batch x block-table width x KV heads (the context lengths
 // are on the device); 150 pages per warp at 8 warps per SM separates the two regimes.
+// pi_set_decode_attn_ring overrides the choice for plain launches.
+template <int D, int S>
+int ring_stages(int batch, int64_t bt_stride, int hkv, bool plain) {
+  constexpr int NS = stages_for<D, S>();
+  if constexpr (2 * fast_smem_bytes<D, S, 2>() <= 227 * 1024 && NS > 2) {
+    const double pages_bound = static_cast<double>(batch) * static_cast<double>(bt_stride) *
+                               static_cast<double>(hkv);
+    const double warps2 = static_cast<double>(device_sm_count()) * 2 * kWarps;
+    const int ring = decode_attn_ring();
+    const bool shallow = ring == PI_ATTN_RING_SHALLOW ||
+                         (ring == PI_ATTN_RING_AUTO && pages_bound >= 150.0 * warps2);
+    if (plain && shallow) return 2;
+  }
+  return NS;
+}
+
 template <typename T, int D, int S>
 int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, int64_t rows,
                 int dtype, cudaStream_t stream) {
   constexpr int NS = stages_for<D, S>();
-  if constexpr (2 * fast_smem_bytes<D, S, 2>() <= 227 * 1024 && NS > 2) {
-    const bool plain = fp.slot_mapping == nullptr && fp.ag.world == 0;
-    const double pages_bound = static_cast<double>(fp.batch) * static_cast<double>(fp.bt_stride) *
-                               static_cast<double>(fp.hkv);
-    const double warps2 = static_cast<double>(device_sm_count()) * 2 * kWarps;
-    if (plain && pages_bound >= 150.0 * warps2)
+  const bool plain = fp.slot_mapping == nullptr && fp.ag.world == 0;
+  if constexpr (NS > 2) {
+    if (ring_stages<D, S>(fp.batch, fp.bt_stride, fp.hkv, plain) == 2)
       return launch_fast_ns<T, D, S, 2>(fp, k_pool, v_pool, rows, dtype, stream);
   }
   return launch_fast_ns<T, D, S, NS>(fp, k_pool, v_pool, rows, dtype, stream);
+}
+
+// Whether a launch of this shape takes the TMA fast path, pointer alignment aside (the
+// dispatcher also needs 16-byte pools and 4-byte q; otherwise it runs the SIMT path).
+bool fast_shape(int dtype, int batch, int64_t bt_stride, int num_q_heads, int num_kv_heads,
+                int head_dim, int page_size, int64_t num_pages) {
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0) return false;
+  const int group = num_q_heads / num_kv_heads;
+  const int64_t rows = num_pages * num_kv_heads * page_size;
+  const bool half_type = dtype == PI_DTYPE_BF16 || dtype == PI_DTYPE_F16;
+  return half_type && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
+         (page_size == 16 || page_size == 32) && group <= kHeadsPad && batch <= kMaxBatch &&
+         num_kv_heads <= kMaxKvHeads && rows > 0 && rows < (int64_t{1} << 31) &&
+         static_cast<int64_t>(batch) * bt_stride < (int64_t{1} << 31);
 }
 
 }  // namespace attn
@@ -1229,11 +1256,8 @@ int attn_dispatch(void* out, const void* q, const void* k_pool, const void* v_po
   const float scale_log2 = scale * 1.4426950408889634f;
   const int64_t rows = num_pages * num_kv_heads * page_size;
 
-  const bool half_type = dtype == PI_DTYPE_BF16 || dtype == PI_DTYPE_F16;
-  const bool fast = half_type && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
-                    (page_size == 16 || page_size == 32) && group <= kHeadsPad &&
-                    batch <= kMaxBatch && num_kv_heads <= kMaxKvHeads && rows > 0 && rows < (int64_t{1} << 31) &&
-                    static_cast<int64_t>(batch) * bt_stride < (int64_t{1} << 31) &&
+  const bool fast = fast_shape(dtype, batch, bt_stride, num_q_heads, num_kv_heads, head_dim,
+                               page_size, num_pages) &&
                     aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(q, 4) &&
                     q_stride % 2 == 0 && aligned(out, 2);
   if (ag != nullptr) {
@@ -1353,6 +1377,26 @@ int attn_dispatch(void* out, const void* q, const void* k_pool, const void* v_po
 }  // namespace attn
 }  // namespace pi
 
+extern "C" int pi_paged_decode_attn_ring_stages(int batch, int64_t bt_stride, int num_q_heads,
+                                                int num_kv_heads, int head_dim, int page_size,
+                                                int64_t num_pages, int dtype) {
+  using namespace pi::attn;
+  if (batch <= 0 || bt_stride < 0 || num_pages < 0 ||
+      !fast_shape(dtype, batch, bt_stride, num_q_heads, num_kv_heads, head_dim, page_size,
+                  num_pages))
+    return 0;
+#define PI_RING(D, S) \
+  if (head_dim == D && page_size == S) return ring_stages<D, S>(batch, bt_stride, num_kv_heads, true);
+  PI_RING(64, 16)
+  PI_RING(128, 16)
+  PI_RING(256, 16)
+  PI_RING(64, 32)
+  PI_RING(128, 32)
+  PI_RING(256, 32)
+#undef PI_RING
+  return 0;
+}
+
 extern "C" int pi_paged_decode_attn(void* out, const void* q, const void* k_pool,
                                     const void* v_pool, const int32_t* block_tables,
                                     int64_t bt_stride, const int32_t* ctx_lens, int batch,
@@ -1433,8 +1477,10 @@ int static_scratch_address(void** out) {
   std::lock_guard<std::mutex> lock(mu);
   if (cached[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess || p == nullptr)
+    if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();  // do not leave the failure for a later launch check
       return PI_ERR_CUDA;
+    }
     cached[dev] = p;
   }
   *out = cached[dev];
@@ -1455,6 +1501,14 @@ extern "C" int pi_paged_decode_attn_noalloc(void* out, const void* q, const void
   using namespace pi::attn;
   if (batch <= 0 || num_kv_heads <= 0 || head_dim <= 0) {
     // Nothing that needs scratch; let the regular entry point validate and return.
+    return pi_paged_decode_attn(out, q, k_pool, v_pool, block_tables, bt_stride, ctx_lens, batch,
+                                num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
+                                dtype, q_stride, out_stride, nullptr, 0, err, stream);
+  }
+  if (!fast_shape(dtype, batch, bt_stride, num_q_heads, num_kv_heads, head_dim, page_size,
+                  num_pages)) {
+    // The generic SIMT path (fp32 pools, other head_dim or page sizes, G > 8, ...)
+    // uses no scratch at all: no limit applies.
     return pi_paged_decode_attn(out, q, k_pool, v_pool, block_tables, bt_stride, ctx_lens, batch,
                                 num_q_heads, num_kv_heads, head_dim, page_size, num_pages, scale,
                                 dtype, q_stride, out_stride, nullptr, 0, err, stream);

@@ -52,6 +52,9 @@ __device__ __forceinline__ void pdl_trigger() {
 // Whether launches carry the programmatic attribute (process-wide switch).
 bool programmatic_launch();
 
+// Page-ring depth of plain decode-attention launches (pi_set_decode_attn_ring).
+int decode_attn_ring();
+
 // Launch `kern` on `stream`, with the programmatic attribute when it is switched on.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,

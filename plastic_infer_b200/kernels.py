@@ -27,6 +27,8 @@ These are the batched additions behind the reference's single-request API:
   set_programmatic_launch
                          programmatic dependent launch for the index-copy, prologue and
                          attention kernels
+  set_decode_attn_ring   page-ring depth of plain attention launches (automatic, deep or
+                         shallow), so either kernel instance can be run at any size
 
 Pools are the *physical* tensors [num_pages, kv_heads, page_size, head_dim]. Every
 function launches on torch's current stream, as the reference's ctypes launch does
@@ -319,6 +321,35 @@ def set_programmatic_launch(enable: bool) -> None:
     block_tables. Off by default.
     """
     _capi.call("pi_set_programmatic_launch", 1 if enable else 0)
+
+
+_RING_MODES = {"auto": _capi.PI_ATTN_RING_AUTO, "deep": _capi.PI_ATTN_RING_DEEP,
+               "shallow": _capi.PI_ATTN_RING_SHALLOW}
+
+
+def set_decode_attn_ring(mode: str) -> None:
+    """Page-ring depth of every later plain paged_decode_attention launch.
+
+    "auto" (the default) picks per launch: a two-stage ring with two CTAs per SM when
+    batch x block-table width x KV heads is large, else a deep ring (4 stages at
+    head_dim <= 128) with one CTA per SM. "deep" and "shallow" force one of them
+    (shallow only where two CTAs fit on an SM). Launches with the fused append or the
+    peer all-gather always use the deep ring.
+    """
+    try:
+        code = _RING_MODES[mode]
+    except KeyError:
+        raise ValueError(f"ring mode must be one of {sorted(_RING_MODES)}, got {mode!r}")
+    _capi.call("pi_set_decode_attn_ring", code)
+
+
+def decode_attn_ring_stages(batch: int, bt_stride: int, num_q_heads: int, num_kv_heads: int,
+                            head_dim: int, page_size: int, num_pages: int,
+                            dtype: torch.dtype) -> int:
+    """Ring stages a plain attention launch of this shape would use now (0: SIMT path)."""
+    return int(_capi.load().pi_paged_decode_attn_ring_stages(
+        batch, bt_stride, num_q_heads, num_kv_heads, head_dim, page_size, num_pages,
+        dtype_code(dtype)))
 
 
 def workspace_bytes(batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int) -> int:

@@ -69,4 +69,32 @@ def assert_close(out: np.ndarray, ref: np.ndarray, atol: float, rtol: float) -> 
 
 
 __all__ = ["assert_close", "bf16_bits_to_f32", "from_bits", "host_tensor", "logical_f32",
+           "oracle_decode_by_request",
            "logical_np", "physical_from_logical", "to_bits", "torch_dtype"]
+
+
+def oracle_decode_by_request(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                             tables: list[list[int]], ctx: list[int], page_size: int,
+                             requests: list[int] | None = None) -> np.ndarray:
+    """Oracle decode attention, one request at a time, reading only that request's pages.
+
+    Physical device pools [P, H, S, D] of any size (a full 8B-shape layer is ~0.6 GB per
+    pool): each request's pages are gathered on the device and widened to fp32 on the
+    host, so host memory stays at one request's context. Returns [len(requests), Hq, D].
+    """
+    from oracle import paged_kv_oracle as orc
+
+    reqs = list(range(len(ctx))) if requests is None else list(requests)
+    qf = q.float().cpu().numpy()
+    out = np.zeros((len(reqs), q.shape[1], q.shape[2]), dtype=np.float32)
+    for i, b in enumerate(reqs):
+        n = int(ctx[b])
+        if n <= 0:
+            continue
+        npg = -(-n // page_size)
+        ids = torch.tensor(tables[b][:npg], dtype=torch.int64, device=k_pool.device)
+        kb = logical_f32(k_pool.index_select(0, ids))
+        vb = logical_f32(v_pool.index_select(0, ids))
+        out[i] = orc.paged_attention_decode(qf[b:b + 1], kb, vb, [list(range(npg))], [n],
+                                            page_size)[0]
+    return out

@@ -1,0 +1,133 @@
+"""GPU parity of both page-ring instances of the TMA decode attention (row a2).
+
+The fast path has two instances per head shape: a deep ring (4 stages per warp at
+head_dim <= 128, one CTA per SM) and a shallow ring (2 stages, two CTAs per SM, whose
+split-KV merge stages its partial records through the smaller ring in different
+batches). By default a plain launch picks the shallow ring when batch x block-table
+width x KV heads is large, which is the case for the 8B-shape decode batch the
+benchmark times (64 requests, contexts uniform in [512, 8192]). These tests run that
+exact batch through the automatic choice and through each forced instance, a
+1-KV-head shard (one rank's share at 8 GPUs) above the shallow threshold, and every
+random configuration of the attention suite under both forced instances, all against
+the oracle at the north-star tolerance (max-abs 2e-2 + rel 1e-2, fp32 reference
+arithmetic on the same bf16 inputs).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from plastic_infer_b200 import kernels
+from tests._helpers import assert_close, oracle_decode_by_request
+from tests.test_gpu_attention import CONFIGS, _oracle, _random_batch, _run
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+ATOL, RTOL = 2e-2, 1e-2
+S, D = 16, 128
+
+
+@pytest.fixture(autouse=True)
+def _automatic_ring_afterwards():
+    yield
+    kernels.set_decode_attn_ring("auto")
+
+
+def c3_contexts() -> list[int]:
+    """The 8B-shape decode batch: 64 contexts uniform in [512, 8192], seed 0."""
+    return [int(c) for c in np.random.default_rng(0).integers(512, 8192 + 1, size=64)]
+
+
+def c3_layer(hq: int, hkv: int, width: int | None = None, seed: int = 1):
+    """One layer of the 8B-shape batch: random non-contiguous pages, N(0,1) bf16 data."""
+    ctx = c3_contexts()
+    npg = [-(-c // S) for c in ctx]
+    P = sum(npg) + 3
+    perm = np.random.default_rng(seed).permutation(P).astype(np.int32)
+    tables, cur = [], 0
+    for n in npg:
+        tables.append([int(x) for x in perm[cur:cur + n]])
+        cur += n
+    w = width or max(npg)
+    bt = torch.zeros((len(ctx), w), dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    g = torch.Generator(device=DEV).manual_seed(1234 + seed)
+    kp = torch.empty((P, hkv, S, D), dtype=torch.bfloat16, device=DEV).normal_(generator=g)
+    vp = torch.empty((P, hkv, S, D), dtype=torch.bfloat16, device=DEV).normal_(generator=g)
+    q = torch.randn((len(ctx), hq, D), dtype=torch.bfloat16, device=DEV, generator=g)
+    return q, kp, vp, tables, ctx, bt.to(DEV)
+
+
+def _attend(q, kp, vp, bt, ctx) -> np.ndarray:
+    out = kernels.paged_decode_attention(q, kp, vp, bt,
+                                         torch.tensor(ctx, dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+def _stages(q, kp, bt) -> int:
+    return kernels.decode_attn_ring_stages(q.shape[0], bt.shape[1], q.shape[1], kp.shape[1],
+                                           kp.shape[3], kp.shape[2], kp.shape[0], kp.dtype)
+
+
+@pytest.fixture(scope="module")
+def c3_batch():
+    layer = c3_layer(32, 8)
+    q, kp, vp, tables, ctx, _ = layer
+    return layer, oracle_decode_by_request(q, kp, vp, tables, ctx, S)
+
+
+def test_c3_batch_automatic_choice_is_the_shallow_ring(c3_batch) -> None:
+    (q, kp, vp, tables, ctx, bt), ref = c3_batch
+    kernels.set_decode_attn_ring("auto")
+    assert _stages(q, kp, bt) == 2  # what the benchmark's decode step runs
+    assert_close(_attend(q, kp, vp, bt, ctx), ref, ATOL, RTOL)
+
+
+@pytest.mark.parametrize("mode,stages", [("deep", 4), ("shallow", 2)])
+def test_c3_batch_forced_ring_matches_oracle(c3_batch, mode: str, stages: int) -> None:
+    (q, kp, vp, tables, ctx, bt), ref = c3_batch
+    kernels.set_decode_attn_ring(mode)
+    assert _stages(q, kp, bt) == stages
+    out = _attend(q, kp, vp, bt, ctx)
+    assert_close(out, ref, ATOL, RTOL)
+    # the same launch again gives the same bits (the merge order is fixed per launch shape)
+    assert np.array_equal(_attend(q, kp, vp, bt, ctx), out)
+
+
+def test_c3_one_kv_head_shard_above_the_shallow_threshold() -> None:
+    # One rank's share at 8 GPUs (1 KV head, its 4 query heads); a padded block-table
+    # width puts batch x width x heads above the threshold, so the automatic choice is
+    # the shallow ring with ~11 pieces per (request, head) segment to merge.
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    width = -(-150 * sms * 2 * 4 // 64) + 8
+    q, kp, vp, tables, ctx, bt = c3_layer(4, 1, width=width, seed=5)
+    kernels.set_decode_attn_ring("auto")
+    assert _stages(q, kp, bt) == 2
+    ref = oracle_decode_by_request(q, kp, vp, tables, ctx, S)
+    assert_close(_attend(q, kp, vp, bt, ctx), ref, ATOL, RTOL)
+    kernels.set_decode_attn_ring("deep")
+    assert _stages(q, kp, bt) == 4
+    assert_close(_attend(q, kp, vp, bt, ctx), ref, ATOL, RTOL)
+
+
+@pytest.mark.parametrize("mode", ["deep", "shallow"])
+@pytest.mark.parametrize("cfg", CONFIGS, ids=[c[0] for c in CONFIGS])
+def test_attention_configs_under_forced_ring(cfg, mode: str) -> None:
+    import zlib
+
+    name, B, Hq, Hkv, Dh, Sp, gen = cfg
+    rng = np.random.default_rng(zlib.crc32(name.encode()) + 17)
+    ctx = [int(c) for c in gen(rng, B)]
+    q, kp, vp, tables = _random_batch(11, B, Hq, Hkv, Dh, Sp, ctx, torch.bfloat16)
+    kernels.set_decode_attn_ring(mode)
+    out = _run(q, kp, vp, tables, ctx)
+    assert_close(out, _oracle(q, kp, vp, tables, ctx, Sp), ATOL, RTOL)
+
+
+def test_ring_mode_rejects_unknown_values() -> None:
+    with pytest.raises(ValueError):
+        kernels.set_decode_attn_ring("medium")

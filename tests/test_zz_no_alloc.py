@@ -27,7 +27,7 @@ DEV = torch.device("cuda", 0)
 ATOL, RTOL = 2e-2, 1e-2
 
 
-def _batch(seed: int, ctx: list[int], Hq=32, Hkv=8, D=128, S=16):
+def _batch(seed: int, ctx: list[int], Hq=32, Hkv=8, D=128, S=16, dtype=torch.bfloat16):
     g = torch.Generator().manual_seed(seed)
     npg = [-(-c // S) for c in ctx]
     P = sum(npg) + 2
@@ -37,9 +37,9 @@ def _batch(seed: int, ctx: list[int], Hq=32, Hkv=8, D=128, S=16):
     for i, n in enumerate(npg):
         bt[i, :n] = perm[cur:cur + n].to(torch.int32)
         cur += n
-    q = torch.randn((len(ctx), Hq, D), generator=g).to(torch.bfloat16).to(DEV)
-    kp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(DEV)
-    vp = torch.randn((P, Hkv, S, D), generator=g).to(torch.bfloat16).to(DEV)
+    q = torch.randn((len(ctx), Hq, D), generator=g).to(dtype).to(DEV)
+    kp = torch.randn((P, Hkv, S, D), generator=g).to(dtype).to(DEV)
+    vp = torch.randn((P, Hkv, S, D), generator=g).to(dtype).to(DEV)
     return q, kp, vp, bt.to(DEV), torch.tensor(ctx, dtype=torch.int32, device=DEV)
 
 
@@ -49,7 +49,7 @@ def _noalloc(q, kp, vp, bt, ctx_lens, out, err=None) -> int:
     lib = _capi.load()
     return lib.pi_paged_decode_attn_noalloc(
         out.data_ptr(), q.data_ptr(), kp.data_ptr(), vp.data_ptr(), bt.data_ptr(), bt.stride(0),
-        ctx_lens.data_ptr(), B, Hq, Hkv, D, S, P, 1.0 / math.sqrt(D), _capi.PI_DTYPE_BF16,
+        ctx_lens.data_ptr(), B, Hq, Hkv, D, S, P, 1.0 / math.sqrt(D), kernels.dtype_code(q.dtype),
         q.stride(0), out.stride(0), None if err is None else err.data_ptr(),
         torch.cuda.current_stream().cuda_stream)
 
@@ -88,3 +88,15 @@ def test_noalloc_rejects_requests_beyond_its_scratch() -> None:
     rc = _noalloc(q, kp, vp, bt, ctx_lens, out)
     assert rc == _capi.PI_ERR_SCRATCH_LIMIT
     assert "scratch" in _capi.error_string(rc)
+
+
+def test_noalloc_serves_simt_path_shapes_without_a_scratch_limit() -> None:
+    # fp32 pools at head_dim 256 run on the generic SIMT path, which uses no scratch, so
+    # the size limit does not apply even though the fast path's need would exceed it.
+    q, kp, vp, bt, ctx_lens = _batch(4, [40, 70, 1], Hq=8, Hkv=2, D=256, dtype=torch.float32)
+    ref = kernels.paged_decode_attention(q, kp, vp, bt, ctx_lens)
+    out = torch.full_like(ref, float("nan"))
+    rc = _noalloc(q, kp, vp, bt, ctx_lens, out)
+    assert rc == _capi.PI_OK, _capi.error_string(rc)
+    torch.cuda.synchronize()
+    assert torch.allclose(out, ref, atol=1e-5, rtol=1e-5)
