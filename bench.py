@@ -16,10 +16,15 @@ and MLP are outside the path and not run.
              the attention outputs are inside the timed region
   roofline   the attention kernel: algorithmic bytes (context K/V + q + out + block
              table) / its CUDA-event time, against the measured HBM copy bandwidth
-  index_copy C2 microbench (65536-page pool): GB/s at B = 1, 64, 512 and a large-B sweep
-  cpu_baseline the oracle (numpy port of the reference path) on a bounded sample
+  index_copy C2 microbench (65536-page pool): GB/s at B = 1, 64, 512, a whole 36-layer
+             step in one launch (2304) and a large-B sweep; graphs of back-to-back launches
+             with L2 flushed before every timed replay
+  cpu_baseline the oracle (numpy port of the reference path) on layer 0 of the timed step
+  parity     that layer's GPU output against the oracle's (the run exits non-zero on a
+             mismatch)
 
-`--impl reference` times the CPU reference path instead (rank 0 only).
+`--impl reference` times the reference's CPU path instead (rank 0 only): its own torch
+operations (oracle/ref_torch_path.py), one real layer of the step per timed step.
 Multi-GPU (torchrun, N = 2/4/8): KV heads and their pools are split across ranks;
 each rank attends its heads and the per-layer outputs are all-gathered before o_proj
 would run, inside the attention kernel (NVLink peer stores; --nccl: an NCCL
@@ -47,7 +52,8 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tok/s (Qwen3-8B shape, paged KV); index-copy GB/s vs HBM peak"
 C3 = dict(layers=36, batch=64, hq=32, hkv=8, head_dim=128, page_size=16, ctx_lo=512,
           ctx_hi=8192, seed=0)
-C2 = dict(pages=65536, page_size=16, hkv=8, head_dim=128, batches=(1, 64, 512, 4096, 65536))
+C2 = dict(pages=65536, page_size=16, hkv=8, head_dim=128,
+          batches=(1, 64, 512, 2304, 4096, 65536))
 C3["desc"] = ("C3 qwen3-8b-shape paged decode KV path: 36 layers x (index-copy of 64 new K/V "
               "rows + paged GQA decode attention), B=64, ctx U[512,8192] seed 0, 32q/8kv heads, "
               "head_dim 128, page 16")
@@ -308,30 +314,55 @@ def barrier(world: int) -> None:
     torch.cuda.synchronize()
 
 
+def l2_flush_buffer(dev: torch.device) -> torch.Tensor:
+    """A buffer larger than L2 (126 MB on B200): writing it evicts everything cached."""
+    return torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+
 def bench_index_copy(dev: torch.device, peak: float) -> dict:
-    """C2: scatter of B rows into a 65536-page bf16 pool; per-launch device time."""
+    """C2: scatter of B rows into a 65536-page bf16 pool; per-launch device time.
+
+    Each B is timed as a CUDA graph of R back-to-back launches, as a decode step issues
+    them (one per layer): launch i reads its own source rows and writes its own random
+    distinct slots, and L2 is flushed (a 256 MB write, outside the timed region)
+    before every timed replay, so no launch finds its rows in L2. B = 2304 is a whole
+    36-layer step of the 8B shape written by one launch (all layers share the pool).
+    """
     from plastic_infer_b200 import kernels
 
     P, S, H, D = C2["pages"], C2["page_size"], C2["hkv"], C2["head_dim"]
     g = torch.Generator(device=dev).manual_seed(7)
     kp = torch.zeros((P, H, S, D), dtype=torch.bfloat16, device=dev)
     vp = torch.zeros_like(kp)
+    flush = l2_flush_buffer(dev)
     res = {}
     rng = np.random.default_rng(0)
-    perm = rng.permutation(P * S)
+    perm = torch.from_numpy(rng.permutation(P * S).astype(np.int64)).to(dev)
     for B in C2["batches"]:
-        slots = torch.from_numpy(perm[:B].astype(np.int64)).to(dev)
-        kn = torch.randn((B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
-        vn = torch.randn((B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
-        reps = 200 if B <= 4096 else 20
-        fn = lambda: kernels.kv_index_copy(kp, vp, kn, vn, slots)  # noqa: E731
-        graph = graph_of(fn)
+        row_bytes = B * H * D * 2  # one of K or V
+        R = int(max(8, min(100, (1 << 30) // row_bytes)))
+        k_src = torch.randn((R, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+        v_src = torch.randn((R, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+        n_slots = P * S
+        slots = torch.stack([perm[(i * B) % (n_slots - B + 1):][:B] for i in range(R)])
+
+        def launches(k_src=k_src, v_src=v_src, slots=slots, R=R):
+            for i in range(R):
+                kernels.kv_index_copy(kp, vp, k_src[i], v_src[i], slots[i])
+
+        graph = graph_of(launches)
         graph.replay()
-        ms = time_region(graph.replay, reps, torch.cuda.current_stream())
-        t = ms / reps * 1e-3
+        reps = 5
+        ms = 0.0
+        stream = torch.cuda.current_stream()
+        for _ in range(reps):
+            flush.fill_(1)
+            ms += time_region(graph.replay, 1, stream)
+        t = ms / (reps * R) * 1e-3
         byts = 8200.0 * B
         res[str(B)] = dict(us_per_launch=round(t * 1e6, 3), gbs=round(byts / t / 1e9, 1),
-                           frac_of_hbm=round(byts / t / 1e9 / peak, 3))
+                           frac_of_hbm=round(byts / t / 1e9 / peak, 3), launches_per_graph=R)
+        del graph, k_src, v_src, slots
     return res
 
 
@@ -592,65 +623,109 @@ def bench_host_stream(dev: torch.device) -> dict:
     return res
 
 
-class CpuSample:
-    """The C3 KV path of `requests` requests on the CPU (the oracle, a numpy port of the
-    reference's _write_kv_layer + paged_attention_v1), built once and run per layer.
+class LayerSnapshot:
+    """Layer 0 of the timed step, copied on the device right after the timed region:
+    the attention output and the pages it read (the step's new rows included)."""
 
-    Pools are fp32 in the reference's logical layout [pages, Hkv, D, S]; every layer
-    run reuses the same pools (the work per layer is the same for every layer).
+    def __init__(self, wl: "DecodeWorkload") -> None:
+        S = wl.cfg["page_size"]
+        npg = (wl.ctx + S - 1) // S
+        bt = wl.block_tables[0].cpu().numpy()
+        ids = np.concatenate([bt[b, :npg[b]] for b in range(len(npg))]).astype(np.int64)
+        dev_ids = torch.from_numpy(ids).to(wl.k_pool.device)
+        self.k = wl.k_pool.index_select(0, dev_ids)
+        self.v = wl.v_pool.index_select(0, dev_ids)
+        self.out = wl.out[0].clone()
+        self.q = wl.q[0].clone()
+        self.k_new = wl.k_new[0].clone()
+        self.v_new = wl.v_new[0].clone()
+        self.ctx = wl.ctx.copy()
+        self.npg = npg
+
+
+class CpuSample:
+    """The C3 KV path on the CPU with the oracle (a numpy port of the reference's
+    _write_kv_layer + paged_attention_v1), run per layer on one layer's data.
+
+    Built from a LayerSnapshot, the data are layer 0 of the step the GPU just timed
+    (bf16 values widened to fp32, pools in the reference's logical [pages, Hkv, D, S]
+    layout with the layer's pages renumbered 0..n-1), so the first layer the baseline
+    runs is also the parity check of the timed step: its output must match the GPU's
+    within the north-star tolerance. Without a snapshot the data are random.
     """
 
-    def __init__(self, cfg: dict, requests: int | None = None) -> None:
+    def __init__(self, cfg: dict, snap: LayerSnapshot | None = None) -> None:
         from oracle import paged_kv_oracle as orc
 
         self.orc = orc
         self.cfg = cfg
-        rng = np.random.default_rng(99)
-        self.ctx = c3_contexts(cfg)
         S, D, Hq, Hkv = cfg["page_size"], cfg["head_dim"], cfg["hq"], cfg["hkv"]
-        self.sub = self.ctx[: (requests or cfg["batch"])]
-        npg = (self.sub + S - 1) // S
+        self.ctx = c3_contexts(cfg) if snap is None else snap.ctx
+        npg = (self.ctx + S - 1) // S
         P = int(npg.sum())
-        self.kp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
-        self.vp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
-        perm = rng.permutation(P)
         self.tables, cur = [], 0
-        for n in npg:
-            self.tables.append([int(x) for x in perm[cur:cur + n]])
-            cur += n
-        self.q = rng.standard_normal((len(self.sub), Hq, D), dtype=np.float32)
-        self.kn = rng.standard_normal((len(self.sub), Hkv, D), dtype=np.float32)
-        self.slots = np.array([orc.slot_of(t, int(c) - 1, S) for t, c in zip(self.tables, self.sub)])
+        if snap is not None:
+            for n in npg:
+                self.tables.append(list(range(cur, cur + int(n))))
+                cur += int(n)
+            self.kp = snap.k.permute(0, 1, 3, 2).float().cpu().numpy()
+            self.vp = snap.v.permute(0, 1, 3, 2).float().cpu().numpy()
+            self.q = snap.q.float().cpu().numpy()
+            self.kn = snap.k_new.float().cpu().numpy()
+            self.vn = snap.v_new.float().cpu().numpy()
+            self.gpu_out = snap.out.float().cpu().numpy()
+        else:
+            rng = np.random.default_rng(99)
+            self.kp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+            self.vp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+            perm = rng.permutation(P)
+            for n in npg:
+                self.tables.append([int(x) for x in perm[cur:cur + n]])
+                cur += n
+            self.q = rng.standard_normal((len(self.ctx), Hq, D), dtype=np.float32)
+            self.kn = rng.standard_normal((len(self.ctx), Hkv, D), dtype=np.float32)
+            self.vn = self.kn
+            self.gpu_out = None
+        self.slots = np.array([orc.slot_of(t, int(c) - 1, S) for t, c in zip(self.tables, self.ctx)])
+        self.parity = None
 
-    def layer(self) -> None:
-        self.orc.write_kv_slots(self.kp, self.vp, self.kn, self.kn, self.slots, self.cfg["page_size"])
-        self.orc.paged_attention_decode(self.q, self.kp, self.vp, self.tables, self.sub,
-                                        self.cfg["page_size"])
+    def layer(self) -> np.ndarray:
+        self.orc.write_kv_slots(self.kp, self.vp, self.kn, self.vn, self.slots, self.cfg["page_size"])
+        return self.orc.paged_attention_decode(self.q, self.kp, self.vp, self.tables, self.ctx,
+                                               self.cfg["page_size"])
+
+    def check(self, ref: np.ndarray) -> dict:
+        """Compare the GPU's layer-0 output with the oracle's: |gpu - ref| <= 2e-2 + 1e-2 |ref|."""
+        err = np.abs(self.gpu_out - ref)
+        bad = int((err > 2e-2 + 1e-2 * np.abs(ref)).sum()) + int((~np.isfinite(self.gpu_out)).sum())
+        return dict(status="ok" if bad == 0 else "FAIL",
+                    checked=f"layer 0 of the timed step: {ref.shape[0]} requests x {ref.shape[1]} "
+                            f"query heads x {ref.shape[2]} vs the numpy oracle",
+                    tolerance="|out - ref| <= 2e-2 + 1e-2 |ref| (fp32 oracle on the same bf16 inputs)",
+                    max_abs_err=float(err.max()), violations=bad)
 
     def measure(self, target_s: float) -> dict:
         """Run layers until `target_s` seconds of CPU work (at least one); tok/s of a step."""
         cfg = self.cfg
         layers, t0 = 0, time.perf_counter()
         while True:
-            self.layer()
+            out = self.layer()
+            if layers == 0 and self.gpu_out is not None:
+                self.parity = self.check(out)
             layers += 1
             dt = time.perf_counter() - t0
             if dt >= target_s or layers >= cfg["layers"]:
                 break
-        scale = (self.ctx.sum() / self.sub.sum()) * (cfg["layers"] / layers)
+        scale = cfg["layers"] / layers
         step_s = dt * scale
         return dict(value=round(cfg["batch"] / step_s, 3), unit="tok/s",
                     cores=_blas_threads(), host_cpus=os.cpu_count(), cpu_model=_cpu_model(),
                     kind="port",
-                    sample=f"{layers} layer(s) x {len(self.sub)} of {cfg['batch']} requests "
-                           f"({int(self.sub.sum())} of {int(self.ctx.sum())} context tokens per "
-                           f"layer), fp32 numpy oracle, scaled x{scale:.2f} to one "
-                           f"{cfg['layers']}-layer step; {dt:.1f} s measured")
-
-
-def cpu_baseline_sample(cfg: dict, target_s: float = 12.0) -> dict:
-    """Oracle on a bounded sample (all requests, ~target_s of CPU work), scaled to a step."""
-    return CpuSample(cfg).measure(target_s)
+                    sample=f"{layers} layer(s) x {len(self.ctx)} requests ({int(self.ctx.sum())} "
+                           f"context tokens per layer), fp32 numpy oracle on "
+                           f"{'layer 0 of the timed step' if self.gpu_out is not None else 'random data'}"
+                           f", scaled x{scale:.2f} to one {cfg['layers']}-layer step; {dt:.1f} s "
+                           f"measured")
 
 
 def _cpu_model() -> str:
@@ -677,26 +752,80 @@ def _blas_threads() -> int:
     return os.cpu_count() or 1
 
 
+class ReferenceLayer:
+    """One C3 decode layer on the CPU with the reference's own algorithm (its torch
+    operations, restated in oracle/ref_torch_path.py): for each of the 64 requests, the
+    new K/V row written into a logical [pages, Hkv, D, S] bf16 pool, then gather +
+    repeat_interleave + SDPA over its context. bf16 is the pool dtype of the config.
+    """
+
+    def __init__(self, cfg: dict) -> None:
+        from oracle import ref_torch_path as rtp
+
+        self.rtp = rtp
+        self.cfg = cfg
+        S, D, Hq, Hkv = cfg["page_size"], cfg["head_dim"], cfg["hq"], cfg["hkv"]
+        self.ctx = [int(c) for c in c3_contexts(cfg)]
+        npg = [-(-c // S) for c in self.ctx]
+        P = sum(npg)
+        g = torch.Generator().manual_seed(99)
+        self.kp = torch.empty((P, Hkv, D, S), dtype=torch.bfloat16).normal_(generator=g)
+        self.vp = torch.empty((P, Hkv, D, S), dtype=torch.bfloat16).normal_(generator=g)
+        perm = torch.randperm(P, generator=g).tolist()
+        self.tables, cur = [], 0
+        for n in npg:
+            self.tables.append(perm[cur:cur + n])
+            cur += n
+        B = len(self.ctx)
+        self.q = torch.randn((B, Hq, D), generator=g).to(torch.bfloat16)
+        self.kn = torch.randn((B, Hkv, D), generator=g).to(torch.bfloat16)
+        self.vn = torch.randn((B, Hkv, D), generator=g).to(torch.bfloat16)
+
+    def run(self) -> None:
+        self.rtp.decode_layer(self.q, self.kn, self.vn, self.kp, self.vp, self.tables, self.ctx,
+                              self.cfg["page_size"])
+
+
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference's CPU decode KV path, timed on this host's cores (rank 0 only).
+
+    Each timed step is one real layer of the C3 step: all 64 requests' K/V writes and
+    attention, as the reference's runner does them (a whole 36-layer step would take
+    about a minute per step). `ms_per_step` is that layer's measured time, so `steps` x
+    `ms_per_step` is the time actually spent; `value` is the tok/s of the 36-layer step
+    those layers add up to (64 tokens per 36 layers).
+    """
     if rank != 0:
         return
     cfg = dict(C3)
-    # one step = one layer of every request of the workload, scaled to the 36-layer step
-    sample = CpuSample(cfg)
+    torch.set_num_threads(os.cpu_count() or 1)
+    layer = ReferenceLayer(cfg)
     for _ in range(args.warmup):
-        sample.measure(0.0)
-    vals = [sample.measure(0.0) for _ in range(args.steps)]
-    v = round(statistics.median(x["value"] for x in vals), 4)
-    cb = dict(vals[0])
-    cb["value"] = v
+        layer.run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        layer.run()
+        times.append(time.perf_counter() - t0)
+    t_layer = sum(times) / len(times)
+    v = round(cfg["batch"] / (t_layer * cfg["layers"]), 4)
+    sample = (f"one of the step's {cfg['layers']} layers per timed step: 64 requests x (K/V row "
+              f"write + gather + repeat_interleave + SDPA), {sum(layer.ctx)} context tokens, bf16 "
+              f"pools, torch on {torch.get_num_threads()} threads; tok/s = 64 / (36 x "
+              f"{t_layer * 1e3:.1f} ms)")
+    cb = dict(value=v, unit="tok/s", cores=torch.get_num_threads(), host_cpus=os.cpu_count(),
+              cpu_model=_cpu_model(), kind="port",
+              code="the reference's decode path (runner_paged._write_kv_layer + "
+                   "attention.paged_attention_v1) restated op for op in oracle/ref_torch_path.py",
+              sample=sample)
     line = dict(metric=METRIC, value=v, unit="tok/s", impl="reference", n_gpus=world,
-                steps=args.steps, warmup=args.warmup, ms_per_step=round(cfg["batch"] / v * 1e3, 3),
-                higher_is_better=True, scaling="strong", vs_baseline=None, dtype="f32",
+                steps=args.steps, warmup=args.warmup, ms_per_step=round(t_layer * 1e3, 3),
+                higher_is_better=True, scaling="strong", vs_baseline=None, dtype="bf16",
                 data="synthetic",
                 config=dict(workload="C3 qwen3-8b-shape paged decode KV path (36 layers x "
                             "index-copy + paged attention), B=64, ctx U[512,8192]",
-                            global_batch=cfg["batch"], layers=cfg["layers"],
-                            parallelism="cpu reference (oracle port)"),
+                            global_batch=cfg["batch"], layers=cfg["layers"], layers_per_timed_step=1,
+                            parallelism="cpu reference (torch ops of the reference path)"),
                 cpu_baseline=cb,
                 e2e=dict(value=v, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
@@ -965,6 +1094,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     ms = max_over_ranks(ms, world)
     ms_step = ms / args.steps
     value = cfg["batch"] * args.steps / (ms * 1e-3)
+    # Layer 0 of the step just timed, for the CPU baseline leg's parity check (N = 1).
+    check_cpu = rank == 0 and world == 1 and not args.skip_cpu
+    snap = LayerSnapshot(wl) if check_cpu else None
 
     # attention alone (dominant kernel), same stream, for the roofline
     attn_fn = lambda: wl.step(attention=True, copy=False, gather=False)  # noqa: E731
@@ -987,9 +1119,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
     pro = (bench_prologue(dev, peaks["hbm_gbs"])
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
-    exc = (bench_expert_copy(dev)
-           if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
-    cpu = cpu_baseline_sample(cfg) if (rank == 0 and world == 1 and not args.skip_cpu) else None
+    cpu, parity = None, None
+    if check_cpu:
+        sample = CpuSample(cfg, snap)
+        del snap
+        cpu = sample.measure(12.0)
+        parity = sample.parity
+        del sample
 
     # measured DRAM bytes per launch exist for the C3 single-GPU launch only
     traffic = _profile_traffic() if (args.workload == "c3" and world == 1) else None
@@ -1033,10 +1169,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 workload="fused QK-norm + RoPE + K/V slot write of one decode layer (bf16, D=128, "
                          "theta 1e6, positions < 8192) vs the reference's unfused GPU ops",
                 per_shape=pro, peak=peaks["hbm_gbs"])
-        if exc is not None:
-            line["expert_copy"] = exc
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        line["parity"] = parity if parity is not None else dict(
+            status="not checked in this run",
+            why=("the check runs in the N=1 CPU baseline leg; the sharded path is checked by "
+                 "tests/test_gpu_multi.py") if world > 1 else "--skip-cpu")
         print(json.dumps(line), flush=True)
     # release graphs (they may hold NCCL work) before the process group goes away
     step_fn = attn_fn = copy_fn = None
@@ -1047,6 +1185,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if wl.exchange is not None:
         wl.exchange.close()
         barrier(world)
+    if parity is not None and parity["status"] != "ok":
+        raise SystemExit("parity check of the timed step failed: " + json.dumps(parity))
 
 
 def run_e2e(wl: DecodeWorkload, args, stream, use_graph: bool = False) -> dict:

@@ -20,7 +20,9 @@ import subprocess
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "libref_expert_copy.so"
-DEFAULT_REF = os.environ.get("PLASTIC_INFER_REF", "/root/reference")
+# The reference checkout: $PLASTIC_INFER_REF, else a directory named `reference` beside
+# this repository's root.
+DEFAULT_REF = os.environ.get("PLASTIC_INFER_REF", str(HERE.parent.parent / "reference"))
 CUH_DIR = pathlib.Path("src/plastic_infer/kernel/csrc/jit")
 
 

@@ -46,6 +46,77 @@ def test_attention_matches_reference(case: dict) -> None:
     np.testing.assert_allclose(out, ref, atol=2e-5, rtol=1e-5)
 
 
+@pytest.mark.parametrize("case", ATTENTION_CASES, ids=[c["name"] for c in ATTENTION_CASES])
+def test_reference_torch_path_matches_reference(case: dict) -> None:
+    # The timed reference arm (the reference's torch operations, restated) reproduces the
+    # reference's own attention outputs on the same fp32 inputs.
+    import torch
+
+    from oracle import ref_torch_path as rtp
+
+    g = np.load(GOLD / "attention.npz")
+    x = attention_inputs(case)
+    kp, vp = torch.from_numpy(x["k"]), torch.from_numpy(x["v"])
+    q = torch.from_numpy(x["q"])
+    out = np.stack([
+        rtp.decode_attention(q[b].view(1, 1, *q.shape[1:]), kp, vp,
+                             x["tables"][b][:-(-n // case["S"])], case["S"], n)[0, 0].numpy()
+        for b, n in enumerate(x["ctx"])])
+    np.testing.assert_allclose(out, g[case["name"] + "/out"], atol=2e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_reference_torch_path_write_matches_reference(dtype: str) -> None:
+    import torch
+
+    from oracle import ref_torch_path as rtp
+
+    g = np.load(GOLD / f"index_copy_{dtype}.npz")
+    S = int(g["page_size"])
+    conv = ((lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16))
+            if dtype == "bf16" else torch.from_numpy)
+    k = torch.zeros_like(conv(g["k_pages"]))
+    v = torch.zeros_like(k)
+    kn, vn = conv(g["k_new"]), conv(g["v_new"])
+    for i, s in enumerate(g["slots"].tolist()):
+        rtp.write_kv_token(k, v, s // S, s % S, kn[i], vn[i])
+    back = (lambda t: t.view(torch.int16).numpy().view(np.uint16)) if dtype == "bf16" else (
+        lambda t: t.numpy())
+    assert np.array_equal(back(k), g["k_pages"])
+    assert np.array_equal(back(v), g["v_pages"])
+
+
+def test_reference_torch_path_decode_layer_matches_oracle() -> None:
+    # write-then-attend over a batch: the reference arm's step equals the oracle's
+    import torch
+
+    from oracle import ref_torch_path as rtp
+
+    rng = np.random.default_rng(4)
+    B, Hq, Hkv, D, S = 5, 8, 2, 64, 16
+    ctx = [1, 16, 17, 40, 0]
+    npg = [-(-n // S) for n in ctx]
+    P = sum(npg) + 2
+    perm = rng.permutation(P)
+    tables, cur = [], 0
+    for n in npg:
+        tables.append([int(x) for x in perm[cur:cur + n]])
+        cur += n
+    kp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+    vp = rng.standard_normal((P, Hkv, D, S), dtype=np.float32)
+    q = rng.standard_normal((B, Hq, D), dtype=np.float32)
+    kn = rng.standard_normal((B, Hkv, D), dtype=np.float32)
+    vn = rng.standard_normal((B, Hkv, D), dtype=np.float32)
+    tk, tv = torch.from_numpy(kp.copy()), torch.from_numpy(vp.copy())
+    got = rtp.decode_layer(torch.from_numpy(q), torch.from_numpy(kn), torch.from_numpy(vn), tk, tv,
+                           tables, ctx, S).numpy()
+    slots = np.array([orc.slot_of(t, n - 1, S) if n > 0 else -1 for t, n in zip(tables, ctx)])
+    orc.write_kv_slots(kp, vp, kn, vn, slots, S)
+    ref = orc.paged_attention_decode(q, kp, vp, tables, ctx, S)
+    assert np.array_equal(tk.numpy(), kp)
+    np.testing.assert_allclose(got, ref, atol=2e-5, rtol=1e-5)
+
+
 def test_gather_matches_reference_layout() -> None:
     # gather_paged_kv of a non-contiguous table [4, 1, 3] with a partial last page
     # (tests/test_ops.py:227-266 geometry) == page-by-page permute + concat.
