@@ -65,10 +65,10 @@ C4 = dict(layers=48, batch=128, hq=32, hkv=4, head_dim=128, page_size=16, ctx_lo
                "K/V rows + paged GQA decode attention, G=8), B=128, ctx U[256,4096] seed 0, "
                "32q/4kv heads, head_dim 128, page 16",
           metric="decode tok/s (Qwen3-30B-A3B shape, paged KV attention path)")
-# long-context offload. Device pool = 25% of all pages; layers
-# stream in from the pinned host KV store (LRU at layer granularity) on a side stream.
-C5 = dict(layers=36, batch=8, hq=32, hkv=8, head_dim=128, page_size=16, ctx=32768,
-          pool_frac=0.25, seed=0)
+# long-context offload. Device pool = 25% of all pages; the rest of
+# every request's KV lives in the pinned host KV store (256-token chunks).
+C5 = dict(layers=36, batch=8, hq=32, hkv=8, head_dim=128, page_size=16, pages_per_chunk=16,
+          ctx=32768, pool_frac=0.25, seed=0)
 WORKLOADS = {"c3": C3, "c4": C4}
 
 
@@ -314,9 +314,21 @@ def barrier(world: int) -> None:
     torch.cuda.synchronize()
 
 
-def l2_flush_buffer(dev: torch.device) -> torch.Tensor:
-    """A buffer larger than L2 (126 MB on B200): writing it evicts everything cached."""
-    return torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+class L2Flush:
+    """Evicts L2 (126 MB on B200) between timed regions, outside them.
+
+    A 256 MB buffer is written (evicting whatever was cached) and then read, so that L2
+    is left holding clean lines: without the read, the written lines would still be
+    dirty in L2 and their write-back would land inside the next timed region.
+    """
+
+    def __init__(self, dev: torch.device) -> None:
+        self.buf = torch.empty(256 << 18, dtype=torch.int32, device=dev)
+        self.sink = torch.empty((), dtype=torch.int64, device=dev)
+
+    def __call__(self) -> None:
+        self.buf.fill_(1)
+        torch.sum(self.buf, dim=0, dtype=torch.int64, out=self.sink)
 
 
 def bench_index_copy(dev: torch.device, peak: float) -> dict:
@@ -324,8 +336,8 @@ def bench_index_copy(dev: torch.device, peak: float) -> dict:
 
     Each B is timed as a CUDA graph of R back-to-back launches, as a decode step issues
     them (one per layer): launch i reads its own source rows and writes its own random
-    distinct slots, and L2 is flushed (a 256 MB write, outside the timed region)
-    before every timed replay, so no launch finds its rows in L2. B = 2304 is a whole
+    distinct slots, and L2 is flushed (a 256 MB write then read, outside the timed
+    region) before every timed replay, so no launch finds its rows in L2. B = 2304 is a whole
     36-layer step of the 8B shape written by one launch (all layers share the pool).
     """
     from plastic_infer_b200 import kernels
@@ -334,7 +346,7 @@ def bench_index_copy(dev: torch.device, peak: float) -> dict:
     g = torch.Generator(device=dev).manual_seed(7)
     kp = torch.zeros((P, H, S, D), dtype=torch.bfloat16, device=dev)
     vp = torch.zeros_like(kp)
-    flush = l2_flush_buffer(dev)
+    flush = L2Flush(dev)
     res = {}
     rng = np.random.default_rng(0)
     perm = torch.from_numpy(rng.permutation(P * S).astype(np.int64)).to(dev)
@@ -356,7 +368,7 @@ def bench_index_copy(dev: torch.device, peak: float) -> dict:
         ms = 0.0
         stream = torch.cuda.current_stream()
         for _ in range(reps):
-            flush.fill_(1)
+            flush()
             ms += time_region(graph.replay, 1, stream)
         t = ms / (reps * R) * 1e-3
         byts = 8200.0 * B
@@ -364,6 +376,52 @@ def bench_index_copy(dev: torch.device, peak: float) -> dict:
                            frac_of_hbm=round(byts / t / 1e9 / peak, 3), launches_per_graph=R)
         del graph, k_src, v_src, slots
     return res
+
+
+def bench_page_copy(dev: torch.device, peak: float, profile: bool = False) -> dict:
+    """Page gather / scatter between the pool and a chunk-layout staging buffer (row a3).
+
+    The C5 sink unit: 8 chunks of 36 layers x 16 pages (4,608 pages, 151 MB per pool at
+    the 8B head shape) at random ids of a 65,536-page bf16 pool, moved by one launch,
+    as KVStore.sink_completed_chunks (gather) and load_prefix (scatter) issue them.
+    Algorithmic bytes = 2 x the bytes moved (read + write). Timed as a CUDA graph of R
+    back-to-back launches, each on its own random page set, with L2 flushed (write then
+    read of 256 MB, outside the timed region) before every replay.
+    """
+    from plastic_infer_b200 import kernels
+
+    P, S, H, D = C2["pages"], C2["page_size"], C2["hkv"], C2["head_dim"]
+    n, R = 8 * 36 * 16, 6
+    pool = torch.empty((P, H, S, D), dtype=torch.bfloat16, device=dev).normal_()
+    staging = [torch.empty((n, H, S, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    rng = np.random.default_rng(3)
+    ids = [torch.from_numpy(rng.permutation(P)[:n].astype(np.int32)).to(dev) for _ in range(R)]
+    moved = float(staging[0].numel() * staging[0].element_size())
+    flush = L2Flush(dev)
+    stream = torch.cuda.current_stream()
+    res = {}
+    ops = {
+        "gather": lambda i: kernels.page_gather(pool, ids[i], staging[i % 2], pages_per_group=16),
+        "scatter": lambda i: kernels.page_scatter(staging[i % 2], ids[i], pool, pages_per_group=16),
+    }
+    for name, op in ops.items():
+        if profile:
+            for i in range(3):
+                op(i)
+            continue
+        graph = graph_of(lambda op=op: [op(i) for i in range(R)])
+        reps, ms = 5, 0.0
+        for _ in range(reps):
+            flush()
+            ms += time_region(graph.replay, 1, stream)
+        t = ms / (reps * R) * 1e-3
+        res[name] = dict(us_per_launch=round(t * 1e6, 2), gbs=round(2 * moved / t / 1e9, 1),
+                         frac_of_hbm=round(2 * moved / t / 1e9 / peak, 3), launches_per_graph=R)
+        del graph
+    torch.cuda.synchronize()
+    return dict(workload=f"{n} pages (8 chunks x 36 layers x 16 pages) of a {P}-page bf16 pool, "
+                         f"{H} heads x {S} x {D}; one launch", bytes_moved=int(moved),
+                per_op=res, peak=peak)
 
 
 def bench_prologue(dev: torch.device, peak: float) -> dict:
@@ -853,135 +911,65 @@ def run_c2_only(args, dev: torch.device) -> None:
     print(json.dumps(dict(profile=True, c2_batches=list(C2["batches"]))), flush=True)
 
 
-class OffloadWorkload:
-    """C5: decode over a KV cache four times larger than the device pool.
+def c5_prefill(cfg: dict, dev: torch.device):
+    """C5 state through the host KV store API: B requests of `ctx` tokens, written chunk
+    by chunk into a device pool that holds `pool_frac` of all pages; every chunk is sunk
+    to the pinned host store as it completes, and the oldest sunk chunks are evicted to
+    make room for the next one. Returns (store, caches, decoder)."""
+    from plastic_infer_b200 import kernels
+    from plastic_infer_b200.decode import HostStoreDecoder
+    from plastic_infer_b200.kv.kv_store import KVConfig, KVStore
 
-    All K/V pages live in a pinned host store [layer][page] (the host KV store of
-    src/plastic_infer/kv/kv_store.py:185-406, here at page granularity, physical
-    layout). The device pool holds 25% of them. A layer must be resident to be
-    attended; a missing layer is brought in on the copy stream (one host->device copy
-    into a staging buffer, then page_scatter into free pool pages), evicting the least
-    recently used resident layer after writing its dirty pages (the pages that
-    received this step's new tokens) back to the host. Loads of the next layers
-    overlap the attention of the current one.
-    """
-
-    def __init__(self, cfg: dict, dev: torch.device) -> None:
-        from plastic_infer_b200 import kernels
-
-        self.k = kernels
-        self.cfg = cfg
-        self.dev = dev
-        L, B, S, D, H, Hq = (cfg[x] for x in ("layers", "batch", "page_size", "head_dim", "hkv", "hq"))
-        self.L, self.B, self.S = L, B, S
-        self.npg = cfg["ctx"] // S                    # pages per request per layer
-        self.per_layer = B * self.npg                 # pages per layer
-        self.pool_pages = int(cfg["pool_frac"] * L * self.per_layer)
-        self.slots_per_pool = self.pool_pages // self.per_layer
-        assert self.slots_per_pool >= 3, "pool must hold at least three layers"
-        page_shape = (H, S, D)
-        # host store, pinned, filled with random bf16 values layer by layer
-        self.kh = torch.empty((L, self.per_layer, *page_shape), dtype=torch.bfloat16, pin_memory=True)
-        self.vh = torch.empty_like(self.kh, pin_memory=True)
-        g = torch.Generator(device=dev).manual_seed(cfg["seed"])
-        tmp = torch.empty((self.per_layer, *page_shape), dtype=torch.bfloat16, device=dev)
-        for l in range(L):
-            self.kh[l].copy_(tmp.normal_(generator=g))
-            self.vh[l].copy_(tmp.normal_(generator=g))
-        del tmp
-        self.k_pool = torch.empty((self.pool_pages, *page_shape), dtype=torch.bfloat16, device=dev)
-        self.v_pool = torch.empty_like(self.k_pool)
-        self.stage_k = [torch.empty((self.per_layer, *page_shape), dtype=torch.bfloat16, device=dev)
-                        for _ in range(2)]
-        self.stage_v = [torch.empty_like(self.stage_k[0]) for _ in range(2)]
-        self.q = torch.randn((L, B, Hq, D), dtype=torch.bfloat16, device=dev, generator=g)
-        self.k_new = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
-        self.v_new = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
-        self.out = torch.empty((L, B, Hq, D), dtype=torch.bfloat16, device=dev)
-        self.ctx = torch.full((B,), cfg["ctx"], dtype=torch.int32, device=dev)
-        self.ws = kernels.Workspace(dev)
-        self.copy_stream = torch.cuda.Stream(device=dev)
-        self.free = list(range(self.pool_pages - 1, -1, -1))
-        self.resident: dict[int, np.ndarray] = {}     # layer -> device page ids [per_layer]
-        self.tables: dict[int, torch.Tensor] = {}     # layer -> block table [B, npg]
-        self.slot: dict[int, torch.Tensor] = {}       # layer -> new-token slots [B]
-        self.loaded: dict[int, torch.cuda.Event] = {}
-        self.done: dict[int, torch.cuda.Event] = {}
-        self.lru: list[int] = []                      # resident layers, least recent first
-        self.stage_i = 0
-        self.h2d_bytes = 0
-        self.d2h_bytes = 0
-
-    def _evict_one(self, keep: set) -> None:
-        v = next(x for x in self.lru if x not in keep)
-        self.lru.remove(v)
-        ids = self.resident.pop(v)
-        # write the dirty pages (the last page of every request got this step's token)
-        cs = self.copy_stream
-        cs.wait_event(self.done[v])
-        with torch.cuda.stream(cs):
-            for b in range(self.B):
-                j = b * self.npg + self.npg - 1
-                pid = int(ids[j])
-                self.kh[v, j].copy_(self.k_pool[pid], non_blocking=True)
-                self.vh[v, j].copy_(self.v_pool[pid], non_blocking=True)
-                self.d2h_bytes += 2 * self.k_pool[pid].numel() * 2
-        self.free.extend(int(x) for x in ids)
-        self.tables.pop(v)
-        self.slot.pop(v)
-
-    def load(self, l: int, keep: set) -> None:
-        if l in self.resident:
-            return
-        while len(self.free) < self.per_layer:
-            self._evict_one(keep)
-        ids = np.array([self.free.pop() for _ in range(self.per_layer)], dtype=np.int32)
-        ids_d = torch.from_numpy(ids).to(self.dev, non_blocking=False)
-        i = self.stage_i
-        self.stage_i ^= 1
-        cs = self.copy_stream
-        with torch.cuda.stream(cs):
-            self.stage_k[i].copy_(self.kh[l], non_blocking=True)
-            self.stage_v[i].copy_(self.vh[l], non_blocking=True)
-            self.k.page_scatter(self.stage_k[i], ids_d, self.k_pool)
-            self.k.page_scatter(self.stage_v[i], ids_d, self.v_pool)
-            ev = torch.cuda.Event()
-            ev.record(cs)
-        ids_d.record_stream(cs)
-        self.h2d_bytes += 2 * self.stage_k[i].numel() * 2
-        self.loaded[l] = ev
-        self.resident[l] = ids
-        self.lru.append(l)
-        self.tables[l] = torch.from_numpy(ids.reshape(self.B, self.npg)).to(self.dev)
-        last = ids.reshape(self.B, self.npg)[:, -1].astype(np.int64) * self.S + (self.S - 1)
-        self.slot[l] = torch.from_numpy(last).to(self.dev)
-
-    def step(self, ahead: int = 2) -> None:
-        cur = torch.cuda.current_stream()
-        for l in range(self.L):
-            for a in range(ahead + 1):
-                nxt = (l + a) % self.L
-                self.load(nxt, keep={(l + x) % self.L for x in range(ahead + 1)})
-            if l in self.lru:
-                self.lru.remove(l)
-                self.lru.append(l)
-            cur.wait_event(self.loaded[l])
-            self.k.kv_index_copy(self.k_pool, self.v_pool, self.k_new[l], self.v_new[l], self.slot[l])
-            self.k.paged_decode_attention(self.q[l], self.k_pool, self.v_pool, self.tables[l], self.ctx,
-                                          out=self.out[l], workspace=self.ws)
-            ev = torch.cuda.Event()
-            ev.record(cur)
-            self.done[l] = ev
+    L, B, S, D, H = (cfg[x] for x in ("layers", "batch", "page_size", "head_dim", "hkv"))
+    ppc = cfg["pages_per_chunk"]
+    tpc = S * ppc
+    total_pages = L * B * cfg["ctx"] // S
+    pool = int(cfg["pool_frac"] * total_pages)
+    kvc = KVConfig(n_layers=L, n_kv_heads=H, head_dim=D, page_size=S, pages_per_chunk=ppc,
+                   max_pages=pool, max_host_chunks=B * (cfg["ctx"] // tpc) + B,
+                   dtype=torch.bfloat16, device=dev)
+    store = KVStore(kvc)
+    caches = [store.new_request(request_id=b) for b in range(B)]
+    # headroom for one decode step's new pages (a page per layer per request)
+    dec = HostStoreDecoder(store, caches, budget_pages=pool - L * B)
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    rows_k = torch.empty((tpc * L, H, D), dtype=torch.bfloat16, device=dev)
+    rows_v = torch.empty_like(rows_k)
+    rng = np.random.default_rng(cfg["seed"])
+    chunk_pages = L * ppc
+    for c in range(cfg["ctx"] // tpc):
+        for cache in caches:
+            dec.evict_to(pool - chunk_pages)  # room for this chunk
+            start = cache.length
+            cache.reserve_tokens(tpc)
+            slots = torch.tensor([cache.block_table.slot(l, start + t)
+                                  for t in range(tpc) for l in range(L)],
+                                 dtype=torch.int64, device=dev)
+            rows_k.normal_(generator=g)
+            rows_v.normal_(generator=g)
+            kernels.kv_index_copy(store.gpu.k_phys, store.gpu.v_phys, rows_k, rows_v, slots)
+            cache.extend_token_ids([int(x) for x in rng.integers(0, 151936, tpc)])
+            store.sink_completed_chunks_async(cache)
+    dec.evict_to(dec.budget)
+    torch.cuda.synchronize()
+    return store, caches, dec
 
 
 def run_c5(args, rank: int, world: int, dev: torch.device) -> None:
-    """C5 long-context offload line (rank 0, one GPU)."""
+    """C5 long-context offload line (rank 0, one GPU), through the KV store API.
+
+    Every request has most of its KV in the pinned host store. Each decode step runs
+    HostStoreDecoder: per layer the new K/V rows are written, and every request is
+    attended by host-stream attention over its evicted chunks (read in place over the
+    host link) plus its device tail; completed chunks are sunk on the store's side
+    stream and evicted to the pool budget. The roofline is the host link: host bytes
+    read per step / step time against a pinned 1 GiB host->device copy measured here.
+    """
     if rank != 0:
         return
     cfg = dict(C5)
     if args.layers:
         cfg["layers"] = args.layers
-    # link peak of this box: pinned 1 GiB host->device copy
     h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
     d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
     d.copy_(h)
@@ -989,34 +977,61 @@ def run_c5(args, rank: int, world: int, dev: torch.device) -> None:
     link = 1.0 / (time_region(lambda: d.copy_(h, non_blocking=True), 3,
                               torch.cuda.current_stream()) / 3 * 1e-3) * (1 << 30) / 1e9
     del h, d
-    wl = OffloadWorkload(cfg, dev)
-    stream = torch.cuda.current_stream()
-    for _ in range(max(1, args.warmup)):
-        wl.step()
+    t0 = time.perf_counter()
+    store, caches, dec = c5_prefill(cfg, dev)
+    prefill_s = time.perf_counter() - t0
+    L, B, D, H, Hq = (cfg[x] for x in ("layers", "batch", "head_dim", "hkv", "hq"))
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"] + 1)
+    q = torch.randn((L, B, Hq, D), dtype=torch.bfloat16, device=dev, generator=g)
+    kn = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+    vn = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
+    out = torch.empty_like(q)
+    rng = np.random.default_rng(cfg["seed"] + 2)
+    tpc = cfg["page_size"] * cfg["pages_per_chunk"]
+    chunk_layer_bytes = 2 * tpc * H * D * 2          # K + V of one chunk of one layer
+
+    def step():
+        dec.step(q, kn, vn, token_ids=[int(x) for x in rng.integers(0, 151936, B)], out=out)
+
+    for _ in range(args.warmup):
+        step()
     torch.cuda.synchronize()
-    wl.h2d_bytes = wl.d2h_bytes = 0
+    host_bytes = 0
     with ClockSampler([dev.index or 0]) as clk:
-        ms = time_region(wl.step, args.steps, stream)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            host_bytes += sum(c.evicted_chunks for c in caches) * chunk_layer_bytes * L
+            step()
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end)
     ms_step = ms / args.steps
-    h2d = wl.h2d_bytes / args.steps
-    d2h = wl.d2h_bytes / args.steps
-    link_gbs = h2d / (ms_step * 1e-3) / 1e9
+    hb = host_bytes / args.steps
+    link_gbs = hb / (ms_step * 1e-3) / 1e9
+    resident = sum(c.length - c.evicted_chunks * tpc for c in caches)
     line = dict(
         metric="decode tok/s (long-context host offload, Qwen3-8B attention shape)",
-        value=round(cfg["batch"] * args.steps / (ms * 1e-3), 2), unit="tok/s", n_gpus=1,
+        value=round(B * args.steps / (ms * 1e-3), 2), unit="tok/s", n_gpus=1,
         steps=args.steps, warmup=args.warmup, ms_per_step=round(ms_step, 2), higher_is_better=True,
         scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic",
-        config=dict(workload="C5 long-context offload: B=8 x 32768 tokens, 36 layers, 32q/8kv heads, "
-                    "head_dim 128, page 16; device pool = 25% of all pages; layer-granular LRU "
-                    "over a pinned host store; loads (H2D + page_scatter) on a side stream "
-                    "overlapped with index-copy + attention; dirty pages written back D2H",
-                    pool_pages=wl.pool_pages, pages_per_layer=wl.per_layer,
-                    host_store_gb=round(2 * wl.kh.numel() * 2 / 1e9, 1)),
+        config=dict(workload=f"C5 long-context offload through the KV store API: B={B} x "
+                    f"{cfg['ctx']} tokens, {L} layers, {Hq}q/{H}kv heads, head_dim {D}, page "
+                    f"{cfg['page_size']}; device pool = {cfg['pool_frac']:.0%} of all pages; "
+                    "HostStoreDecoder: per layer index-copy + host-stream attention over the "
+                    "evicted chunks (pinned, read in place) and the device tail; async sink + "
+                    "eviction to the budget after every step",
+                    pool_pages=store.gpu.total_pages, budget_pages=dec.budget,
+                    evicted_chunks=sum(c.evicted_chunks for c in caches),
+                    resident_tokens=resident, host_store_gb=round(
+                        store.host_cache_size * 2 * L * chunk_layer_bytes / 2 / 1e9, 1),
+                    prefill_s=round(prefill_s, 1)),
         roofline=dict(bound="host link", achieved=round(link_gbs, 1), peak=round(link, 1),
                       unit="GB/s", frac=round(link_gbs / link, 3),
                       peak_source="pinned 1 GiB host->device copy measured in this run"),
-        h2d_bytes_per_step=int(h2d), d2h_bytes_per_step=int(d2h),
-        gpu_launches=args.steps * cfg["layers"] * 4,
+        host_bytes_read_per_step=int(hb),
         clocks=clk.summary(),
     )
     print(json.dumps(line), flush=True)
@@ -1033,6 +1048,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         return
     if args.prefill_only:
         print(json.dumps(dict(prefill=bench_prefill(dev, measured_peaks()))), flush=True)
+        return
+    if args.page_copy_only:
+        print(json.dumps(dict(page_copy=bench_page_copy(dev, measured_peaks()["hbm_gbs"],
+                                                        profile=args.profile))), flush=True)
         return
     if args.expert_copy_only:
         print(json.dumps(dict(expert_copy=bench_expert_copy(dev))), flush=True)
@@ -1327,6 +1346,9 @@ def main() -> None:
                     help="print only the host-stream attention microbench (C5 shape)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the paged prefill attention microbench")
+    ap.add_argument("--page-copy-only", action="store_true",
+                    help="run only the page gather/scatter microbench (with --profile: plain "
+                         "launches for ncu)")
     ap.add_argument("--expert-copy-only", action="store_true",
                     help="run only the MoE expert-slot copy microbench")
     ap.add_argument("--prologue-only", action="store_true",

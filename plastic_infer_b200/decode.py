@@ -108,3 +108,131 @@ def decode_step_paged_batched(weights: DenseWeights, config: ModelConfig, store:
         x = x + linear(ffn, weights[p + "mlp.down_proj.weight"])
     x = rms_norm(x, weights["norm.weight"])
     return linear(x[:, -1, :], weights["lm_head.weight"])
+
+
+class HostStoreDecoder:
+    """Decode steps for requests whose KV outgrows the device pool (the host KV store
+    wired into the decode loop).
+
+    The reference keeps the host store's primitives (sink_completed_chunks, load_prefix,
+    evict_chunks, host_stream_attention_v1; src/plastic_infer/kv/kv_store.py:230-386,
+    src/plastic_infer/exec/attention.py:193-250) but its engine never calls them
+    (src/plastic_infer/runtime/engine.py:501-539). This driver does, once per step:
+
+    begin_step   every request gets the slot of its new token; when the pool has too few
+                 free pages for them, the oldest host-backed chunks are evicted first.
+    attend       per layer: the new K/V rows are written (one index-copy launch), the
+                 requests that still hold all their chunks on the device are attended in
+                 one paged_decode_attention launch, and every request with evicted chunks
+                 through host_stream_attention_v1 over its host chunks (pinned, read in
+                 place) and its device tail (KVStore.host_stream_chunks).
+    end_step     completed chunks are sunk to the host store on the store's side stream
+                 without waiting (KVStore.sink_completed_chunks_async), so the copies run
+                 under the next step's attention, and chunks are evicted until the pool
+                 holds at most `budget_pages` pages.
+
+    Only chunks whose sink has been queued are evicted; each request keeps at least its
+    newest complete chunk and its partial tail on the device (evict_chunks' rule).
+    Inputs per layer are the step's post-RoPE q [B, Hq, D] and new k, v [B, Hkv, D].
+    """
+
+    def __init__(self, store: KVStore, caches: list[KVRequestCache],
+                 budget_pages: int | None = None) -> None:
+        self.store = store
+        self.caches = caches
+        cfg = store.config
+        self.budget = store.gpu.total_pages if budget_pages is None else int(budget_pages)
+        self.chunk_pages = cfg.n_layers * cfg.pages_per_chunk
+        self.tables = BatchTables(store, caches)
+        self.device = store.gpu.device
+        self.workspace = kernels.default_workspace(self.device)
+        self.positions: list[int] = []
+        self.slots: torch.Tensor | None = None
+        self.ctx_resident: torch.Tensor | None = None
+        self.streamed: list[int] = []
+        self.evictions = 0
+
+    # -- pool budget -------------------------------------------------------------
+
+    def used_pages(self) -> int:
+        gpu = self.store.gpu
+        return gpu.total_pages - gpu.allocator.free_pages
+
+    def _evictable(self, cache: KVRequestCache) -> bool:
+        c = cache.evicted_chunks
+        return (c < cache.num_complete_chunks() - 1 and c < len(cache.chunk_keys)
+                and self.store.has_host_chunk(cache.chunk_keys[c].full_key))
+
+    def evict_to(self, max_used: int) -> int:
+        """Evict one chunk at a time, from the request with the most resident complete
+        chunks, until at most `max_used` pages are in use; returns pages freed."""
+        freed = 0
+        while self.used_pages() > max_used:
+            cands = [c for c in self.caches if self._evictable(c)]
+            if not cands:
+                break
+            victim = max(cands, key=lambda c: c.num_complete_chunks() - c.evicted_chunks)
+            got = self.store.evict_chunks(self.chunk_pages, protected_request=victim)
+            if got == 0:
+                break
+            freed += got
+            self.evictions += 1
+        return freed
+
+    # -- one step ---------------------------------------------------------------
+
+    def begin_step(self, token_ids: list[int] | None = None) -> None:
+        """Reserve every request's next slot; `token_ids` (one per request) extend the
+        requests' chunk keys, so the chunks they complete can be sunk."""
+        cfg = self.store.config
+        need = sum(cfg.n_layers for c in self.caches
+                   if c.length % cfg.page_size == 0)  # a new page in every layer
+        gpu = self.store.gpu
+        if gpu.allocator.free_pages < need:
+            self.evict_to(gpu.total_pages - need)
+        self.positions = [c.length for c in self.caches]
+        for i, c in enumerate(self.caches):
+            c.reserve_tokens(1)
+            if token_ids is not None:
+                c.extend_token_ids([token_ids[i]])
+        self.tables.refresh()
+        L = cfg.n_layers
+        self.slots = torch.tensor([[c.block_table.slot(l, p) for c, p in zip(self.caches, self.positions)]
+                                   for l in range(L)], dtype=torch.int64, device=self.device)
+        self.streamed = [b for b, c in enumerate(self.caches) if c.evicted_chunks > 0]
+        ctx = [0 if b in self.streamed else p + 1 for b, p in enumerate(self.positions)]
+        self.ctx_resident = torch.tensor(ctx, dtype=torch.int32, device=self.device)
+
+    def attend(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        from .exec.attention import host_stream_attention_v1
+
+        gpu = self.store.gpu
+        kernels.kv_index_copy(gpu.k_phys, gpu.v_phys, k_new, v_new, self.slots[layer])
+        # streamed requests get ctx 0 here (zeros), then their host-stream result
+        out = kernels.paged_decode_attention(q, gpu.k_phys, gpu.v_phys, self.tables.tables[layer],
+                                             self.ctx_resident, out=out, workspace=self.workspace)
+        B, Hq, D = q.shape
+        for b in self.streamed:
+            chunks, rk, rv = self.store.host_stream_chunks(self.caches[b], layer,
+                                                           self.tables.tables[layer, b])
+            o = host_stream_attention_v1(q[b].view(1, 1, Hq, D), chunks, rk, rv,
+                                         q_start_pos=self.positions[b], causal=True)
+            out[b].copy_(o.view(Hq, D))
+        return out
+
+    def end_step(self) -> None:
+        for c in self.caches:
+            self.store.sink_completed_chunks_async(c)
+        self.evict_to(self.budget)
+
+    def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+             token_ids: list[int] | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The KV path of one whole step: q [L, B, Hq, D], k_new/v_new [L, B, Hkv, D]."""
+        self.begin_step(token_ids)
+        if out is None:
+            out = torch.empty_like(q)
+        for layer in range(q.shape[0]):
+            self.attend(layer, q[layer], k_new[layer], v_new[layer], out=out[layer])
+        self.end_step()
+        return out

@@ -43,6 +43,18 @@ def _chain(tokens: list[int], chunk_size: int, salt: bytes) -> tuple[list[ChunkK
     return keys, running
 
 
+def next_chunk_key(running: bytes | None, chunk_tokens: list[int],
+                   initial_salt: bytes = _INITIAL_SALT) -> ChunkKey:
+    """Key of the chunk that follows `running` (the previous chunk's cumulative key, or
+    None for the first chunk): the step of the chain above, so keys built one chunk at a
+    time equal compute_prefix_hashes over the whole sequence."""
+    if running is None:
+        running = hashlib.sha256(initial_salt).digest()
+    body = struct.pack(f"<{len(chunk_tokens)}I", *chunk_tokens)
+    return ChunkKey(prefix_key=running,
+                    cumulative_key=hashlib.sha256(running + hashlib.sha256(body).digest()).digest())
+
+
 def compute_prefix_hashes(tokens: list[int], chunk_size: int = DEFAULT_CHUNK_SIZE,
                           initial_salt: bytes = _INITIAL_SALT) -> list[ChunkKey]:
     return _chain(tokens, chunk_size, initial_salt)[0]

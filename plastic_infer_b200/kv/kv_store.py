@@ -36,7 +36,8 @@ from typing import Optional
 import torch
 
 from .. import kernels
-from .chunk import ChunkKey, compute_prefix_hashes_and_final, longest_prefix_hits
+from .chunk import (ChunkKey, compute_prefix_hashes_and_final, longest_prefix_hits,
+                    next_chunk_key)
 from .paged import DEFAULT_CHUNK_PAGES, DEFAULT_PAGE_SIZE, BlockTable, PageAllocator
 
 
@@ -113,6 +114,8 @@ class KVRequestCache:
         # Leading complete chunks whose device pages evict_chunks released: their K/V
         # live only in the host store, and their block-table entries are -1.
         self.evicted_chunks = 0
+        # token ids after the last complete chunk (extend_token_ids)
+        self._token_tail: list[int] = []
 
     @property
     def length(self) -> int:
@@ -153,6 +156,7 @@ class KVRequestCache:
 
     def set_token_ids(self, token_ids: list[int]) -> None:
         n_full = len(token_ids) // self.cfg.tokens_per_chunk
+        self._token_tail = list(token_ids[n_full * self.cfg.tokens_per_chunk:])
         if n_full == 0:
             self.chunk_keys = []
             self._final_hash = None
@@ -161,6 +165,22 @@ class KVRequestCache:
             token_ids[:n_full * self.cfg.tokens_per_chunk], chunk_size=self.cfg.tokens_per_chunk)
         self.chunk_keys = keys
         self._final_hash = final_h
+
+    def extend_token_ids(self, token_ids: list[int]) -> int:
+        """Append token ids (e.g. the ones a decode step generated) after those given so
+        far; every chunk they complete gets its key, the same key set_token_ids over the
+        whole sequence gives. Returns the number of chunk keys added (no reference
+        counterpart: the reference recomputes every key with set_token_ids)."""
+        tpc = self.cfg.tokens_per_chunk
+        self._token_tail.extend(int(t) for t in token_ids)
+        added = 0
+        while len(self._token_tail) >= tpc:
+            key = next_chunk_key(self._final_hash, self._token_tail[:tpc])
+            self.chunk_keys.append(key)
+            self._final_hash = key.cumulative_key
+            del self._token_tail[:tpc]
+            added += 1
+        return added
 
     def get_block_table_for_layer(self, layer: int) -> list[int]:
         return list(self.block_table.pages[layer])
@@ -205,6 +225,10 @@ class KVStore:
             (c.n_layers, c.n_kv_heads, c.tokens_per_chunk, c.head_dim), c.dtype, pin=on_cuda)
         self._copy_stream: Optional[torch.cuda.Stream] = (
             torch.cuda.Stream(device=self.gpu.device) if on_cuda else None)
+        # Sinks run on the side stream without blocking the caller: the event of the
+        # latest one, and per host chunk the event after which its buffer holds the data.
+        self._pending_sink: Optional[torch.cuda.Event] = None
+        self._host_ready: dict[bytes, torch.cuda.Event] = {}
 
     # -- request lifecycle -------------------------------------------------------
 
@@ -212,6 +236,7 @@ class KVStore:
         return KVRequestCache(self, request_id=request_id)
 
     def free_request(self, cache: KVRequestCache) -> None:
+        self._order_page_reuse()
         self.gpu.allocator.free_many([p for p in cache.block_table.all_page_ids() if p >= 0])
         for c in range(min(cache.evicted_chunks, len(cache.chunk_keys))):
             self._unpin_host(cache.chunk_keys[c].full_key)
@@ -237,7 +262,26 @@ class KVStore:
         cached chunks are only touched in the LRU, the host LRU is evicted to make
         room, and the return value counts newly sunk chunks. The copy is batched:
         one gather launch for all new chunks, one device->host copy per chunk on the
-        store's side stream; the call returns once the host copies are complete.
+        store's side stream; like the reference's, this call returns once the host
+        copies are complete (sink_completed_chunks_async does not wait).
+        """
+        n, ev = self.sink_completed_chunks_async(cache)
+        if ev is not None:
+            ev.synchronize()
+        return n
+
+    def sink_completed_chunks_async(self, cache: KVRequestCache
+                                    ) -> tuple[int, Optional[torch.cuda.Event]]:
+        """sink_completed_chunks without the wait (no reference counterpart).
+
+        The gather and the device->host copies are queued on the store's side stream,
+        after the work already queued on the current stream, and the call returns at
+        once with (newly sunk chunks, event); the new host chunks hold their data once
+        the event has completed. The store orders its own later work after it: attention
+        over the chunks (host_stream_chunks) waits for the event on the GPU, and device
+        pages freed by evict_chunks / free_request are reused only after the gather that
+        reads them. Code that reads `_host_cache` tensors on the host must wait for the
+        event first.
         """
         cfg = self.config
         todo: list[tuple[int, ChunkKey]] = []
@@ -260,18 +304,31 @@ class KVStore:
         # later one of the same call (more new chunks than max_host_chunks); the
         # reference copies and then drops it, here it is simply not copied.
         live = [(i, key) for i, key in todo if key.full_key in self._host_cache]
+        ev = None
         if live:
             page_ids: list[int] = []
             for chunk_idx, _ in live:
                 page_ids += self._chunk_page_list(cache, chunk_idx)
-            bufs = self._move_out(page_ids, len(live))
+            bufs, ev = self._move_out(page_ids, len(live))
             for (_, key), (kb, vb) in zip(live, bufs):
                 self._host_phys[key.full_key] = (kb, vb)
                 self._host_cache[key.full_key] = (kb.permute(0, 1, 3, 2), vb.permute(0, 1, 3, 2))
-        return len(todo)
+                self._host_ready[key.full_key] = ev
+            self._pending_sink = ev
+        return len(todo), ev
 
-    def _move_out(self, page_ids: list[int], n_chunks: int) -> list[tuple[torch.Tensor, torch.Tensor]]:
-        """Gather pages (ordered chunk, layer, page) into pinned chunk buffers."""
+    def _order_page_reuse(self) -> None:
+        """Before device pages are freed: later work on the current stream (which may
+        write into the pages once they are handed out again) waits for the side-stream
+        gathers of the sinks queued so far, which may still read them."""
+        if self._pending_sink is not None and self.gpu.device.type == "cuda":
+            torch.cuda.current_stream(self.gpu.device).wait_event(self._pending_sink)
+            self._pending_sink = None
+
+    def _move_out(self, page_ids: list[int], n_chunks: int
+                  ) -> tuple[list[tuple[torch.Tensor, torch.Tensor]], torch.cuda.Event]:
+        """Gather pages (ordered chunk, layer, page) into pinned chunk buffers, on the
+        side stream; returns the buffers and the event that completes the copies."""
         cfg = self.config
         dev = self.gpu.device
         if dev.type != "cuda":
@@ -290,10 +347,11 @@ class KVStore:
             for c, (kb, vb) in enumerate(outs):
                 kb.copy_(staging_k[c], non_blocking=True)
                 vb.copy_(staging_v[c], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(side)
         for t in (ids, staging_k, staging_v):
             t.record_stream(side)
-        side.synchronize()
-        return outs
+        return outs, ev
 
     # -- prefix loading (host -> device) ------------------------------------------
 
@@ -377,6 +435,7 @@ class KVStore:
         cfg = self.config
         cache = protected_request
         freed = 0
+        self._order_page_reuse()
         n_full = cache.num_complete_chunks()
         while cache.evicted_chunks < n_full - 1 and freed < need_pages:
             c = cache.evicted_chunks
@@ -396,7 +455,8 @@ class KVStore:
             cache.evicted_chunks += 1
         return freed
 
-    def host_stream_chunks(self, cache: KVRequestCache, layer: int
+    def host_stream_chunks(self, cache: KVRequestCache, layer: int,
+                           device_table: Optional[torch.Tensor] = None
                            ) -> tuple[list[tuple[torch.Tensor, torch.Tensor]], torch.Tensor, torch.Tensor]:
         """The KV of one layer of `cache` as host_stream_attention_v1 takes it.
 
@@ -404,21 +464,33 @@ class KVStore:
         of the request's evicted chunks, oldest first, as [H_kv, D, C] views of the
         pinned chunk buffers: the kernel reads them in place, nothing is copied back.
         resident_k / resident_v [1, R, H_kv, D] are the tokens still in the device pool,
-        gathered in one launch each.
+        gathered in one launch each. `device_table`, when given, is this layer's block
+        table row of the request already on the device (int32, at least as long as the
+        row; entries of evicted chunks are not read); otherwise the row is copied from
+        the host list.
         """
         cfg = self.config
         chunks: list[tuple[torch.Tensor, torch.Tensor]] = []
+        waited: list[torch.cuda.Event] = []
         for c in range(cache.evicted_chunks):
             key = cache.chunk_keys[c].full_key if c < len(cache.chunk_keys) else None
             kv = self._host_cache.get(key) if key is not None else None
             if kv is None or kv[0] is None:
                 raise RuntimeError(f"chunk {c} left the device pool without a host copy")
             chunks.append((kv[0][layer], kv[1][layer]))
+            ready = self._host_ready.get(key)
+            if ready is not None and ready not in waited:
+                # the kernel reads the host buffer in place: after its sink's copies
+                torch.cuda.current_stream(self.gpu.device).wait_event(ready)
+                waited.append(ready)
         start = cache.evicted_chunks * cfg.pages_per_chunk
-        table = cache.block_table.pages[layer][start:]
         n_tail = cache.length - cache.evicted_chunks * cfg.tokens_per_chunk
         dev = self.gpu.device
-        bt = torch.tensor(table if table else [0], dtype=torch.int32, device=dev)
+        if device_table is not None:
+            bt = device_table[start:]
+        else:
+            table = cache.block_table.pages[layer][start:]
+            bt = torch.tensor(table if table else [0], dtype=torch.int32, device=dev)
         rk = kernels.paged_kv_gather(self.gpu.k_phys, bt, n_tail).unsqueeze(0)
         rv = kernels.paged_kv_gather(self.gpu.v_phys, bt, n_tail).unsqueeze(0)
         return chunks, rk, rv
@@ -449,12 +521,17 @@ class KVStore:
             return False
         del self._host_lru[oldest]
         del self._host_cache[oldest]
+        self._host_ready.pop(oldest, None)
         self._prefix_index.pop(oldest, None)
         phys = self._host_phys.pop(oldest, None)
         if phys is not None:
             self._chunk_pool.give(phys[0])
             self._chunk_pool.give(phys[1])
         return True
+
+    def has_host_chunk(self, full_key: bytes) -> bool:
+        """Whether the host store holds (or is being sent) the chunk with this key."""
+        return full_key in self._host_cache
 
     @property
     def host_cache_size(self) -> int:

@@ -198,3 +198,28 @@ def test_streaming_an_unsunk_evicted_chunk_raises() -> None:
     assert store.evict_chunks(need_pages=1, protected_request=cache) == 4
     with pytest.raises(RuntimeError, match="without a host copy"):
         store.host_stream_chunks(cache, 0)
+
+
+def test_extend_token_ids_gives_the_keys_of_set_token_ids() -> None:
+    import numpy as np
+    import torch
+
+    from plastic_infer_b200.kv.kv_store import KVConfig, KVStore
+
+    cfg = KVConfig(n_layers=1, n_kv_heads=1, head_dim=8, page_size=4, pages_per_chunk=2,
+                   max_pages=8, device=torch.device("cpu"))
+    store = KVStore(cfg)
+    rng = np.random.default_rng(0)
+    ids = [int(x) for x in rng.integers(0, 2**32 - 1, 61, dtype=np.uint64)]
+    whole = store.new_request(0)
+    whole.set_token_ids(ids)
+    step = store.new_request(1)
+    step.set_token_ids(ids[:5])
+    cur, added = 5, 0
+    for n in (1, 2, 9, 1, 20, 23):
+        added += step.extend_token_ids(ids[cur:cur + n])
+        cur += n
+    assert cur == len(ids)
+    assert added == len(whole.chunk_keys) == 7
+    assert step.chunk_keys == whole.chunk_keys
+    assert step._final_hash == whole._final_hash
