@@ -125,3 +125,69 @@ def test_index_copy_misaligned_falls_back_to_narrow_vectors() -> None:
     kernels.kv_index_copy(kp, vp, new, -new, slots)
     assert torch.equal(kp[slots // S, :, slots % S, :], new)
     assert torch.equal(vp[slots // S, :, slots % S, :], -new)
+
+
+# Geometries that reach every launch shape of the kernel: one chunk per token (a single
+# KV head), a partial last chunk (3 heads x 10 vectors), rows whose vector count is not a
+# power of two (division path), two chunks per warp (whole 36-layer step in one launch)
+# and four chunks per pass with a grid-stride loop (65,536 tokens).
+GEOMETRIES = [
+    # name, pages, kv_heads, page_size, head_dim, dtype, tokens
+    ("c4_four_heads", 512, 4, 16, 128, torch.bfloat16, 128),
+    ("one_head", 256, 1, 16, 128, torch.bfloat16, 300),
+    ("d96_rows_of_12_vectors", 256, 8, 16, 96, torch.bfloat16, 200),
+    ("h3_d80_partial_chunk", 256, 3, 16, 80, torch.float16, 333),
+    ("d64_page32", 256, 8, 32, 64, torch.bfloat16, 1000),
+    ("f32_d64", 512, 2, 16, 64, torch.float32, 777),
+    ("whole_step_36_layers", 4096, 8, 16, 128, torch.bfloat16, 36 * 64),
+    ("large_65536", 8192, 8, 16, 128, torch.bfloat16, 65536),
+]
+
+
+@pytest.mark.parametrize("geom", GEOMETRIES, ids=[g[0] for g in GEOMETRIES])
+def test_index_copy_geometries_vs_oracle(geom) -> None:
+    name, P, H, S, D, dtype, B = geom
+    rng = np.random.default_rng(len(name) * 7919 + B)
+    init_k = _rand_rows(rng, (P, H, S, D), dtype)
+    init_v = _rand_rows(rng, (P, H, S, D), dtype)
+    kp, vp = init_k.to(DEV), init_v.to(DEV)
+    slots = rng.permutation(P * S)[:B].astype(np.int64)
+    slots[rng.random(B) < 0.05] = -1  # some padding tokens
+    k_new = _rand_rows(rng, (B, H, D), dtype)
+    v_new = _rand_rows(rng, (B, H, D), dtype)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kernels.kv_index_copy(kp, vp, k_new.to(DEV), v_new.to(DEV), torch.from_numpy(slots).to(DEV),
+                          err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    view = (lambda t: t.view(torch.int16).numpy()) if dtype != torch.float32 else (lambda t: t.numpy())
+    ek = view(init_k.permute(0, 1, 3, 2).contiguous()).copy()
+    ev = view(init_v.permute(0, 1, 3, 2).contiguous()).copy()
+    orc.write_kv_slots(ek, ev, view(k_new), view(v_new), slots, S)
+    assert np.array_equal(view(kp.permute(0, 1, 3, 2).contiguous().cpu()), ek)
+    assert np.array_equal(view(vp.permute(0, 1, 3, 2).contiguous().cpu()), ev)
+
+
+def test_index_copy_duplicate_slots_write_one_of_the_rows() -> None:
+    # Duplicate slots in one launch: each 16-byte piece holds the bytes of one of the
+    # duplicates (which one is unspecified); every other slot is exact.
+    P, H, S, D, B = 64, 8, 16, 128, 96
+    rng = np.random.default_rng(3)
+    slots = rng.permutation(P * S)[:B].astype(np.int64)
+    slots[50:60] = slots[0:10]
+    kp = torch.zeros((P, H, S, D), dtype=torch.bfloat16, device=DEV)
+    vp = torch.zeros_like(kp)
+    k_new = _rand_rows(rng, (B, H, D), torch.bfloat16).to(DEV)
+    v_new = _rand_rows(rng, (B, H, D), torch.bfloat16).to(DEV)
+    st = torch.from_numpy(slots).to(DEV)
+    kernels.kv_index_copy(kp, vp, k_new, v_new, st)
+    got_k = kp[st // S, :, st % S, :].view(B, -1, 8)   # 16-byte pieces
+    got_v = vp[st // S, :, st % S, :].view(B, -1, 8)
+    kk, vv = k_new.view(B, -1, 8), v_new.view(B, -1, 8)
+    for i in range(B):
+        j = i - 50 if 50 <= i < 60 else (i + 50 if i < 10 else i)
+        for got, src in ((got_k, kk), (got_v, vv)):
+            piece_ok = (got[i] == src[i]).all(-1) | (got[i] == src[j]).all(-1)
+            assert bool(piece_ok.all()), f"token {i}"
+            if j == i:
+                assert torch.equal(got[i], src[i])
