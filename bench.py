@@ -557,7 +557,8 @@ def bench_prefill(dev: torch.device, peaks: dict) -> dict:
     head_dim 128, 16-token pages, bf16): a first 4096-token prefill (causal from 0) and a
     1024-token chunk at position 3072 (the reference's offset-mask path). Ours against the
     reference's algorithm on the same GPU (page gather, repeat_interleave, SDPA with
-    is_causal or with its dense mask). FLOPs = 4 * D * Hq * sum of the rows' key counts.
+    is_causal or with its dense mask). Ours is timed on both kernels: tcgen05 (S and O in
+    tensor memory) and mma.sync. FLOPs = 4 * D * Hq * sum of the rows' key counts.
     """
     import torch.nn.functional as F
 
@@ -576,8 +577,11 @@ def bench_prefill(dev: torch.device, peaks: dict) -> dict:
         rows = torch.arange(q_start, q_start + q_len, dtype=torch.float64) + 1
         flops = 4.0 * D * Hq * float(rows.clamp(max=kv).sum())
 
-        def ours():
-            kernels.paged_prefill_attention(q, kp, vp, bt, kv, q_start, True)
+        def ours_tc():
+            kernels.paged_prefill_attention(q, kp, vp, bt, kv, q_start, True, impl="tc")
+
+        def ours_mma():
+            kernels.paged_prefill_attention(q, kp, vp, bt, kv, q_start, True, impl="mma")
 
         def reference():
             k = kp[bt.long()].permute(0, 2, 1, 3).reshape(-1, Hkv, D)[:kv]
@@ -593,15 +597,18 @@ def bench_prefill(dev: torch.device, peaks: dict) -> dict:
             return F.scaled_dot_product_attention(qt, kt, vt, attn_mask=am[None, None])
 
         entry = dict(q_len=q_len, q_start=q_start, kv_len=kv, gflop=round(flops / 1e9, 1))
-        for label, fn in (("ours", ours), ("reference_algorithm", reference)):
+        for label, fn in (("ours_tc", ours_tc), ("ours_mma", ours_mma),
+                          ("reference_algorithm", reference)):
             for _ in range(3):
                 fn()
             torch.cuda.synchronize()
             reps = 10
             us = time_region(fn, reps, torch.cuda.current_stream()) / reps * 1e3
             entry[label] = dict(us=round(us, 1), tflops=round(flops / (us * 1e-6) / 1e12, 1))
-        entry["speedup"] = round(entry["reference_algorithm"]["us"] / entry["ours"]["us"], 2)
-        entry["ours"]["frac_of_bf16_peak"] = round(entry["ours"]["tflops"] / peaks["bf16_tflops"], 3)
+        for label in ("ours_tc", "ours_mma"):
+            entry[label]["speedup_vs_reference_algorithm"] = round(
+                entry["reference_algorithm"]["us"] / entry[label]["us"], 2)
+            entry[label]["frac_of_bf16_peak"] = round(entry[label]["tflops"] / peaks["bf16_tflops"], 3)
         res[name] = entry
     return res
 

@@ -316,6 +316,22 @@ int pi_paged_prefill_attn(void* out, const void* q, const void* k_pool, const vo
                           cudaStream_t stream);
 
 /*
+ * pi_paged_prefill_attn on the 5th-generation tensor cores (tcgen05): same arguments,
+ * semantics, shape coverage and errors, plus q must be 16-byte aligned with
+ * q_tok_stride a multiple of 8 elements (PI_ERR_MISALIGNED otherwise). A CTA takes 128
+ * query rows of one KV head; S = Q K^T and O = P V accumulate in tensor memory, K/V
+ * pages stream through a TMA ring, every wait is bounded (PI_ERR_TIMEOUT through `err`).
+ * Same replaced reference code as pi_paged_prefill_attn
+ * (src/plastic_infer/exec/runner_paged.py:36-95).
+ */
+int pi_paged_prefill_attn_tc(void* out, const void* q, const void* k_pool, const void* v_pool,
+                             const int32_t* block_table, int64_t table_len, int q_len,
+                             int kv_len, int q_start, int causal, int num_q_heads,
+                             int num_kv_heads, int head_dim, int page_size, int64_t num_pages,
+                             float scale, int dtype, int64_t q_tok_stride,
+                             int64_t out_tok_stride, int* err, cudaStream_t stream);
+
+/*
  * One span of a KV sequence for pi_host_stream_attn: `len` tokens whose K element
  * (kv head h, token t, dim d) is k[h * head_stride + t * tok_stride + d * dim_stride]
  * (V the same with v). k and v point to device memory or to page-locked host memory

@@ -89,6 +89,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i64,
          _f32, _i32, _i64, _i64, _vp, _vp],
     ),
+    # same arguments as pi_paged_prefill_attn (tcgen05 kernel)
+    "pi_paged_prefill_attn_tc": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i64,
+         _f32, _i32, _i64, _i64, _vp, _vp],
+    ),
     # dst_ptrs, src_ptrs, feat_bytes, num_banks, dst_indices, src_indices, length,
     # num_indices, use_int32, err, stream
     "pi_expert_slot_copy": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _i64, _vp, _i32, _vp, _vp]),

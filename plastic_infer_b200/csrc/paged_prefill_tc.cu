@@ -287,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++issued;
     }
     // ---- online softmax of this row
+    __syncwarp();  // warp 0 converged again after thread 0's TMA issue: the loads are .aligned
     float sv[kN];
 #pragma unroll
     for (int c = 0; c < kN / 32; ++c) tmem_ld32(t_row + 32 * c, sv + 32 * c);
@@ -361,8 +362,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = consumed; j < issued; ++j)
         mbar_wait_bounded(smem_u32(bars + (j % kStages)), static_cast<uint32_t>((j / kStages) & 1));
     }
-  } else if (tok < p.q_len) {
-    T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(tok) * p.out_tok_stride +
+  } else {
+    // The TMEM loads are warp-collective (.sync.aligned): every thread of the CTA runs
+    // them on the same path, rows past q_len included (a warp can straddle q_len); only
+    // the stores depend on the row.
+    const bool row_valid = tok < p.q_len;
+    T* orow = static_cast<T*>(p.out) +
+              static_cast<int64_t>(row_valid ? tok : 0) * p.out_tok_stride +
               static_cast<int64_t>(h * G + r % G) * D;
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll
@@ -375,17 +381,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) ov[e] = 0.f;
       }
+      if (row_valid) {
 #pragma unroll
-      for (int e = 0; e < 32; e += 2)
-        *reinterpret_cast<uint32_t*>(orow + 32 * c + e) = MmaOp<T>::pack(ov[e] * inv, ov[e + 1] * inv);
-    }
-  } else if (n_tiles > 0) {
-    // rows past q_len still take part in the warp-collective TMEM loads above
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float ov[32];
-      tmem_ld32(t_row + kOCol + 32 * c, ov);
-      tmem_wait_ld();
+        for (int e = 0; e < 32; e += 2)
+          *reinterpret_cast<uint32_t*>(orow + 32 * c + e) =
+              MmaOp<T>::pack(ov[e] * inv, ov[e + 1] * inv);
+      }
     }
   }
   tc_fence_before();

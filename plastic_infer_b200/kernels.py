@@ -532,6 +532,7 @@ def paged_prefill_attention(
     scale: float | None = None,
     out: torch.Tensor | None = None,
     err: torch.Tensor | None = None,
+    impl: str = "mma",
 ) -> torch.Tensor:
     """Prefill attention of one request's q [q_len, Hq, D] (or [1, q_len, Hq, D]) over the
     first kv_len tokens of its pages (block_table: int32 [n] page ids, device).
@@ -539,8 +540,11 @@ def paged_prefill_attention(
     Query i sits at position q_start + i; with `causal` it sees keys j <= q_start + i
     (the reference's is_causal when q_start == 0, its offset mask otherwise:
     src/plastic_infer/exec/runner_paged.py:36-95). Returns [q_len, Hq, D] in the pool dtype
-    (the input's leading batch axis is kept when given).
+    (the input's leading batch axis is kept when given). `impl` picks the kernel: "tc"
+    (tcgen05, S and O in tensor memory) or "mma" (mma.sync, accumulators in registers).
     """
+    if impl not in ("tc", "mma"):
+        raise ValueError(f"impl must be 'tc' or 'mma', got {impl!r}")
     P, Hkv, S, D = _check_pool(k_pool, "k_pool")
     if v_pool.shape != k_pool.shape or v_pool.dtype != k_pool.dtype:
         raise ValueError("k_pool and v_pool must have the same shape and dtype")
@@ -574,8 +578,10 @@ def paged_prefill_attention(
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     block_table = block_table.contiguous()
+    if impl == "tc" and (q3.data_ptr() % 16 or q3.stride(0) % 8):
+        q3 = q3.contiguous()  # the tcgen05 kernel reads q rows as 16-byte vectors
     _capi.call(
-        "pi_paged_prefill_attn",
+        "pi_paged_prefill_attn_tc" if impl == "tc" else "pi_paged_prefill_attn",
         out3.data_ptr(), q3.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_table.data_ptr(), block_table.numel(), q_len, int(kv_len), int(q_start),
         1 if causal else 0, Hq, Hkv, D, S, P, float(scale), dtype_code(k_pool.dtype),

@@ -51,7 +51,7 @@ def test_exports_are_the_declared_symbols(lib: ctypes.CDLL) -> None:
     out = subprocess.run([nm, "-D", "--defined-only", str(_capi.lib_path())], capture_output=True,
                          text=True, check=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T pi_" in line}
-    assert exported == set(declared_functions()) | {"pi_paged_prefill_attn_tc"}
+    assert exported == set(declared_functions())
 
 
 def test_version_and_strings(lib: ctypes.CDLL) -> None:

@@ -1,4 +1,5 @@
-"""GPU parity of paged prefill attention (pi_paged_prefill_attn).
+"""GPU parity of paged prefill attention (pi_paged_prefill_attn and its tcgen05 twin
+pi_paged_prefill_attn_tc; every case runs on both).
 
 One request's q_len new tokens attend, straight from the page pool, to the first kv_len
 tokens of their pages: causally from position q_start (the reference's is_causal path
@@ -68,8 +69,12 @@ def _setup(q_len, kv_len, Hq, Hkv, D, S, dtype, seed, poison=False, k_rows=None,
     return q_d, kp_d, vp_d, torch.from_numpy(table).to(DEV), lk, lv, list(table)
 
 
+IMPLS = ["mma", "tc"]  # mma.sync kernel, tcgen05 kernel (S and O in tensor memory)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
 @pytest.mark.parametrize("case", PREFILL_CASES, ids=[c["name"] for c in PREFILL_CASES])
-def test_prefill_matches_reference_golden(case: dict) -> None:
+def test_prefill_matches_reference_golden(case: dict, impl: str) -> None:
     g = np.load(GOLD / "prefill.npz")
     n = case["name"]
     x = prefill_inputs(case)
@@ -77,7 +82,7 @@ def test_prefill_matches_reference_golden(case: dict) -> None:
                                           case["D"], case["S"], torch.bfloat16, 0, k_rows=x["k"],
                                           v_rows=x["v"], q=x["q"], table=g[n + "__table"])
     out = kernels.paged_prefill_attention(q, kp, vp, bt, case["kv_len"], case["q_start"],
-                                          case["causal"])
+                                          case["causal"], impl=impl)
     torch.cuda.synchronize()
     got = out.float().cpu().numpy()
     ref = orc.paged_attention_prefill(q.float().cpu().numpy(), lk, lv, table, case["kv_len"],
@@ -99,11 +104,13 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("impl", IMPLS)
 @pytest.mark.parametrize("q_len,kv_len,q_start,causal,Hq,Hkv,D,S,dtype", CASES)
-def test_prefill_vs_oracle(q_len, kv_len, q_start, causal, Hq, Hkv, D, S, dtype) -> None:
+def test_prefill_vs_oracle(q_len, kv_len, q_start, causal, Hq, Hkv, D, S, dtype, impl) -> None:
     q, kp, vp, bt, lk, lv, table = _setup(q_len, kv_len, Hq, Hkv, D, S, dtype, seed=q_len + kv_len,
                                           poison=True)
-    out = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start, causal)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start, causal, err=err, impl=impl)
     torch.cuda.synchronize()
     lk = np.nan_to_num(lk)  # the oracle reads only context rows; the NaNs are past kv_len
     lv = np.nan_to_num(lv)
@@ -111,33 +118,63 @@ def test_prefill_vs_oracle(q_len, kv_len, q_start, causal, Hq, Hkv, D, S, dtype)
                                       causal, S)
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all()
+    assert int(err.item()) == 0
     _close(got, ref)
 
 
-def test_prefill_strided_q_out_param_and_empty_context() -> None:
+# Larger shapes for the tcgen05 kernel: many 128-key tiles through the 2-stage ring,
+# several query blocks per KV head, a q block that straddles q_len inside a warp.
+TC_CASES = [
+    # (q_len, kv_len, q_start, causal, Hq, Hkv, D, S, dtype)
+    (1024, 4096, 3072, True, 32, 8, 128, 16, torch.bfloat16),   # chunk of a 4k prefill
+    (1000, 1000, 0, True, 32, 8, 128, 16, torch.bfloat16),      # first prefill, ragged
+    (77, 2500, 1200, False, 16, 16, 64, 32, torch.float16),     # non-causal, MHA, f16
+    (200, 3000, 2800, True, 32, 2, 128, 32, torch.bfloat16),    # G = 16, 32-token pages
+]
+
+
+@pytest.mark.parametrize("q_len,kv_len,q_start,causal,Hq,Hkv,D,S,dtype", TC_CASES)
+def test_prefill_tc_long_contexts_vs_oracle(q_len, kv_len, q_start, causal, Hq, Hkv, D, S,
+                                            dtype) -> None:
+    q, kp, vp, bt, lk, lv, table = _setup(q_len, kv_len, Hq, Hkv, D, S, dtype, seed=kv_len,
+                                          poison=True)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start, causal, err=err,
+                                          impl="tc")
+    torch.cuda.synchronize()
+    ref = orc.paged_attention_prefill(q.float().cpu().numpy(), np.nan_to_num(lk),
+                                      np.nan_to_num(lv), table, kv_len, q_start, causal, S)
+    assert int(err.item()) == 0
+    _close(out.float().cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_prefill_strided_q_out_param_and_empty_context(impl: str) -> None:
     q_len, kv_len, Hq, Hkv, D, S = 48, 100, 16, 4, 128, 16
     q, kp, vp, bt, lk, lv, table = _setup(q_len, kv_len, Hq, Hkv, D, S, torch.bfloat16, seed=7)
     qkv = torch.zeros((q_len, (Hq + 2 * Hkv) * D), dtype=torch.bfloat16, device=DEV)
     qkv[:, :Hq * D] = q.reshape(q_len, Hq * D)
     q_view = qkv[:, :Hq * D].view(q_len, Hq, D)
     out = torch.full((q_len, Hq, D), 7.0, dtype=torch.bfloat16, device=DEV)
-    kernels.paged_prefill_attention(q_view, kp, vp, bt, kv_len, q_start=52, causal=True, out=out)
-    ref = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start=52, causal=True)
+    kernels.paged_prefill_attention(q_view, kp, vp, bt, kv_len, q_start=52, causal=True, out=out,
+                                    impl=impl)
+    ref = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start=52, causal=True, impl=impl)
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
     # no context: zeros
-    empty = kernels.paged_prefill_attention(q, kp, vp, bt[:0], 0, q_start=0, causal=True)
+    empty = kernels.paged_prefill_attention(q, kp, vp, bt[:0], 0, q_start=0, causal=True, impl=impl)
     torch.cuda.synchronize()
     assert int(torch.count_nonzero(empty)) == 0
 
 
-def test_prefill_matches_reference_algorithm_on_gpu() -> None:
+@pytest.mark.parametrize("impl", IMPLS)
+def test_prefill_matches_reference_algorithm_on_gpu(impl: str) -> None:
     # the reference's path (gather, repeat_interleave, SDPA with its offset mask) on the GPU
     import torch.nn.functional as F
 
     q_len, kv_len, q_start, Hq, Hkv, D, S = 96, 160, 64, 32, 8, 128, 16
     q, kp, vp, bt, lk, lv, table = _setup(q_len, kv_len, Hq, Hkv, D, S, torch.bfloat16, seed=11)
-    out = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start, True)
+    out = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start, True, impl=impl)
     kk = kp[bt.long()].permute(0, 2, 1, 3).reshape(-1, Hkv, D)[:kv_len]
     vv = vp[bt.long()].permute(0, 2, 1, 3).reshape(-1, Hkv, D)[:kv_len]
     G = Hq // Hkv
