@@ -7,20 +7,25 @@
 //   lim(i) = min(kv_len, q_start + i + 1) when causal, kv_len otherwise.
 //
 // CTA = (block of 128 / G query tokens, KV head): 128 query rows, row r = token * G + g,
-// one row per thread and per TMEM lane. The context streams in tiles of 128 keys (128 / S
-// pages, TMA, 2-stage ring). Per tile:
-//   1. one thread issues S = Q K^T: tcgen05.mma kind::f16, M = 128, N = 128, K = 16 steps,
+// one row per thread and per TMEM lane. The context streams in tiles of 64 keys (64 / S
+// pages by TMA): K and V each through a 2-slot ring. Per tile:
+//   1. one thread issues S = Q K^T: tcgen05.mma kind::f16, M = 128, N = 64, K = 16 steps,
 //      A = Q and B = the K tile, both K-major with the 128-byte swizzle; S lands in TMEM
-//      columns [0, 128);
-//   2. every thread reads its row of S from TMEM (tcgen05.ld 32x32b), masks it, and
-//      runs the online softmax in base 2; P goes to shared memory as T, swizzled K-major;
-//      the row's O (TMEM columns [128, 128 + D)) is rescaled when its maximum moved;
+//      columns [0, 64);
+//   2. every thread reads its row of S (tcgen05.ld 32x32b), masks it and runs the online
+//      softmax in base 2; P goes to shared memory, swizzled K-major. The running maximum
+//      moves only when a row's new maximum exceeds it by more than 2^8, so P <= 256 and O
+//      (TMEM) is rescaled on those rare tiles only; the stale maximum cancels in O / l;
 //   3. one thread issues O += P V: A = P (K-major), B = the V tile, MN-major (its rows are
 //      head_dim-contiguous per key).
-// tcgen05.commit on an mbarrier marks the end of each tile's MMAs; waiting for the next
-// tile's S also covers the previous P V, so the K/V stage and P are free at that point.
-// V rows past the context in the last tile are zeroed before P V (an unused slot may hold
-// NaN, and 0 * NaN is NaN). Every wait is bounded: a timeout sets PI_ERR_TIMEOUT, the CTA
+// K(j + 2) and V(j + 1) load while tile j computes; thread 0 reads the page ids of a tile
+// one iteration before it issues the tile's loads. The CTA needs 113 KB of shared memory
+// at head_dim 128, so two CTAs share an SM and one CTA's softmax runs under the other's
+// MMAs. tcgen05.commit on an mbarrier marks
+// the end of each tile's S (and of every earlier MMA: they complete in order). V rows past
+// the context in the last tile are zeroed before P V (an unused slot may hold NaN, and
+// 0 * NaN is NaN). Warp-collective tcgen05 loads and stores always run on a path every
+// thread of the warp takes. Every wait is bounded: a timeout sets PI_ERR_TIMEOUT, the CTA
 // drains its loads and MMAs, frees its TMEM and exits.
 #include <cudaTypedefs.h>
 
@@ -40,23 +45,29 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kM = 128;       // query rows per CTA = TMEM lanes
-constexpr int kN = 128;       // keys per tile
-constexpr int kStages = 2;
-constexpr uint32_t kTmemCols = 256;  // S in [0, 128), O in [128, 128 + D)
-constexpr uint32_t kOCol = 128;
+constexpr int kN = 64;        // keys per tile
+constexpr int kKSlots = 2;    // K ring
+constexpr int kVSlots = 2;    // V ring
+constexpr uint32_t kOCol = 64;  // S in TMEM columns [0, 64), O in [64, 64 + D)
+constexpr float kRescaleLog2 = 8.0f;  // a row's running maximum moves by more than this only
 
 template <int D, int S>
 struct Cfg {
-  static constexpr int kBoxes = D / 64;                 // 64-element (128-byte) column boxes
-  static constexpr int kBoxRows = 128;                  // rows of every tile (kM == kN)
-  static constexpr int kBoxBytes = kBoxRows * 128;
-  static constexpr int kQBytes = kBoxes * kBoxBytes;    // Q tile [boxes][128 rows][128 B]
-  static constexpr int kKVBytes = kBoxes * kBoxBytes;   // K or V tile [boxes][128 keys][128 B]
-  static constexpr int kStageBytes = 2 * kKVBytes;
-  static constexpr int kPBytes = 2 * kBoxBytes;         // P [2 boxes of 64 keys][128 rows][128 B]
+  static constexpr int kBoxes = D / 64;                   // 64-element (128-byte) column boxes
+  static constexpr int kQBoxBytes = kM * 128;
+  static constexpr int kKVBoxBytes = kN * 128;
+  static constexpr int kQBytes = kBoxes * kQBoxBytes;     // Q tile [boxes][128 rows][128 B]
+  static constexpr int kKVBytes = kBoxes * kKVBoxBytes;   // K or V tile [boxes][64 keys][128 B]
+  static constexpr int kPBytes = kM * 128;                // P [128 rows][64 keys] bf16: one box
   static constexpr int kPagesPerTile = kN / S;
-  static constexpr int kSmem = 1024 /* alignment */ + kQBytes + kStages * kStageBytes + kPBytes +
-                               (kStages + 1) * 8 /* mbarriers */ + 16 /* TMEM address */;
+  static constexpr uint32_t kTmemCols = kOCol + D <= 128 ? 128 : 256;
+  static constexpr int kBarBytes = 64;                    // 5 mbarriers + TMEM address
+  static constexpr int kLayoutBytes = kQBytes + (kKSlots + kVSlots) * kKVBytes + kPBytes + kBarBytes;
+  // Slack for aligning the tiles to 1024 bytes (the 128-byte swizzle's period). 896 bytes
+  // covers any base aligned to 128 bytes and keeps two head_dim-128 CTAs on one SM (228 KB,
+  // 1 KB reserved per CTA); the kernel checks the fit and reports PI_ERR_MISALIGNED if not.
+  static constexpr int kSlack = 896;
+  static constexpr int kSmem = kSlack + kLayoutBytes;
 };
 
 struct Params {
@@ -139,35 +150,43 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int ch) {
 }
 
 template <typename T, int D, int S>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                             const __grid_constant__ CUtensorMap tmap_v, const Params p) {
   using C = Cfg<D, S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* qs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
-  uint8_t* kv = qs + C::kQBytes;                     // stage s: K at s * kStageBytes, then V
-  uint8_t* ps = kv + kStages * C::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + C::kPBytes);  // [kStages] loads, [kStages] MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kStages + 1);
+  uint8_t* ks = qs + C::kQBytes;                    // K slot s at s * kKVBytes
+  uint8_t* vs = ks + kKSlots * C::kKVBytes;         // V slot s at s * kKVBytes
+  uint8_t* ps = vs + kVSlots * C::kKVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + C::kPBytes);  // K[0..1], V[0..1], MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kKSlots + kVSlots + 1);
+  if ((qs - smem_raw) + C::kLayoutBytes > C::kSmem) {  // CTA-uniform: the base is too unaligned
+    if (threadIdx.x == 0) record_error(p.err, PI_ERR_MISALIGNED);
+    return;
+  }
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int G = p.group;
   const int h = blockIdx.y;
-  const int t0 = blockIdx.x * p.tokens_per_cta;
+  // causal: the latest (heaviest) query blocks first
+  const int qblk = p.causal ? static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x)
+                            : static_cast<int>(blockIdx.x);
+  const int t0 = qblk * p.tokens_per_cta;
   const int t_end = min(p.q_len, t0 + p.tokens_per_cta);
   // keys any row of this CTA may see
   const int kv_hi = p.causal ? min(p.kv_len, p.q_start + t_end) : p.kv_len;
   const int n_tiles = kv_hi > 0 ? (kv_hi + kN - 1) / kN : 0;
   const int n_pages = (kv_hi + S - 1) / S;
-  const uint32_t mma_bar = smem_u32(bars + kStages);
+  const uint32_t mma_bar = smem_u32(bars + kKSlots + kVSlots);
 
   pdl_trigger();
   pdl_wait();
 
   if (tid == 0) {
-    for (int s = 0; s <= kStages; ++s) mbar_init(smem_u32(bars + s), 1);
+    for (int b = 0; b < kKSlots + kVSlots + 1; ++b) mbar_init(smem_u32(bars + b), 1);
     fence_mbar_init();
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
@@ -175,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+                 "r"(C::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -198,32 +217,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * warp) << 16);  // this warp's lanes
 
-  // Loads of tile j into stage j % kStages (thread 0); returns the pages issued.
-  auto issue_tile = [&](int j) {
-    const int s = j % kStages;
-    const uint32_t bar = smem_u32(bars + s);
-    const uint32_t kdst = smem_u32(kv + s * C::kStageBytes);
-    const uint32_t vdst = kdst + C::kKVBytes;
+  // Page ids of tile j (thread 0). They are fetched one iteration before the loads that use
+  // them, so the TMA issue never waits on a block-table read.
+  auto fetch_ids = [&](int j, int (&ids)[C::kPagesPerTile]) {
+#pragma unroll
+    for (int pp = 0; pp < C::kPagesPerTile; ++pp) {
+      const int pg = j * C::kPagesPerTile + pp;
+      ids[pp] = (j < n_tiles && pg < n_pages) ? p.block_table[pg] : 0;
+    }
+  };
+  // K (kind 0) or V (kind 1) of tile j into `dst`, completing on `bar` (thread 0).
+  auto issue_load = [&](int j, int kind, uint32_t dst, uint32_t bar, const int (&ids)[C::kPagesPerTile]) {
     const int pg0 = j * C::kPagesPerTile;
     const int np = min(C::kPagesPerTile, n_pages - pg0);
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(np * 2 * C::kBoxes * S * 128));
-    for (int pp = 0; pp < np; ++pp) {
-      int pid = p.block_table[pg0 + pp];
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(np * C::kBoxes * S * 128));
+#pragma unroll
+    for (int pp = 0; pp < C::kPagesPerTile; ++pp) {
+      if (pp >= np) break;
+      int pid = ids[pp];
       if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
         record_error(p.err, PI_ERR_PAGE_RANGE);
         pid = 0;
       }
       const int row = (pid * p.hkv + h) * S;
 #pragma unroll
-      for (int b = 0; b < C::kBoxes; ++b) {
-        tma_load_2d(kdst + b * C::kBoxBytes + pp * S * 128, &tmap_k, bar, 64 * b, row);
-        tma_load_2d(vdst + b * C::kBoxBytes + pp * S * 128, &tmap_v, bar, 64 * b, row);
-      }
+      for (int b = 0; b < C::kBoxes; ++b)
+        tma_load_2d(dst + b * C::kKVBoxBytes + pp * S * 128, kind ? &tmap_v : &tmap_k, bar, 64 * b,
+                    row);
     }
   };
-  int issued = 0;  // tiles whose loads thread 0 has issued
-  if (tid == 0)
-    for (; issued < min(kStages, n_tiles); ++issued) issue_tile(issued);
+  const uint32_t k_addr0 = smem_u32(ks);
+  const uint32_t v_addr0 = smem_u32(vs);
+  int k_issued = 0, v_issued = 0;  // loads thread 0 has issued
+  // Thread 0's page ids: at the top of iteration j, ids_k holds tile j + 1's (for V(j + 1))
+  // and ids_n tile j + 2's (for K(j + 2)); ids_v serves the first tile's loads.
+  int ids_v[C::kPagesPerTile], ids_k[C::kPagesPerTile], ids_n[C::kPagesPerTile];
+  if (tid == 0) {
+    fetch_ids(0, ids_v);
+    fetch_ids(1, ids_k);
+    if (n_tiles > 0) issue_load(0, 0, k_addr0, smem_u32(bars + 0), ids_v);
+    if (n_tiles > 0) issue_load(0, 1, v_addr0, smem_u32(bars + kKSlots), ids_v);
+    if (n_tiles > 1) issue_load(1, 0, k_addr0 + C::kKVBytes, smem_u32(bars + 1), ids_k);
+    if (n_tiles > 1) issue_load(1, 1, v_addr0 + C::kKVBytes, smem_u32(bars + kKSlots + 1), ids_k);
+    k_issued = v_issued = min(2, n_tiles);
+    fetch_ids(2, ids_n);
+  }
 
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t id_s = umma::instr_desc_f16(kBf16, kM, kN, false, false);
@@ -237,39 +275,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   float m_run = -INFINITY;
   float l_run = 0.f;
   uint32_t mma_phase = 0;
-  int consumed = 0;  // tiles whose loads completed
+  int k_done = 0, v_done = 0;  // loads whose completion every thread has seen
   bool failed = false;
 
   for (int j = 0; j < n_tiles; ++j) {
-    const int s = j % kStages;
-    if (!mbar_wait_bounded(smem_u32(bars + s), static_cast<uint32_t>((j / kStages) & 1))) failed = true;
+    const int ksl = j % kKSlots;
+    if (!mbar_wait_bounded(smem_u32(bars + ksl), static_cast<uint32_t>((j / kKSlots) & 1)))
+      failed = true;
     if (__syncthreads_or(failed)) {
       failed = true;
       break;
     }
-    consumed = j + 1;
-    const int valid = min(kN, kv_hi - j * kN);
-    if (valid < kN) {  // zero the V rows past the context (they may hold NaN)
-      uint8_t* vt = kv + s * C::kStageBytes + C::kKVBytes;
-      const int per_box = (kN - valid) * 8;
-      for (int c = tid; c < C::kBoxes * per_box; c += kThreads) {
-        const int b = c / per_box;
-        const int rem = c - b * per_box;
-        *reinterpret_cast<uint4*>(vt + b * C::kBoxBytes + (valid + rem / 8) * 128 + (rem & 7) * 16) =
-            make_uint4(0u, 0u, 0u, 0u);
-      }
-      fence_proxy_async_smem();
-      __syncthreads();
-    }
-    // ---- S = Q K^T into TMEM columns [0, 128)
+    k_done = j + 1;
+    // ---- S = Q K^T into TMEM columns [0, 64)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t k_addr = smem_u32(kv + s * C::kStageBytes);
+      const uint32_t k_addr = k_addr0 + ksl * C::kKVBytes;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = static_cast<uint32_t>((kk >> 2) * C::kBoxBytes + (kk & 3) * 32);
-        umma_f16(tmem, umma::smem_desc(q_addr + off, 16, 1024, umma::kSwizzle128),
-                 umma::smem_desc(k_addr + off, 16, 1024, umma::kSwizzle128), id_s, kk > 0 ? 1u : 0u);
+        const uint32_t col = static_cast<uint32_t>((kk & 3) * 32);
+        umma_f16(tmem,
+                 umma::smem_desc(q_addr + (kk >> 2) * C::kQBoxBytes + col, 16, 1024, umma::kSwizzle128),
+                 umma::smem_desc(k_addr + (kk >> 2) * C::kKVBoxBytes + col, 16, 1024, umma::kSwizzle128),
+                 id_s, kk > 0 ? 1u : 0u);
       }
       umma_commit(mma_bar);
     }
@@ -280,17 +308,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       break;
     }
     tc_fence_after();
-    // S complete, and with it the previous tile's P V: tile j - 1's stage is free and takes
-    // tile j - 1 + kStages
-    if (tid == 0 && j >= 1 && issued == j - 1 + kStages && issued < n_tiles) {
-      issue_tile(issued);
-      ++issued;
-    }
-    // ---- online softmax of this row
-    __syncwarp();  // warp 0 converged again after thread 0's TMA issue: the loads are .aligned
-    float sv[kN];
+    // S(j) is done, and with it every earlier MMA (P V of tile j - 1): K slot j % 2 and V
+    // slot (j + 1) % 2 are free. Tile j + 2's K and V go out now (V(j + 2) needs the slot
+    // of V(j), read by P V(j) at the end of this tile: it goes out next iteration).
+    if (tid == 0) {
+      if (k_issued < n_tiles && k_issued == j + kKSlots) {
+        issue_load(k_issued, 0, k_addr0 + ksl * C::kKVBytes, smem_u32(bars + ksl), ids_n);
+        ++k_issued;
+      }
+      if (j >= 1 && v_issued < n_tiles && v_issued == j + 1) {
+        const int vsl = v_issued % kVSlots;
+        issue_load(v_issued, 1, v_addr0 + vsl * C::kKVBytes, smem_u32(bars + kKSlots + vsl), ids_k);
+        ++v_issued;
+      }
+      // ids_k held tile j + 1's ids, ids_n tile j + 2's; move on by one tile
 #pragma unroll
-    for (int c = 0; c < kN / 32; ++c) tmem_ld32(t_row + 32 * c, sv + 32 * c);
+      for (int pp = 0; pp < C::kPagesPerTile; ++pp) ids_k[pp] = ids_n[pp];
+      fetch_ids(j + 3, ids_n);
+    }
+    __syncwarp();  // warp 0 converged again after thread 0's issue: the loads are .aligned
+    // ---- online softmax of this row
+    float sv[kN];
+    tmem_ld32(t_row, sv);
+    tmem_ld32(t_row + 32, sv + 32);
     tmem_wait_ld();
     const int key0 = j * kN;
     float mt = -INFINITY;
@@ -299,8 +339,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       sv[c] = key0 + c < lim ? sv[c] * p.scale_log2 : -INFINITY;
       mt = fmaxf(mt, sv[c]);
     }
-    const float mn = fmaxf(m_run, mt);
-    const float alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mn);
+    // The running maximum moves only past a margin: P = 2^(s - m) stays <= 2^kRescaleLog2,
+    // and O needs rescaling only on the tiles where a row's maximum jumps.
+    float m_new = m_run;
+    bool rescale = false;
+    if (mt > m_run + kRescaleLog2) {
+      rescale = m_run != -INFINITY;  // before any key O is zero: nothing to rescale
+      m_new = mt;
+    }
+    const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
     float ls = 0.f;
 #pragma unroll
     for (int ch = 0; ch < kN / 8; ++ch) {
@@ -308,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float x = sv[ch * 8 + e];
-        pv[e] = x == -INFINITY ? 0.f : fast_exp2(x - mn);
+        pv[e] = x == -INFINITY ? 0.f : fast_exp2(x - m_new);
         ls += pv[e];
       }
       const uint4 packed = make_uint4(MmaOp<T>::pack(pv[0], pv[1]), MmaOp<T>::pack(pv[2], pv[3]),
@@ -316,9 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       *reinterpret_cast<uint4*>(ps + sw128_off(r, ch)) = packed;
     }
     l_run = l_run * alpha + ls;
-    m_run = mn;
-    // ---- O of earlier tiles, rescaled to this row's new maximum
-    if (j > 0) {
+    m_run = m_new;
+    // ---- O of earlier tiles, rescaled where a row's maximum moved (P V of tile j - 1 is
+    // complete). The TMEM loads are warp-collective: the whole warp takes the branch.
+    if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float ov[32];
@@ -330,19 +378,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_wait_st();
     }
-    fence_proxy_async_smem();  // P, written by the threads, is read by the MMA
+    // ---- V(j) in its slot; rows past the context zeroed (they may hold NaN)
+    const int vsl = j % kVSlots;
+    uint8_t* vs_j = vs + vsl * C::kKVBytes;
+    if (!mbar_wait_bounded(smem_u32(bars + kKSlots + vsl), static_cast<uint32_t>((j / kVSlots) & 1)))
+      failed = true;
+    if (__syncthreads_or(failed)) {
+      failed = true;
+      break;
+    }
+    v_done = j + 1;
+    const int valid = min(kN, kv_hi - key0);
+    if (valid < kN) {
+      const int per_box = (kN - valid) * 8;
+      for (int c = tid; c < C::kBoxes * per_box; c += kThreads) {
+        const int b = c / per_box;
+        const int rem = c - b * per_box;
+        *reinterpret_cast<uint4*>(vs_j + b * C::kKVBoxBytes + (valid + rem / 8) * 128 + (rem & 7) * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    fence_proxy_async_smem();  // P and the zeroed V rows are read by the MMA
     tc_fence_before();
     __syncthreads();
-    // ---- O += P V into TMEM columns [128, 128 + D)
+    // ---- O += P V into TMEM columns [64, 64 + D)
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t v_addr = smem_u32(kv + s * C::kStageBytes + C::kKVBytes);
 #pragma unroll
       for (int kk = 0; kk < kN / 16; ++kk) {
-        const uint64_t a = umma::smem_desc(p_addr + static_cast<uint32_t>((kk >> 2) * C::kBoxBytes + (kk & 3) * 32),
-                                           16, 1024, umma::kSwizzle128);
-        const uint64_t b = umma::smem_desc(v_addr + static_cast<uint32_t>(kk * 16 * 128),
-                                           C::kBoxBytes, 1024, umma::kSwizzle128);
+        const uint64_t a = umma::smem_desc(p_addr + static_cast<uint32_t>(kk * 32), 16, 1024,
+                                           umma::kSwizzle128);
+        const uint64_t b = umma::smem_desc(v_addr0 + static_cast<uint32_t>(vsl * C::kKVBytes + kk * 16 * 128),
+                                           C::kKVBoxBytes, 1024, umma::kSwizzle128);
         umma_f16(tmem + kOCol, a, b, id_o, (j > 0 || kk > 0) ? 1u : 0u);
       }
     }
@@ -359,8 +426,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
       record_error(p.err, PI_ERR_TIMEOUT);
       // loads still in flight must land before the CTA's shared memory is released
-      for (int j = consumed; j < issued; ++j)
-        mbar_wait_bounded(smem_u32(bars + (j % kStages)), static_cast<uint32_t>((j / kStages) & 1));
+      for (int j = k_done; j < k_issued; ++j)
+        mbar_wait_bounded(smem_u32(bars + (j % kKSlots)), static_cast<uint32_t>((j / kKSlots) & 1));
+      for (int j = v_done; j < v_issued; ++j)
+        mbar_wait_bounded(smem_u32(bars + kKSlots + (j % kVSlots)),
+                          static_cast<uint32_t>((j / kVSlots) & 1));
     }
   } else {
     // The TMEM loads are warp-collective (.sync.aligned): every thread of the CTA runs
@@ -393,7 +463,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(C::kTmemCols)
                  : "memory");
   }
 }

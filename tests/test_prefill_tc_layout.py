@@ -1,14 +1,15 @@
 """CPU check of the tcgen05 prefill kernel's addressing (csrc/paged_prefill_tc.cu).
 
-The kernel has not run on a GPU yet. This restates its layout constants and index
-arithmetic and checks, for every instantiated shape (head_dim 64/128, pages of 16/32)
-and a sweep of launch shapes, that:
-- every shared-memory offset it forms (Q, the K/V stages, TMA box destinations, P, the
-  V zeroing of the last tile, the MMA descriptor start addresses) stays inside its region,
-  and the regions fit the dynamic allocation it requests;
-- each tile's expect-tx byte count equals the bytes its TMA boxes deliver;
+This restates the kernel's layout constants and index arithmetic and checks, for every
+instantiated shape (head_dim 64/128, pages of 16/32) and a sweep of launch shapes, that:
+- every shared-memory offset it forms (Q, the K and V rings, TMA box
+  destinations, P, the V zeroing of the last tile, the MMA descriptor start addresses)
+  stays inside its region, the regions fit the dynamic allocation it requests, and two
+  CTAs of head_dim 128 fit on one SM (228 KB of shared memory, 1 KB reserved per CTA)
+  while their TMEM columns fit the SM's 512;
+- each load's expect-tx byte count equals the bytes its TMA boxes deliver;
 - every page id it reads lies inside block_table[0, ceil(kv_len / S));
-- the TMEM columns it uses fit the 256 it allocates.
+- the TMEM columns it uses fit the ones it allocates.
 The constants are restated here on purpose: a change on one side fails the check.
 """
 
@@ -22,22 +23,28 @@ import pytest
 
 SRC = pathlib.Path(__file__).resolve().parent.parent / "plastic_infer_b200" / "csrc" / "paged_prefill_tc.cu"
 
-KM = KN = 128
-STAGES = 2
-TMEM_COLS = 256
-O_COL = 128
+KM = 128
+KN = 64
+K_SLOTS = 2
+V_SLOTS = 2
+SLACK = 896
+O_COL = 64
+SM_SMEM = 228 * 1024
+TMEM_PER_SM = 512
 
 
 def cfg(D: int, S: int) -> dict:
     boxes = D // 64
-    box_bytes = 128 * 128
-    q_bytes = boxes * box_bytes
-    kv_bytes = boxes * box_bytes
-    stage = 2 * kv_bytes
-    p_bytes = 2 * box_bytes
-    smem = 1024 + q_bytes + STAGES * stage + p_bytes + (STAGES + 1) * 8 + 16
-    return dict(boxes=boxes, box=box_bytes, q=q_bytes, kv=kv_bytes, stage=stage, p=p_bytes,
-                pages_per_tile=KN // S, smem=smem)
+    q_box = KM * 128
+    kv_box = KN * 128
+    q_bytes = boxes * q_box
+    kv_bytes = boxes * kv_box
+    p_bytes = KM * 128
+    tmem_cols = 128 if O_COL + D <= 128 else 256
+    layout = q_bytes + (K_SLOTS + V_SLOTS) * kv_bytes + p_bytes + 64
+    smem = SLACK + layout
+    return dict(boxes=boxes, q_box=q_box, kv_box=kv_box, q=q_bytes, kv=kv_bytes, p=p_bytes,
+                pages_per_tile=KN // S, smem=smem, layout=layout, tmem_cols=tmem_cols)
 
 
 def sw128_off(r: int, ch: int) -> int:
@@ -46,46 +53,58 @@ def sw128_off(r: int, ch: int) -> int:
 
 def test_constants_match_the_kernel_source() -> None:
     src = SRC.read_text()
-    for name, val in (("kM", KM), ("kN", KN), ("kStages", STAGES)):
+    for name, val in (("kM", KM), ("kN", KN), ("kKSlots", K_SLOTS), ("kVSlots", V_SLOTS)):
         assert re.search(rf"constexpr int {name} = {val};", src), name
-    assert re.search(rf"constexpr uint32_t kTmemCols = {TMEM_COLS};", src)
     assert re.search(rf"constexpr uint32_t kOCol = {O_COL};", src)
+    assert re.search(rf"static constexpr int kSlack = {SLACK};", src)
+    assert "kOCol + D <= 128 ? 128 : 256" in src
+    assert "(kKSlots + kVSlots) * kKVBytes + kPBytes + kBarBytes" in src
 
 
 @pytest.mark.parametrize("D,S", list(itertools.product((64, 128), (16, 32))))
 def test_shared_memory_and_tmem_bounds(D: int, S: int) -> None:
     c = cfg(D, S)
     assert c["smem"] <= 227 * 1024
-    q0, kv0 = 0, c["q"]
-    p0 = kv0 + STAGES * c["stage"]
+    # CTAs per SM by shared memory, and their TMEM never exceeds the SM's 512 columns (so
+    # tcgen05.alloc never has to wait for another CTA's columns)
+    ctas = SM_SMEM // (c["smem"] + 1024)
+    assert ctas >= 2
+    assert ctas * c["tmem_cols"] <= TMEM_PER_SM
+    q0 = 0
+    k0 = q0 + c["q"]
+    v0 = k0 + K_SLOTS * c["kv"]
+    p0 = v0 + V_SLOTS * c["kv"]
     bars0 = p0 + c["p"]
-    slot0 = bars0 + (STAGES + 1) * 8
-    assert slot0 + 4 <= c["smem"] - 1024  # after the 1024-byte alignment slack
-    assert kv0 % 1024 == 0 and p0 % 1024 == 0 and c["stage"] % 1024 == 0
+    assert bars0 + (K_SLOTS + V_SLOTS + 1) * 8 + 4 <= c["layout"]
+    for off in (k0, v0, p0, c["kv"]):
+        assert off % 1024 == 0
+    # the layout fits after aligning any 128-byte aligned base up to 1024 bytes
+    assert all((-base) % 1024 + c["layout"] <= c["smem"] for base in range(0, 4096, 128))
     # Q writes: rows < 128, 16-byte chunks < D / 8
     assert max(sw128_off(r, ch) for r in range(KM) for ch in range(D // 8)) + 16 <= c["q"]
-    # P writes: 128 keys = 16 chunks per row
+    # P writes: 64 keys = 8 chunks per row, one box
     assert max(sw128_off(r, ch) for r in range(KM) for ch in range(KN // 8)) + 16 <= c["p"]
-    # TMA box destinations of one tile (K and V alike): box b, page pp
+    # TMA box destinations of one K or V tile: box b, page pp
     for pp in range(c["pages_per_tile"]):
         for b in range(c["boxes"]):
-            off = b * c["box"] + pp * S * 128
+            off = b * c["kv_box"] + pp * S * 128
             assert off % 1024 == 0 and off + S * 128 <= c["kv"]
-    # S = Q K^T descriptors: k step kk at box kk // 4, +32 B inside the 128-byte row
+    # S = Q K^T descriptors: k step kk at box kk // 4 (Q boxes 16 KB, K boxes 8 KB), +32 B
     for kk in range(D // 16):
-        off = (kk >> 2) * c["box"] + (kk & 3) * 32
-        assert off + 32 <= c["q"] and (off >> 4) < (1 << 14)
-    # O += P V: P (K-major) as above over 128 keys; V (MN-major) steps 16 keys = 2048 B,
+        q_off = (kk >> 2) * c["q_box"] + (kk & 3) * 32
+        k_off = (kk >> 2) * c["kv_box"] + (kk & 3) * 32
+        assert q_off + 32 <= c["q"] and k_off + 32 <= c["kv"]
+    # O += P V: P (K-major) over 64 keys in one box; V (MN-major) steps 16 keys = 2048 B,
     # its second 64-column block one box further (the leading byte offset)
     for kk in range(KN // 16):
-        assert (kk >> 2) * c["box"] + (kk & 3) * 32 + 32 <= c["p"]
+        assert kk * 32 + 32 <= 128
         v_off = kk * 16 * 128
-        assert v_off + 16 * 128 <= c["box"]
-        assert v_off + (c["boxes"] - 1) * c["box"] + 16 * 128 <= c["kv"]
+        assert v_off + 16 * 128 <= c["kv_box"]
+        assert v_off + (c["boxes"] - 1) * c["kv_box"] + 16 * 128 <= c["kv"]
     # descriptors hold addresses >> 4 in 14 bits: the whole allocation must stay below 256 KB
     assert c["smem"] < (1 << 18)
-    # TMEM: S in [0, 128), O in [128, 128 + D)
-    assert KN <= O_COL and O_COL + D <= TMEM_COLS
+    # TMEM: S in [0, 64), O in [64, 64 + D)
+    assert KN <= O_COL and O_COL + D <= c["tmem_cols"]
 
 
 @pytest.mark.parametrize("D,S", list(itertools.product((64, 128), (16, 32))))
@@ -99,7 +118,10 @@ def test_page_reads_tiles_and_expect_tx(D: int, S: int, G: int) -> None:
         (7, 0, 0, True), (200, 5000, 4800, True),
     ]:
         table_len = -(-kv_len // S)
-        for qb in range(-(-q_len // T)):
+        n_qblocks = -(-q_len // T)
+        for bx in range(n_qblocks):
+            qb = n_qblocks - 1 - bx if causal else bx   # heaviest block first when causal
+            assert 0 <= qb < n_qblocks
             t0 = qb * T
             t_end = min(q_len, t0 + T)
             kv_hi = min(kv_len, q_start + t_end) if causal else kv_len
@@ -110,16 +132,16 @@ def test_page_reads_tiles_and_expect_tx(D: int, S: int, G: int) -> None:
                 pg0 = j * c["pages_per_tile"]
                 np_ = min(c["pages_per_tile"], n_pages - pg0)
                 assert np_ >= 1 and pg0 + np_ <= n_pages
-                # expect-tx bytes == what the boxes deliver (K and V, every box, every page)
-                assert np_ * 2 * c["boxes"] * S * 128 == sum(
-                    S * 128 for _ in range(np_) for _ in range(c["boxes"]) for _ in range(2))
-                # last tile: V rows past the context are zeroed inside the V tile
+                # expect-tx bytes of one K (or V) load == what its boxes deliver
+                assert np_ * c["boxes"] * S * 128 == sum(
+                    S * 128 for _ in range(np_) for _ in range(c["boxes"]))
+                # last tile: V rows past the context are zeroed inside V(j)'s slot
                 valid = min(KN, kv_hi - j * KN)
                 assert 1 <= valid <= KN
                 per_box = (KN - valid) * 8
                 for cc in range(c["boxes"] * per_box):
                     b, rem = divmod(cc, per_box)
-                    off = b * c["box"] + (valid + rem // 8) * 128 + (rem & 7) * 16
+                    off = b * c["kv_box"] + (valid + rem // 8) * 128 + (rem & 7) * 16
                     assert off + 16 <= c["kv"]
             # a row's visible keys never exceed what the CTA loaded
             for r in range(KM):
@@ -127,3 +149,26 @@ def test_page_reads_tiles_and_expect_tx(D: int, S: int, G: int) -> None:
                 lim = min(kv_len, q_start + tok + 1) if causal else kv_len
                 if tok < q_len:
                     assert lim <= kv_hi
+
+
+def test_load_slots_phases_and_page_ids() -> None:
+    # K(t) in slot t % 2, V(t) in V slot t % 2 (phase (t // 2) & 1). Tiles 0 and 1 load in
+    # the prologue; after S(j) completes (and with it P V(j - 1)), K(j + 2) takes K(j)'s slot
+    # and V(j + 1) takes V(j - 1)'s. Thread 0's page ids: ids_k = tile j + 1, ids_n = tile
+    # j + 2 at the top of iteration j.
+    for n in range(0, 12):
+        k_issued = v_issued = min(2, n)
+        ids_k, ids_n = 1, 2
+        for j in range(n):
+            assert j < k_issued and j < v_issued  # tile j's K and V were issued before its waits
+            if k_issued < n and k_issued == j + K_SLOTS:
+                assert k_issued % K_SLOTS == j % K_SLOTS   # K(j) consumed by S(j): done
+                assert ids_n == k_issued
+                k_issued += 1
+            if j >= 1 and v_issued < n and v_issued == j + 1:
+                # V(j + 1)'s slot held V(j - 1), read by P V(j - 1): done before S(j)
+                assert v_issued % V_SLOTS == (j - 1) % V_SLOTS
+                assert ids_k == v_issued
+                v_issued += 1
+            ids_k, ids_n = ids_n, j + 3
+        assert k_issued == n and v_issued == n
