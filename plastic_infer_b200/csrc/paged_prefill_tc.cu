@@ -275,29 +275,30 @@ __global__ void __launch_bounds__(kThreads, 2)
   float m_run = -INFINITY;
   float l_run = 0.f;
   uint32_t mma_phase = 0;
-  int k_done = 0, v_done = 0;  // loads whose completion every thread has seen
+  int k_done = 0, v_done = 0;  // loads whose completion thread 0 has seen (for the drain)
   bool failed = false;
 
   for (int j = 0; j < n_tiles; ++j) {
     const int ksl = j % kKSlots;
-    if (!mbar_wait_bounded(smem_u32(bars + ksl), static_cast<uint32_t>((j / kKSlots) & 1)))
-      failed = true;
-    if (__syncthreads_or(failed)) {
-      failed = true;
-      break;
-    }
-    k_done = j + 1;
-    // ---- S = Q K^T into TMEM columns [0, 64)
+    // ---- S = Q K^T into TMEM columns [0, 64), issued once K(j) has landed. Only thread 0
+    // waits for the load; it commits even after a timeout (so the others' wait below ends)
+    // and its failure reaches every thread at the barrier after that wait.
     if (tid == 0) {
-      tc_fence_after();
-      const uint32_t k_addr = k_addr0 + ksl * C::kKVBytes;
+      if (!failed &&
+          mbar_wait_bounded(smem_u32(bars + ksl), static_cast<uint32_t>((j / kKSlots) & 1))) {
+        k_done = j + 1;
+        tc_fence_after();
+        const uint32_t k_addr = k_addr0 + ksl * C::kKVBytes;
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t col = static_cast<uint32_t>((kk & 3) * 32);
-        umma_f16(tmem,
-                 umma::smem_desc(q_addr + (kk >> 2) * C::kQBoxBytes + col, 16, 1024, umma::kSwizzle128),
-                 umma::smem_desc(k_addr + (kk >> 2) * C::kKVBoxBytes + col, 16, 1024, umma::kSwizzle128),
-                 id_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t col = static_cast<uint32_t>((kk & 3) * 32);
+          umma_f16(tmem,
+                   umma::smem_desc(q_addr + (kk >> 2) * C::kQBoxBytes + col, 16, 1024, umma::kSwizzle128),
+                   umma::smem_desc(k_addr + (kk >> 2) * C::kKVBoxBytes + col, 16, 1024, umma::kSwizzle128),
+                   id_s, kk > 0 ? 1u : 0u);
+        }
+      } else {
+        failed = true;
       }
       umma_commit(mma_bar);
     }
@@ -309,8 +310,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     tc_fence_after();
     // S(j) is done, and with it every earlier MMA (P V of tile j - 1): K slot j % 2 and V
-    // slot (j + 1) % 2 are free. Tile j + 2's K and V go out now (V(j + 2) needs the slot
-    // of V(j), read by P V(j) at the end of this tile: it goes out next iteration).
+    // slot (j + 1) % 2 are free, so K(j + 2) and V(j + 1) go out now.
     if (tid == 0) {
       if (k_issued < n_tiles && k_issued == j + kKSlots) {
         issue_load(k_issued, 0, k_addr0 + ksl * C::kKVBytes, smem_u32(bars + ksl), ids_n);
@@ -333,11 +333,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     tmem_ld32(t_row + 32, sv + 32);
     tmem_wait_ld();
     const int key0 = j * kN;
+    // Tiles whose keys this row sees in full (all but the causal diagonal and the last
+    // tile) skip the per-key mask: the raw maximum is scaled once and each P is one FMA
+    // and one exp2. Others mask by select and scale every score.
+    const bool fast = key0 + kN <= lim && p.scale_log2 > 0.f;
     float mt = -INFINITY;
+    if (fast) {
 #pragma unroll
-    for (int c = 0; c < kN; ++c) {
-      sv[c] = key0 + c < lim ? sv[c] * p.scale_log2 : -INFINITY;
-      mt = fmaxf(mt, sv[c]);
+      for (int c = 0; c < kN; ++c) mt = fmaxf(mt, sv[c]);
+      mt *= p.scale_log2;
+    } else {
+#pragma unroll
+      for (int c = 0; c < kN; ++c) {
+        sv[c] = key0 + c < lim ? sv[c] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, sv[c]);
+      }
     }
     // The running maximum moves only past a margin: P = 2^(s - m) stays <= 2^kRescaleLog2,
     // and O needs rescaling only on the tiles where a row's maximum jumps.
@@ -349,18 +359,35 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
     float ls = 0.f;
-#pragma unroll
-    for (int ch = 0; ch < kN / 8; ++ch) {
-      float pv[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float x = sv[ch * 8 + e];
-        pv[e] = x == -INFINITY ? 0.f : fast_exp2(x - m_new);
-        ls += pv[e];
-      }
+    auto store_p = [&](int ch, const float (&pv)[8]) {
       const uint4 packed = make_uint4(MmaOp<T>::pack(pv[0], pv[1]), MmaOp<T>::pack(pv[2], pv[3]),
                                       MmaOp<T>::pack(pv[4], pv[5]), MmaOp<T>::pack(pv[6], pv[7]));
       *reinterpret_cast<uint4*>(ps + sw128_off(r, ch)) = packed;
+    };
+    if (fast) {
+      const float neg_m = -m_new;  // finite: 64 visible keys
+#pragma unroll
+      for (int ch = 0; ch < kN / 8; ++ch) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = fast_exp2(fmaf(sv[ch * 8 + e], p.scale_log2, neg_m));
+          ls += pv[e];
+        }
+        store_p(ch, pv);
+      }
+    } else {
+#pragma unroll
+      for (int ch = 0; ch < kN / 8; ++ch) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x = sv[ch * 8 + e];
+          pv[e] = x == -INFINITY ? 0.f : fast_exp2(x - m_new);
+          ls += pv[e];
+        }
+        store_p(ch, pv);
+      }
     }
     l_run = l_run * alpha + ls;
     m_run = m_new;
@@ -378,18 +405,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       tmem_wait_st();
     }
-    // ---- V(j) in its slot; rows past the context zeroed (they may hold NaN)
+    // ---- V(j): on the last tile every thread waits for it and zeroes the rows past the
+    // context (they may hold NaN); otherwise only the MMA issuer waits, below.
     const int vsl = j % kVSlots;
-    uint8_t* vs_j = vs + vsl * C::kKVBytes;
-    if (!mbar_wait_bounded(smem_u32(bars + kKSlots + vsl), static_cast<uint32_t>((j / kVSlots) & 1)))
-      failed = true;
-    if (__syncthreads_or(failed)) {
-      failed = true;
-      break;
-    }
-    v_done = j + 1;
+    const uint32_t v_bar = smem_u32(bars + kKSlots + vsl);
+    const uint32_t v_parity = static_cast<uint32_t>((j / kVSlots) & 1);
     const int valid = min(kN, kv_hi - key0);
     if (valid < kN) {
+      if (!mbar_wait_bounded(v_bar, v_parity)) failed = true;
+      if (__syncthreads_or(failed)) {
+        failed = true;
+        break;
+      }
+      if (tid == 0) v_done = j + 1;
+      uint8_t* vs_j = vs + vsl * C::kKVBytes;
       const int per_box = (kN - valid) * 8;
       for (int c = tid; c < C::kBoxes * per_box; c += kThreads) {
         const int b = c / per_box;
@@ -403,14 +432,22 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     // ---- O += P V into TMEM columns [64, 64 + D)
     if (tid == 0) {
-      tc_fence_after();
+      if (valid == kN && !failed) {
+        if (mbar_wait_bounded(v_bar, v_parity))
+          v_done = j + 1;
+        else
+          failed = true;
+      }
+      if (!failed) {
+        tc_fence_after();
 #pragma unroll
-      for (int kk = 0; kk < kN / 16; ++kk) {
-        const uint64_t a = umma::smem_desc(p_addr + static_cast<uint32_t>(kk * 32), 16, 1024,
-                                           umma::kSwizzle128);
-        const uint64_t b = umma::smem_desc(v_addr0 + static_cast<uint32_t>(vsl * C::kKVBytes + kk * 16 * 128),
-                                           C::kKVBoxBytes, 1024, umma::kSwizzle128);
-        umma_f16(tmem + kOCol, a, b, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          const uint64_t a = umma::smem_desc(p_addr + static_cast<uint32_t>(kk * 32), 16, 1024,
+                                             umma::kSwizzle128);
+          const uint64_t b = umma::smem_desc(v_addr0 + static_cast<uint32_t>(vsl * C::kKVBytes + kk * 16 * 128),
+                                             C::kKVBoxBytes, 1024, umma::kSwizzle128);
+          umma_f16(tmem + kOCol, a, b, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
       }
     }
   }
