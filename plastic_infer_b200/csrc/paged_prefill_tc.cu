@@ -7,26 +7,26 @@
 //   lim(i) = min(kv_len, q_start + i + 1) when causal, kv_len otherwise.
 //
 // CTA = (block of 128 / G query tokens, KV head): 128 query rows, row r = token * G + g,
-// one row per thread and per TMEM lane. The context streams in tiles of 64 keys (64 / S
-// pages by TMA): K and V each through a 2-slot ring. Per tile:
-//   1. one thread issues S = Q K^T: tcgen05.mma kind::f16, M = 128, N = 64, K = 16 steps,
-//      A = Q and B = the K tile, both K-major with the 128-byte swizzle; S lands in TMEM
-//      columns [0, 64);
-//   2. every thread reads its row of S (tcgen05.ld 32x32b), masks it and runs the online
-//      softmax in base 2; P goes to shared memory, swizzled K-major. The running maximum
-//      moves only when a row's new maximum exceeds it by more than 2^8, so P <= 256 and O
-//      (TMEM) is rescaled on those rare tiles only; the stale maximum cancels in O / l;
-//   3. one thread issues O += P V: A = P (K-major), B = the V tile, MN-major (its rows are
-//      head_dim-contiguous per key).
-// K(j + 2) and V(j + 1) load while tile j computes; thread 0 reads the page ids of a tile
-// one iteration before it issues the tile's loads. The CTA needs 113 KB of shared memory
-// at head_dim 128, so two CTAs share an SM and one CTA's softmax runs under the other's
-// MMAs. tcgen05.commit on an mbarrier marks
-// the end of each tile's S (and of every earlier MMA: they complete in order). V rows past
-// the context in the last tile are zeroed before P V (an unused slot may hold NaN, and
-// 0 * NaN is NaN). Warp-collective tcgen05 loads and stores always run on a path every
-// thread of the warp takes. Every wait is bounded: a timeout sets PI_ERR_TIMEOUT, the CTA
-// drains its loads and MMAs, frees its TMEM and exits.
+// one row per TMEM lane. The context streams in tiles of 64 keys (64 / S pages by TMA).
+// Warp-specialized, six warps, synchronized only through mbarriers (full / empty pairs):
+//   - load warp: TMA of K(t) and V(t) into 2-slot rings, each slot reloaded once the MMA
+//     that read it has completed;
+//   - MMA warp (one thread): S(t) = Q K(t)^T into one of two TMEM buffers (columns [0, 64)
+//     and [64, 128)) as soon as K(t) has landed and the softmax has read that buffer's
+//     previous S, then O += P(t - 1) V(t - 1) (columns [128, 128 + D)); kind::f16, M = 128,
+//     K-major Q, K and P with the 128-byte swizzle, MN-major V;
+//   - 4 softmax warps (one thread per row): read S(t), release its buffer, run the online
+//     softmax in base 2, wait for the previous P V, store P (bf16/f16, swizzled K-major)
+//     and rescale O where needed, then signal P ready.
+// So S(t + 1) computes while the softmax of tile t runs, and the softmax never waits on a
+// load. The running maximum of a row moves only when it grows by more than 2^8: P <= 256,
+// and O is rescaled on those rare tiles only (the stale maximum cancels in O / l). Tiles a
+// row sees in full skip the per-key mask (one FMA and one exp2 per score). V rows past the
+// context in the last tile are zeroed before P V (an unused slot may hold NaN, and
+// 0 * NaN is NaN). Warp-collective tcgen05 loads and stores run on a path every thread of
+// the warp takes. The CTA needs 113 KB of shared memory at head_dim 128, so two CTAs share
+// an SM. Every wait is bounded: a timeout sets PI_ERR_TIMEOUT, the roles leave their loops,
+// in-flight loads and MMAs complete, TMEM is freed.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -43,12 +43,17 @@ bool pool_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, int D, i
 namespace prefill_tc {
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kSoftmaxWarps = 4;  // one per TMEM lane quadrant, one thread per query row
+constexpr int kMmaWarp = 4;       // issues every tcgen05.mma (lane 0)
+constexpr int kLoadWarp = 5;      // issues every TMA load (lane 0)
+constexpr int kThreads = 32 * 6;
 constexpr int kM = 128;       // query rows per CTA = TMEM lanes
 constexpr int kN = 64;        // keys per tile
 constexpr int kKSlots = 2;    // K ring
 constexpr int kVSlots = 2;    // V ring
-constexpr uint32_t kOCol = 64;  // S in TMEM columns [0, 64), O in [64, 64 + D)
+constexpr uint32_t kOCol = 128;  // S double-buffered in TMEM columns [0, 64) and [64, 128),
+                                 // O in [128, 128 + D)
+constexpr uint32_t kTmemCols = 256;
 constexpr float kRescaleLog2 = 8.0f;  // a row's running maximum moves by more than this only
 
 template <int D, int S>
@@ -60,14 +65,16 @@ struct Cfg {
   static constexpr int kKVBytes = kBoxes * kKVBoxBytes;   // K or V tile [boxes][64 keys][128 B]
   static constexpr int kPBytes = kM * 128;                // P [128 rows][64 keys] bf16: one box
   static constexpr int kPagesPerTile = kN / S;
-  static constexpr uint32_t kTmemCols = kOCol + D <= 128 ? 128 : 256;
-  static constexpr int kBarBytes = 64;                    // 5 mbarriers + TMEM address
+  static constexpr int kBarBytes = 128;  // 15 mbarriers + TMEM address
   static constexpr int kLayoutBytes = kQBytes + (kKSlots + kVSlots) * kKVBytes + kPBytes + kBarBytes;
-  // Slack for aligning the tiles to 1024 bytes (the 128-byte swizzle's period). 896 bytes
-  // covers any base aligned to 128 bytes and keeps two head_dim-128 CTAs on one SM (228 KB,
+  // Slack for aligning the tiles to 1024 bytes (the 128-byte swizzle's period). 768 bytes
+  // covers any base aligned to 256 bytes and keeps two head_dim-128 CTAs on one SM (228 KB,
   // 1 KB reserved per CTA); the kernel checks the fit and reports PI_ERR_MISALIGNED if not.
-  static constexpr int kSlack = 896;
+  static constexpr int kSlack = 768;
   static constexpr int kSmem = kSlack + kLayoutBytes;
+  // Dynamic shared memory requested at launch: at least 80 KB, so that at most two CTAs
+  // share an SM and their 2 x 256 TMEM columns fit its 512 (tcgen05.alloc never waits).
+  static constexpr int kLaunchSmem = kSmem > 80 * 1024 ? kSmem : 80 * 1024;
 };
 
 struct Params {
@@ -104,6 +111,10 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // 32 consecutive TMEM columns of this thread's lane (32x32b shape, warp-collective).
@@ -149,6 +160,21 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int ch) {
   return static_cast<uint32_t>((ch >> 3) * (128 * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
+// Barrier slots (mbarriers in shared memory): full / empty pairs of the K and V rings and
+// of the two S buffers, P ready, P V done, and a one-phase drain barrier.
+enum Bar : int {
+  kKFull = 0,    // [2] K(t) landed (TMA bytes)
+  kKEmpty = 2,   // [2] S(t) complete: K slot free (MMA commit)
+  kVFull = 4,    // [2] V(t) landed
+  kVEmpty = 6,   // [2] P V(t) complete: V slot free
+  kSFull = 8,    // [2] S(t) complete (MMA commit)
+  kSEmpty = 10,  // [2] S(t) read by the 4 softmax warps
+  kPFull = 12,   // P(t) in shared memory and O rescaled (4 softmax warps)
+  kOFree = 13,   // P V(t) complete: P buffer and O free (MMA commit)
+  kDrain = 14,   // every MMA issued has completed (one phase, at the end)
+  kNumBars = 15,
+};
+
 template <typename T, int D, int S>
 __global__ void __launch_bounds__(kThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
@@ -160,15 +186,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* ks = qs + C::kQBytes;                    // K slot s at s * kKVBytes
   uint8_t* vs = ks + kKSlots * C::kKVBytes;         // V slot s at s * kKVBytes
   uint8_t* ps = vs + kVSlots * C::kKVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + C::kPBytes);  // K[0..1], V[0..1], MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kKSlots + kVSlots + 1);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + C::kPBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   if ((qs - smem_raw) + C::kLayoutBytes > C::kSmem) {  // CTA-uniform: the base is too unaligned
     if (threadIdx.x == 0) record_error(p.err, PI_ERR_MISALIGNED);
     return;
   }
+  auto bar = [&](int i) { return smem_u32(bars + i); };
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const int lane = tid & 31;
   const int G = p.group;
   const int h = blockIdx.y;
   // causal: the latest (heaviest) query blocks first
@@ -180,13 +208,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int kv_hi = p.causal ? min(p.kv_len, p.q_start + t_end) : p.kv_len;
   const int n_tiles = kv_hi > 0 ? (kv_hi + kN - 1) / kN : 0;
   const int n_pages = (kv_hi + S - 1) / S;
-  const uint32_t mma_bar = smem_u32(bars + kKSlots + kVSlots);
 
   pdl_trigger();
   pdl_wait();
 
   if (tid == 0) {
-    for (int b = 0; b < kKSlots + kVSlots + 1; ++b) mbar_init(smem_u32(bars + b), 1);
+    for (int b = 0; b < kNumBars; ++b)
+      mbar_init(bar(b), (b == kSEmpty || b == kSEmpty + 1 || b == kPFull) ? kSoftmaxWarps : 1);
     fence_mbar_init();
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
@@ -194,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(C::kTmemCols)
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -215,293 +243,290 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * warp) << 16);  // this warp's lanes
-
-  // Page ids of tile j (thread 0). They are fetched one iteration before the loads that use
-  // them, so the TMA issue never waits on a block-table read.
-  auto fetch_ids = [&](int j, int (&ids)[C::kPagesPerTile]) {
-#pragma unroll
-    for (int pp = 0; pp < C::kPagesPerTile; ++pp) {
-      const int pg = j * C::kPagesPerTile + pp;
-      ids[pp] = (j < n_tiles && pg < n_pages) ? p.block_table[pg] : 0;
-    }
-  };
-  // K (kind 0) or V (kind 1) of tile j into `dst`, completing on `bar` (thread 0).
-  auto issue_load = [&](int j, int kind, uint32_t dst, uint32_t bar, const int (&ids)[C::kPagesPerTile]) {
-    const int pg0 = j * C::kPagesPerTile;
-    const int np = min(C::kPagesPerTile, n_pages - pg0);
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(np * C::kBoxes * S * 128));
-#pragma unroll
-    for (int pp = 0; pp < C::kPagesPerTile; ++pp) {
-      if (pp >= np) break;
-      int pid = ids[pp];
-      if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
-        record_error(p.err, PI_ERR_PAGE_RANGE);
-        pid = 0;
-      }
-      const int row = (pid * p.hkv + h) * S;
-#pragma unroll
-      for (int b = 0; b < C::kBoxes; ++b)
-        tma_load_2d(dst + b * C::kKVBoxBytes + pp * S * 128, kind ? &tmap_v : &tmap_k, bar, 64 * b,
-                    row);
-    }
-  };
   const uint32_t k_addr0 = smem_u32(ks);
   const uint32_t v_addr0 = smem_u32(vs);
-  int k_issued = 0, v_issued = 0;  // loads thread 0 has issued
-  // Thread 0's page ids: at the top of iteration j, ids_k holds tile j + 1's (for V(j + 1))
-  // and ids_n tile j + 2's (for K(j + 2)); ids_v serves the first tile's loads.
-  int ids_v[C::kPagesPerTile], ids_k[C::kPagesPerTile], ids_n[C::kPagesPerTile];
-  if (tid == 0) {
-    fetch_ids(0, ids_v);
-    fetch_ids(1, ids_k);
-    if (n_tiles > 0) issue_load(0, 0, k_addr0, smem_u32(bars + 0), ids_v);
-    if (n_tiles > 0) issue_load(0, 1, v_addr0, smem_u32(bars + kKSlots), ids_v);
-    if (n_tiles > 1) issue_load(1, 0, k_addr0 + C::kKVBytes, smem_u32(bars + 1), ids_k);
-    if (n_tiles > 1) issue_load(1, 1, v_addr0 + C::kKVBytes, smem_u32(bars + kKSlots + 1), ids_k);
-    k_issued = v_issued = min(2, n_tiles);
-    fetch_ids(2, ids_n);
-  }
-
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  const uint32_t id_s = umma::instr_desc_f16(kBf16, kM, kN, false, false);
-  const uint32_t id_o = umma::instr_desc_f16(kBf16, kM, D, false, true);
-  const uint32_t q_addr = smem_u32(qs);
-  const uint32_t p_addr = smem_u32(ps);
-
-  const int r = tid;  // this thread's query row and TMEM lane
-  const int tok = t0 + r / G;
-  const int lim = p.causal ? min(p.kv_len, p.q_start + tok + 1) : p.kv_len;
-  float m_run = -INFINITY;
-  float l_run = 0.f;
-  uint32_t mma_phase = 0;
-  int k_done = 0, v_done = 0;  // loads whose completion thread 0 has seen (for the drain)
   bool failed = false;
+  // Every wait is bounded. A role whose wait times out leaves its loop at once; the roles
+  // waiting on it then time out too, and all meet at the barrier after the loops.
 
-  for (int j = 0; j < n_tiles; ++j) {
-    const int ksl = j % kKSlots;
-    // ---- S = Q K^T into TMEM columns [0, 64), issued once K(j) has landed. Only thread 0
-    // waits for the load; it commits even after a timeout (so the others' wait below ends)
-    // and its failure reaches every thread at the barrier after that wait.
-    if (tid == 0) {
-      if (!failed &&
-          mbar_wait_bounded(smem_u32(bars + ksl), static_cast<uint32_t>((j / kKSlots) & 1))) {
-        k_done = j + 1;
-        tc_fence_after();
-        const uint32_t k_addr = k_addr0 + ksl * C::kKVBytes;
+  if (warp == kLoadWarp) {
+    // ---------------- TMA producer: K(t) and V(t) into slot t % 2 ----------------
+    int issued[2] = {0, 0};  // K and V loads issued (tiles 0 .. issued - 1)
+    if (lane == 0) {
+      for (int t = 0; t < n_tiles; ++t) {
+        const int sl = t % kKSlots;
+        const uint32_t free_parity = static_cast<uint32_t>(((t / kKSlots) & 1) ^ 1);
+        const int pg0 = t * C::kPagesPerTile;
+        const int np = min(C::kPagesPerTile, n_pages - pg0);
+        int ids[C::kPagesPerTile];
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t col = static_cast<uint32_t>((kk & 3) * 32);
-          umma_f16(tmem,
-                   umma::smem_desc(q_addr + (kk >> 2) * C::kQBoxBytes + col, 16, 1024, umma::kSwizzle128),
-                   umma::smem_desc(k_addr + (kk >> 2) * C::kKVBoxBytes + col, 16, 1024, umma::kSwizzle128),
-                   id_s, kk > 0 ? 1u : 0u);
+        for (int pp = 0; pp < C::kPagesPerTile; ++pp) {
+          int pid = pp < np ? p.block_table[pg0 + pp] : 0;
+          if (pid < 0 || static_cast<int64_t>(pid) >= p.num_pages) {
+            record_error(p.err, PI_ERR_PAGE_RANGE);
+            pid = 0;
+          }
+          ids[pp] = pid;
         }
-      } else {
-        failed = true;
-      }
-      umma_commit(mma_bar);
-    }
-    if (!mbar_wait_bounded(mma_bar, mma_phase)) failed = true;
-    mma_phase ^= 1u;
-    if (__syncthreads_or(failed)) {
-      failed = true;
-      break;
-    }
-    tc_fence_after();
-    // S(j) is done, and with it every earlier MMA (P V of tile j - 1): K slot j % 2 and V
-    // slot (j + 1) % 2 are free, so K(j + 2) and V(j + 1) go out now.
-    if (tid == 0) {
-      if (k_issued < n_tiles && k_issued == j + kKSlots) {
-        issue_load(k_issued, 0, k_addr0 + ksl * C::kKVBytes, smem_u32(bars + ksl), ids_n);
-        ++k_issued;
-      }
-      if (j >= 1 && v_issued < n_tiles && v_issued == j + 1) {
-        const int vsl = v_issued % kVSlots;
-        issue_load(v_issued, 1, v_addr0 + vsl * C::kKVBytes, smem_u32(bars + kKSlots + vsl), ids_k);
-        ++v_issued;
-      }
-      // ids_k held tile j + 1's ids, ids_n tile j + 2's; move on by one tile
+        const uint32_t bytes = static_cast<uint32_t>(np * C::kBoxes * S * 128);
+        for (int kind = 0; kind < 2; ++kind) {
+          if (!mbar_wait_bounded(bar((kind ? kVEmpty : kKEmpty) + sl), free_parity)) {
+            failed = true;
+            break;
+          }
+          const uint32_t full = bar((kind ? kVFull : kKFull) + sl);
+          const uint32_t dst = (kind ? v_addr0 : k_addr0) + sl * C::kKVBytes;
+          mbar_arrive_expect_tx(full, bytes);
 #pragma unroll
-      for (int pp = 0; pp < C::kPagesPerTile; ++pp) ids_k[pp] = ids_n[pp];
-      fetch_ids(j + 3, ids_n);
-    }
-    __syncwarp();  // warp 0 converged again after thread 0's issue: the loads are .aligned
-    // ---- online softmax of this row
-    float sv[kN];
-    tmem_ld32(t_row, sv);
-    tmem_ld32(t_row + 32, sv + 32);
-    tmem_wait_ld();
-    const int key0 = j * kN;
-    // Tiles whose keys this row sees in full (all but the causal diagonal and the last
-    // tile) skip the per-key mask: the raw maximum is scaled once and each P is one FMA
-    // and one exp2. Others mask by select and scale every score.
-    const bool fast = key0 + kN <= lim && p.scale_log2 > 0.f;
-    float mt = -INFINITY;
-    if (fast) {
+          for (int pp = 0; pp < C::kPagesPerTile; ++pp) {
+            if (pp >= np) break;
+            const int row = (ids[pp] * p.hkv + h) * S;
 #pragma unroll
-      for (int c = 0; c < kN; ++c) mt = fmaxf(mt, sv[c]);
-      mt *= p.scale_log2;
-    } else {
-#pragma unroll
-      for (int c = 0; c < kN; ++c) {
-        sv[c] = key0 + c < lim ? sv[c] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, sv[c]);
-      }
-    }
-    // The running maximum moves only past a margin: P = 2^(s - m) stays <= 2^kRescaleLog2,
-    // and O needs rescaling only on the tiles where a row's maximum jumps.
-    float m_new = m_run;
-    bool rescale = false;
-    if (mt > m_run + kRescaleLog2) {
-      rescale = m_run != -INFINITY;  // before any key O is zero: nothing to rescale
-      m_new = mt;
-    }
-    const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
-    float ls = 0.f;
-    auto store_p = [&](int ch, const float (&pv)[8]) {
-      const uint4 packed = make_uint4(MmaOp<T>::pack(pv[0], pv[1]), MmaOp<T>::pack(pv[2], pv[3]),
-                                      MmaOp<T>::pack(pv[4], pv[5]), MmaOp<T>::pack(pv[6], pv[7]));
-      *reinterpret_cast<uint4*>(ps + sw128_off(r, ch)) = packed;
-    };
-    if (fast) {
-      const float neg_m = -m_new;  // finite: 64 visible keys
-#pragma unroll
-      for (int ch = 0; ch < kN / 8; ++ch) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = fast_exp2(fmaf(sv[ch * 8 + e], p.scale_log2, neg_m));
-          ls += pv[e];
+            for (int b = 0; b < C::kBoxes; ++b)
+              tma_load_2d(dst + b * C::kKVBoxBytes + pp * S * 128, kind ? &tmap_v : &tmap_k, full,
+                          64 * b, row);
+          }
+          issued[kind] = t + 1;
         }
-        store_p(ch, pv);
+        if (failed) break;
       }
-    } else {
-#pragma unroll
-      for (int ch = 0; ch < kN / 8; ++ch) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float x = sv[ch * 8 + e];
-          pv[e] = x == -INFINITY ? 0.f : fast_exp2(x - m_new);
-          ls += pv[e];
+    }
+    __syncwarp();
+    failed = __syncthreads_or(failed) != 0;
+    // after a failure, loads still in flight land before the shared memory is released
+    if (failed && lane == 0) {
+      for (int kind = 0; kind < 2; ++kind) {
+        for (int sl = 0; sl < kKSlots && sl < issued[kind]; ++sl) {
+          // the last tile loaded into slot sl: its phase completes after the earlier ones
+          const int last = issued[kind] - 1 - ((issued[kind] - 1 - sl) % kKSlots);
+          mbar_wait_bounded(bar((kind ? kVFull : kKFull) + sl),
+                            static_cast<uint32_t>((last / kKSlots) & 1));
         }
-        store_p(ch, pv);
       }
     }
-    l_run = l_run * alpha + ls;
-    m_run = m_new;
-    // ---- O of earlier tiles, rescaled where a row's maximum moved (P V of tile j - 1 is
-    // complete). The TMEM loads are warp-collective: the whole warp takes the branch.
-    if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float ov[32];
-        tmem_ld32(t_row + kOCol + 32 * c, ov);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-        tmem_st32(t_row + kOCol + 32 * c, ov);
-      }
-      tmem_wait_st();
-    }
-    // ---- V(j): on the last tile every thread waits for it and zeroes the rows past the
-    // context (they may hold NaN); otherwise only the MMA issuer waits, below.
-    const int vsl = j % kVSlots;
-    const uint32_t v_bar = smem_u32(bars + kKSlots + vsl);
-    const uint32_t v_parity = static_cast<uint32_t>((j / kVSlots) & 1);
-    const int valid = min(kN, kv_hi - key0);
-    if (valid < kN) {
-      if (!mbar_wait_bounded(v_bar, v_parity)) failed = true;
-      if (__syncthreads_or(failed)) {
-        failed = true;
-        break;
-      }
-      if (tid == 0) v_done = j + 1;
-      uint8_t* vs_j = vs + vsl * C::kKVBytes;
-      const int per_box = (kN - valid) * 8;
-      for (int c = tid; c < C::kBoxes * per_box; c += kThreads) {
-        const int b = c / per_box;
-        const int rem = c - b * per_box;
-        *reinterpret_cast<uint4*>(vs_j + b * C::kKVBoxBytes + (valid + rem / 8) * 128 + (rem & 7) * 16) =
-            make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-    fence_proxy_async_smem();  // P and the zeroed V rows are read by the MMA
-    tc_fence_before();
-    __syncthreads();
-    // ---- O += P V into TMEM columns [64, 64 + D)
-    if (tid == 0) {
-      if (valid == kN && !failed) {
-        if (mbar_wait_bounded(v_bar, v_parity))
-          v_done = j + 1;
-        else
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer: S(t) = Q K(t)^T, then P V(t - 1) ----------------
+    if (lane == 0) {
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      const uint32_t id_s = umma::instr_desc_f16(kBf16, kM, kN, false, false);
+      const uint32_t id_o = umma::instr_desc_f16(kBf16, kM, D, false, true);
+      const uint32_t q_addr = smem_u32(qs);
+      const uint32_t p_addr = smem_u32(ps);
+      auto pv = [&](int u) {  // O += P(u) V(u)
+        const int sl = u % kVSlots;
+        if (!mbar_wait_bounded(bar(kPFull), static_cast<uint32_t>(u & 1)) ||
+            !mbar_wait_bounded(bar(kVFull + sl), static_cast<uint32_t>((u / kVSlots) & 1))) {
           failed = true;
-      }
-      if (!failed) {
+          return;
+        }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kN / 16; ++kk) {
           const uint64_t a = umma::smem_desc(p_addr + static_cast<uint32_t>(kk * 32), 16, 1024,
                                              umma::kSwizzle128);
-          const uint64_t b = umma::smem_desc(v_addr0 + static_cast<uint32_t>(vsl * C::kKVBytes + kk * 16 * 128),
-                                             C::kKVBoxBytes, 1024, umma::kSwizzle128);
-          umma_f16(tmem + kOCol, a, b, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint64_t b = umma::smem_desc(
+              v_addr0 + static_cast<uint32_t>(sl * C::kKVBytes + kk * 16 * 128), C::kKVBoxBytes,
+              1024, umma::kSwizzle128);
+          umma_f16(tmem + kOCol, a, b, id_o, (u > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(kOFree));
+        umma_commit(bar(kVEmpty + sl));
+      };
+      for (int t = 0; t < n_tiles && !failed; ++t) {
+        const int sl = t % kKSlots;
+        const uint32_t parity = static_cast<uint32_t>((t / kKSlots) & 1);
+        if (!mbar_wait_bounded(bar(kKFull + sl), parity) ||
+            !mbar_wait_bounded(bar(kSEmpty + sl), parity ^ 1u)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = k_addr0 + sl * C::kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t col = static_cast<uint32_t>((kk & 3) * 32);
+          umma_f16(tmem + static_cast<uint32_t>(kN * sl),
+                   umma::smem_desc(q_addr + (kk >> 2) * C::kQBoxBytes + col, 16, 1024, umma::kSwizzle128),
+                   umma::smem_desc(k_addr + (kk >> 2) * C::kKVBoxBytes + col, 16, 1024, umma::kSwizzle128),
+                   id_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(kSFull + sl));
+        umma_commit(bar(kKEmpty + sl));
+        if (t >= 1) pv(t - 1);
+      }
+      if (!failed && n_tiles > 0) pv(n_tiles - 1);
+      umma_commit(bar(kDrain));  // arrives once every MMA issued above has completed
+    }
+    __syncwarp();
+    failed = __syncthreads_or(failed) != 0;
+  } else {
+    // ---------------- softmax warps: one thread per query row / TMEM lane ----------------
+    const int r = tid;
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * warp) << 16);  // this warp's lanes
+    const int tok = t0 + r / G;
+    const int lim = p.causal ? min(p.kv_len, p.q_start + tok + 1) : p.kv_len;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int sb = j % 2;
+      if (!mbar_wait_bounded(bar(kSFull + sb), static_cast<uint32_t>((j / 2) & 1))) failed = true;
+      if (__any_sync(0xffffffffu, failed)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      float sv[kN];
+      tmem_ld32(t_row + static_cast<uint32_t>(kN * sb), sv);
+      tmem_ld32(t_row + static_cast<uint32_t>(kN * sb + 32), sv + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kSEmpty + sb));  // S buffer sb may be overwritten
+      const int key0 = j * kN;
+      // Tiles whose keys this row sees in full (all but the causal diagonal and the last
+      // tile) skip the per-key mask: the raw maximum is scaled once and each P is one FMA
+      // and one exp2. Others mask by select and scale every score.
+      const bool fast = key0 + kN <= lim && p.scale_log2 > 0.f;
+      float mt = -INFINITY;
+      if (fast) {
+#pragma unroll
+        for (int c = 0; c < kN; ++c) mt = fmaxf(mt, sv[c]);
+        mt *= p.scale_log2;
+      } else {
+#pragma unroll
+        for (int c = 0; c < kN; ++c) {
+          sv[c] = key0 + c < lim ? sv[c] * p.scale_log2 : -INFINITY;
+          mt = fmaxf(mt, sv[c]);
+        }
+      }
+      // The running maximum moves only past a margin: P = 2^(s - m) stays <= 2^kRescaleLog2,
+      // and O needs rescaling only on the tiles where a row's maximum jumps.
+      float m_new = m_run;
+      bool rescale = false;
+      if (mt > m_run + kRescaleLog2) {
+        rescale = m_run != -INFINITY;  // before any key O is zero: nothing to rescale
+        m_new = mt;
+      }
+      const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
+      float ls = 0.f;
+      uint32_t pk[kN / 2];  // P as packed pairs
+      if (fast) {
+        const float neg_m = -m_new;  // finite: 64 visible keys
+#pragma unroll
+        for (int c = 0; c < kN; c += 2) {
+          const float a = fast_exp2(fmaf(sv[c], p.scale_log2, neg_m));
+          const float b = fast_exp2(fmaf(sv[c + 1], p.scale_log2, neg_m));
+          ls += a + b;
+          pk[c / 2] = MmaOp<T>::pack(a, b);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kN; c += 2) {
+          const float a = sv[c] == -INFINITY ? 0.f : fast_exp2(sv[c] - m_new);
+          const float b = sv[c + 1] == -INFINITY ? 0.f : fast_exp2(sv[c + 1] - m_new);
+          ls += a + b;
+          pk[c / 2] = MmaOp<T>::pack(a, b);
+        }
+      }
+      l_run = l_run * alpha + ls;
+      m_run = m_new;
+      // P V(j - 1) complete: the P buffer and O are free
+      if (j > 0) {
+        if (!mbar_wait_bounded(bar(kOFree), static_cast<uint32_t>((j - 1) & 1))) failed = true;
+        if (__any_sync(0xffffffffu, failed)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int ch = 0; ch < kN / 8; ++ch)
+        *reinterpret_cast<uint4*>(ps + sw128_off(r, ch)) =
+            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+      // O of earlier tiles, rescaled where a row's maximum moved. The TMEM loads are
+      // warp-collective: the whole warp takes the branch.
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float ov[32];
+          tmem_ld32(t_row + kOCol + 32 * c, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+          tmem_st32(t_row + kOCol + 32 * c, ov);
+        }
+        tmem_wait_st();
+      }
+      // Last tile: V rows past the context are zeroed once V has landed (they may hold
+      // NaN); each softmax warp zeroes a quarter of them.
+      const int valid = min(kN, kv_hi - key0);
+      if (valid < kN) {
+        const int vsl = j % kVSlots;
+        if (!mbar_wait_bounded(bar(kVFull + vsl), static_cast<uint32_t>((j / kVSlots) & 1)))
+          failed = true;
+        if (__any_sync(0xffffffffu, failed)) {
+          failed = true;
+          break;
+        }
+        uint8_t* vs_j = vs + vsl * C::kKVBytes;
+        const int per_box = (kN - valid) * 8;
+        for (int c = tid; c < C::kBoxes * per_box; c += 32 * kSoftmaxWarps) {
+          const int b = c / per_box;
+          const int rem = c - b * per_box;
+          *reinterpret_cast<uint4*>(vs_j + b * C::kKVBoxBytes + (valid + rem / 8) * 128 +
+                                    (rem & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_smem();  // P and the zeroed V rows are read by the MMA
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kPFull));
+    }
+    // The last P V, and with it every MMA, completes on the drain barrier.
+    if (!failed && n_tiles > 0 && !mbar_wait_bounded(bar(kDrain), 0)) failed = true;
+    failed = __syncthreads_or(failed) != 0;
+    tc_fence_after();
+    if (!failed) {
+      // The TMEM loads are warp-collective (.sync.aligned): every thread of the warp runs
+      // them on the same path, rows past q_len included (a warp can straddle q_len); only
+      // the stores depend on the row.
+      const bool row_valid = tok < p.q_len;
+      T* orow = static_cast<T*>(p.out) +
+                static_cast<int64_t>(row_valid ? tok : 0) * p.out_tok_stride +
+                static_cast<int64_t>(h * G + r % G) * D;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float ov[32];
+        if (n_tiles > 0) {
+          tmem_ld32(t_row + kOCol + 32 * c, ov);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = 0.f;
+        }
+        if (row_valid) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            *reinterpret_cast<uint32_t*>(orow + 32 * c + e) =
+                MmaOp<T>::pack(ov[e] * inv, ov[e + 1] * inv);
         }
       }
     }
   }
 
-  // ---- wait for the last P V (and, after a failure, for whatever MMA was issued)
-  if (n_tiles > 0) {
-    if (tid == 0) umma_commit(mma_bar);
-    if (!mbar_wait_bounded(mma_bar, mma_phase)) failed = true;
-  }
-  failed = __syncthreads_or(failed) != 0;
-  tc_fence_after();
+  // After a failure every MMA still has to finish before TMEM is freed: the MMA issuer's
+  // last commit (the drain barrier) covers them.
   if (failed) {
-    if (tid == 0) {
-      record_error(p.err, PI_ERR_TIMEOUT);
-      // loads still in flight must land before the CTA's shared memory is released
-      for (int j = k_done; j < k_issued; ++j)
-        mbar_wait_bounded(smem_u32(bars + (j % kKSlots)), static_cast<uint32_t>((j / kKSlots) & 1));
-      for (int j = v_done; j < v_issued; ++j)
-        mbar_wait_bounded(smem_u32(bars + kKSlots + (j % kVSlots)),
-                          static_cast<uint32_t>((j / kVSlots) & 1));
-    }
-  } else {
-    // The TMEM loads are warp-collective (.sync.aligned): every thread of the CTA runs
-    // them on the same path, rows past q_len included (a warp can straddle q_len); only
-    // the stores depend on the row.
-    const bool row_valid = tok < p.q_len;
-    T* orow = static_cast<T*>(p.out) +
-              static_cast<int64_t>(row_valid ? tok : 0) * p.out_tok_stride +
-              static_cast<int64_t>(h * G + r % G) * D;
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float ov[32];
-      if (n_tiles > 0) {
-        tmem_ld32(t_row + kOCol + 32 * c, ov);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] = 0.f;
-      }
-      if (row_valid) {
-#pragma unroll
-        for (int e = 0; e < 32; e += 2)
-          *reinterpret_cast<uint32_t*>(orow + 32 * c + e) =
-              MmaOp<T>::pack(ov[e] * inv, ov[e + 1] * inv);
-      }
-    }
+    if (tid == 0) record_error(p.err, PI_ERR_TIMEOUT);
+    if (warp == kMmaWarp && lane == 0) mbar_wait_bounded(bar(kDrain), 0);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(C::kTmemCols)
+                 "r"(kTmemCols)
                  : "memory");
   }
 }
@@ -517,12 +542,13 @@ int launch(const Params& p, int n_qblocks, const CUtensorMap& tk, const CUtensor
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PI_ERR_CUDA;
   const int slot = (std::is_same<T, __half>::value ? 4 : 0) + (D == 128 ? 2 : 0) + (S == 32 ? 1 : 0);
   if (!configured[dev][slot]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kLaunchSmem) !=
+        cudaSuccess)
       return PI_ERR_CUDA;
     configured[dev][slot] = true;
   }
   const cudaError_t e =
-      launch_kernel(kern, dim3(n_qblocks, p.hkv), dim3(kThreads), C::kSmem, stream, tk, tv, p);
+      launch_kernel(kern, dim3(n_qblocks, p.hkv), dim3(kThreads), C::kLaunchSmem, stream, tk, tv, p);
   return e == cudaSuccess ? PI_OK : PI_ERR_CUDA;
 }
 

@@ -27,8 +27,10 @@ KM = 128
 KN = 64
 K_SLOTS = 2
 V_SLOTS = 2
-SLACK = 896
-O_COL = 64
+SLACK = 768
+O_COL = 128
+TMEM_COLS = 256
+BAR_BYTES = 128
 SM_SMEM = 228 * 1024
 TMEM_PER_SM = 512
 
@@ -40,11 +42,11 @@ def cfg(D: int, S: int) -> dict:
     q_bytes = boxes * q_box
     kv_bytes = boxes * kv_box
     p_bytes = KM * 128
-    tmem_cols = 128 if O_COL + D <= 128 else 256
-    layout = q_bytes + (K_SLOTS + V_SLOTS) * kv_bytes + p_bytes + 64
+    layout = q_bytes + (K_SLOTS + V_SLOTS) * kv_bytes + p_bytes + BAR_BYTES
     smem = SLACK + layout
+    launch = max(smem, 80 * 1024)
     return dict(boxes=boxes, q_box=q_box, kv_box=kv_box, q=q_bytes, kv=kv_bytes, p=p_bytes,
-                pages_per_tile=KN // S, smem=smem, layout=layout, tmem_cols=tmem_cols)
+                pages_per_tile=KN // S, smem=smem, launch=launch, layout=layout)
 
 
 def sw128_off(r: int, ch: int) -> int:
@@ -56,30 +58,32 @@ def test_constants_match_the_kernel_source() -> None:
     for name, val in (("kM", KM), ("kN", KN), ("kKSlots", K_SLOTS), ("kVSlots", V_SLOTS)):
         assert re.search(rf"constexpr int {name} = {val};", src), name
     assert re.search(rf"constexpr uint32_t kOCol = {O_COL};", src)
+    assert re.search(rf"constexpr uint32_t kTmemCols = {TMEM_COLS};", src)
     assert re.search(rf"static constexpr int kSlack = {SLACK};", src)
-    assert "kOCol + D <= 128 ? 128 : 256" in src
+    assert re.search(rf"static constexpr int kBarBytes = {BAR_BYTES};", src)
+    assert "kSmem > 80 * 1024 ? kSmem : 80 * 1024" in src
     assert "(kKSlots + kVSlots) * kKVBytes + kPBytes + kBarBytes" in src
 
 
 @pytest.mark.parametrize("D,S", list(itertools.product((64, 128), (16, 32))))
 def test_shared_memory_and_tmem_bounds(D: int, S: int) -> None:
     c = cfg(D, S)
-    assert c["smem"] <= 227 * 1024
-    # CTAs per SM by shared memory, and their TMEM never exceeds the SM's 512 columns (so
+    assert c["launch"] <= 227 * 1024
+    # exactly two CTAs per SM by shared memory, and their TMEM fits the SM's 512 columns (so
     # tcgen05.alloc never has to wait for another CTA's columns)
-    ctas = SM_SMEM // (c["smem"] + 1024)
-    assert ctas >= 2
-    assert ctas * c["tmem_cols"] <= TMEM_PER_SM
+    ctas = SM_SMEM // (c["launch"] + 1024)
+    assert ctas == 2
+    assert ctas * TMEM_COLS <= TMEM_PER_SM
     q0 = 0
     k0 = q0 + c["q"]
     v0 = k0 + K_SLOTS * c["kv"]
     p0 = v0 + V_SLOTS * c["kv"]
     bars0 = p0 + c["p"]
-    assert bars0 + (K_SLOTS + V_SLOTS + 1) * 8 + 4 <= c["layout"]
+    assert bars0 + 8 * 8 + 4 <= c["layout"]
     for off in (k0, v0, p0, c["kv"]):
         assert off % 1024 == 0
-    # the layout fits after aligning any 128-byte aligned base up to 1024 bytes
-    assert all((-base) % 1024 + c["layout"] <= c["smem"] for base in range(0, 4096, 128))
+    # the layout fits after aligning any 256-byte aligned base up to 1024 bytes
+    assert all((-base) % 1024 + c["layout"] <= c["smem"] for base in range(0, 4096, 256))
     # Q writes: rows < 128, 16-byte chunks < D / 8
     assert max(sw128_off(r, ch) for r in range(KM) for ch in range(D // 8)) + 16 <= c["q"]
     # P writes: 64 keys = 8 chunks per row, one box
@@ -103,8 +107,8 @@ def test_shared_memory_and_tmem_bounds(D: int, S: int) -> None:
         assert v_off + (c["boxes"] - 1) * c["kv_box"] + 16 * 128 <= c["kv"]
     # descriptors hold addresses >> 4 in 14 bits: the whole allocation must stay below 256 KB
     assert c["smem"] < (1 << 18)
-    # TMEM: S in [0, 64), O in [64, 64 + D)
-    assert KN <= O_COL and O_COL + D <= c["tmem_cols"]
+    # TMEM: S double-buffered in [0, 64) and [64, 128), O in [128, 128 + D)
+    assert 2 * KN <= O_COL and O_COL + D <= TMEM_COLS
 
 
 @pytest.mark.parametrize("D,S", list(itertools.product((64, 128), (16, 32))))
@@ -151,24 +155,129 @@ def test_page_reads_tiles_and_expect_tx(D: int, S: int, G: int) -> None:
                     assert lim <= kv_hi
 
 
-def test_load_slots_phases_and_page_ids() -> None:
-    # K(t) in slot t % 2, V(t) in V slot t % 2 (phase (t // 2) & 1). Tiles 0 and 1 load in
-    # the prologue; after S(j) completes (and with it P V(j - 1)), K(j + 2) takes K(j)'s slot
-    # and V(j + 1) takes V(j - 1)'s. Thread 0's page ids: ids_k = tile j + 1, ids_n = tile
-    # j + 2 at the top of iteration j.
-    for n in range(0, 12):
-        k_issued = v_issued = min(2, n)
-        ids_k, ids_n = 1, 2
-        for j in range(n):
-            assert j < k_issued and j < v_issued  # tile j's K and V were issued before its waits
-            if k_issued < n and k_issued == j + K_SLOTS:
-                assert k_issued % K_SLOTS == j % K_SLOTS   # K(j) consumed by S(j): done
-                assert ids_n == k_issued
-                k_issued += 1
-            if j >= 1 and v_issued < n and v_issued == j + 1:
-                # V(j + 1)'s slot held V(j - 1), read by P V(j - 1): done before S(j)
-                assert v_issued % V_SLOTS == (j - 1) % V_SLOTS
-                assert ids_k == v_issued
-                v_issued += 1
-            ids_k, ids_n = ids_n, j + 3
-        assert k_issued == n and v_issued == n
+class _Barrier:
+    """An mbarrier: `count` arrivals complete the current phase; wait(parity) passes once
+    the phase with that parity has completed (a fresh barrier passes parity 1)."""
+
+    def __init__(self, count: int) -> None:
+        self.count, self.arrived, self.phase = count, 0, 0
+
+    def arrive(self) -> None:
+        self.arrived += 1
+        assert self.arrived <= self.count
+        if self.arrived == self.count:
+            self.arrived, self.phase = 0, self.phase + 1
+
+    def passed(self, parity: int) -> bool:
+        return (self.phase & 1) != parity
+
+
+def _simulate(n_tiles: int, seed: int) -> None:
+    """The kernel's three roles (load warp, MMA thread, 4 softmax warps) as coroutines over
+    mbarriers, with TMA loads and MMAs completing asynchronously in random order. Checks
+    that every role finishes (no deadlock) and that no buffer is overwritten before its
+    previous reader or writer has finished."""
+    import random
+
+    rnd = random.Random(seed)
+    B = {name: _Barrier(4 if name.startswith(("SEmpty", "PFull")) else 1) for name in
+         ["KFull0", "KFull1", "KEmpty0", "KEmpty1", "VFull0", "VFull1", "VEmpty0", "VEmpty1",
+          "SFull0", "SFull1", "SEmpty0", "SEmpty1", "PFull", "OFree", "Drain"]}
+    done = {"K": set(), "V": set(), "S": set(), "PV": set()}
+    s_reads = [0] * max(n_tiles, 1)   # softmax warps that have read S(t)
+    p_writes = [0] * max(n_tiles, 1)  # softmax warps that have written their rows of P(t)
+    pending = []          # async completions: (kind, tile, barriers to arrive on)
+    issued_mma = []       # MMAs in issue order (they complete in order)
+
+    def load_warp():
+        for t in range(n_tiles):
+            sl = t % 2
+            for kind in ("K", "V"):
+                empty = ("KEmpty" if kind == "K" else "VEmpty") + str(sl)
+                while not B[empty].passed(((t // 2) & 1) ^ 1):
+                    yield
+                # the slot's previous tile has been read by a completed MMA
+                if t >= 2:
+                    assert (t - 2) in (done["S"] if kind == "K" else done["PV"]), (kind, t)
+                pending.append((kind, t, [("KFull" if kind == "K" else "VFull") + str(sl)]))
+
+    def mma_thread():
+        def pv(u):
+            while not (B["PFull"].passed(u & 1) and B["VFull" + str(u % 2)].passed((u // 2) & 1)):
+                yield
+            assert p_writes[u] == 4 and u in done["V"]
+            issued_mma.append(("PV", u, ["OFree", "VEmpty" + str(u % 2)]))
+
+        for t in range(n_tiles):
+            sl = t % 2
+            while not (B["KFull" + str(sl)].passed((t // 2) & 1) and
+                       B["SEmpty" + str(sl)].passed(((t // 2) & 1) ^ 1)):
+                yield
+            assert t in done["K"]
+            if t >= 2:
+                assert s_reads[t - 2] == 4  # S buffer sl was read by every warp before reuse
+            issued_mma.append(("S", t, ["SFull" + str(sl), "KEmpty" + str(sl)]))
+            if t >= 1:
+                yield from pv(t - 1)
+        if n_tiles > 0:
+            yield from pv(n_tiles - 1)
+        issued_mma.append(("Drain", -1, ["Drain"]))
+
+    def softmax_warp(w):
+        for j in range(n_tiles):
+            while not B["SFull" + str(j % 2)].passed((j // 2) & 1):
+                yield
+            assert j in done["S"]
+            yield  # reading S
+            s_reads[j] += 1
+            B["SEmpty" + str(j % 2)].arrive()
+            if j > 0:
+                while not B["OFree"].passed((j - 1) & 1):
+                    yield
+                assert (j - 1) in done["PV"]  # P buffer and O free
+            if j == n_tiles - 1:
+                while not B["VFull" + str(j % 2)].passed((j // 2) & 1):
+                    yield
+                assert j in done["V"]
+            p_writes[j] += 1
+            B["PFull"].arrive()
+        if n_tiles > 0:
+            while not B["Drain"].passed(0):
+                yield
+            assert (n_tiles - 1) in done["PV"]
+
+    roles = [load_warp(), mma_thread()] + [softmax_warp(w) for w in range(4)]
+    alive = list(roles)
+    steps = 0
+    while alive or pending or issued_mma:
+        steps += 1
+        assert steps < 200000, "no progress: deadlock"
+        choices = list(alive)
+        if pending:
+            choices.append("load")
+        if issued_mma:
+            choices.append("mma")
+        c = rnd.choice(choices)
+        if c == "load":
+            kind, t, bars = pending.pop(rnd.randrange(len(pending)))
+            done[kind].add(t)
+            for b in bars:
+                B[b].arrive()
+        elif c == "mma":
+            kind, t, bars = issued_mma.pop(0)  # tcgen05 MMAs complete in issue order
+            if kind != "Drain":
+                done[kind].add(t)
+            for b in bars:
+                B[b].arrive()
+        else:
+            try:
+                next(c)
+            except StopIteration:
+                alive.remove(c)
+    assert done["PV"] == set(range(n_tiles))
+
+
+@pytest.mark.parametrize("n_tiles", [0, 1, 2, 3, 7, 16])
+def test_warp_specialized_protocol_has_no_deadlock_or_early_reuse(n_tiles: int) -> None:
+    for seed in range(40):
+        _simulate(n_tiles, seed)
