@@ -113,6 +113,27 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+// Paired fp32 arithmetic of sm_100 (fma / add on two lanes of a 64-bit register pair): each
+// lane is the IEEE round-to-nearest result of its scalar operation.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -387,18 +408,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       // tile) skip the per-key mask: the raw maximum is scaled once and each P is one FMA
       // and one exp2. Others mask by select and scale every score.
       const bool fast = key0 + kN <= lim && p.scale_log2 > 0.f;
-      float mt = -INFINITY;
+      // row maximum over 8 independent chains (fmaxf is exact: the order does not matter)
+      float mx[8];
       if (fast) {
 #pragma unroll
-        for (int c = 0; c < kN; ++c) mt = fmaxf(mt, sv[c]);
-        mt *= p.scale_log2;
+        for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+#pragma unroll
+        for (int c = 8; c < kN; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
       } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
         for (int c = 0; c < kN; ++c) {
           sv[c] = key0 + c < lim ? sv[c] * p.scale_log2 : -INFINITY;
-          mt = fmaxf(mt, sv[c]);
+          mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
         }
       }
+      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                       fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      if (fast) mt *= p.scale_log2;
       // The running maximum moves only past a margin: P = 2^(s - m) stays <= 2^kRescaleLog2,
       // and O needs rescaling only on the tiles where a row's maximum jumps.
       float m_new = m_run;
@@ -408,15 +436,20 @@ __global__ void __launch_bounds__(kThreads, 2)
         m_new = mt;
       }
       const float alpha = rescale ? fast_exp2(m_run - m_new) : 1.f;
-      float ls = 0.f;
       uint32_t pk[kN / 2];  // P as packed pairs
+      uint64_t acc[4];      // 4 independent paired partial sums of P
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = 0ull;  // +0.0f in both lanes
       if (fast) {
-        const float neg_m = -m_new;  // finite: 64 visible keys
+        const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t neg_m2 = f2_pack(-m_new, -m_new);  // finite: 64 visible keys
 #pragma unroll
         for (int c = 0; c < kN; c += 2) {
-          const float a = fast_exp2(fmaf(sv[c], p.scale_log2, neg_m));
-          const float b = fast_exp2(fmaf(sv[c + 1], p.scale_log2, neg_m));
-          ls += a + b;
+          float xa, xb;
+          f2_unpack(f2_fma(f2_pack(sv[c], sv[c + 1]), scale2, neg_m2), xa, xb);
+          const float a = fast_exp2(xa);
+          const float b = fast_exp2(xb);
+          acc[(c / 2) & 3] = f2_add(acc[(c / 2) & 3], f2_pack(a, b));
           pk[c / 2] = MmaOp<T>::pack(a, b);
         }
       } else {
@@ -424,10 +457,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kN; c += 2) {
           const float a = sv[c] == -INFINITY ? 0.f : fast_exp2(sv[c] - m_new);
           const float b = sv[c + 1] == -INFINITY ? 0.f : fast_exp2(sv[c + 1] - m_new);
-          ls += a + b;
+          acc[(c / 2) & 3] = f2_add(acc[(c / 2) & 3], f2_pack(a, b));
           pk[c / 2] = MmaOp<T>::pack(a, b);
         }
       }
+      float ls_a, ls_b;
+      f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), ls_a, ls_b);
+      const float ls = ls_a + ls_b;
       l_run = l_run * alpha + ls;
       m_run = m_new;
       // P V(j - 1) complete: the P buffer and O are free
