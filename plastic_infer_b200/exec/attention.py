@@ -110,7 +110,9 @@ def paged_attention_v1(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Te
     Semantics of the reference (attention.py:151-190), including SDPA's top-left
     causal alignment: with causal=True a query at row i sees keys 0..i, so a single
     causal query sees only key 0. Decode callers pass causal=False
-    (src/plastic_infer/exec/runner_paged.py:254-255).
+    (src/plastic_infer/exec/runner_paged.py:254-255). One query runs the paged decode
+    kernel; several (prefill) run the tcgen05 paged prefill kernel straight from the pool
+    when it covers the shape (bf16/f16, head_dim 64/128, pages of 16/32, G in 1/2/4/8/16).
     """
     n_kv = len(block_table) * page_size if kv_num_tokens is None else kv_num_tokens
     if not block_table:
@@ -128,7 +130,16 @@ def paged_attention_v1(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Te
         ctx_t = torch.tensor([ctx], dtype=torch.int32, device=kp.device)
         out = kernels.paged_decode_attention(q.reshape(1, Hq, D), kp, vp, bt.view(1, -1), ctx_t)
         return out.view(1, 1, Hq, D)
-    # Prefill: reference algorithm over the kernel gather.
+    # Prefill straight from the pool on the tcgen05 kernel (SDPA's top-left causal mask is
+    # its causal mode with q_start 0); shapes it does not cover keep the reference algorithm
+    # (gather, repeat_interleave, SDPA) over the kernel gather.
+    kp = physical_pool(k_pages)
+    if n_kv > 0 and kernels.prefill_supported(q, kp):
+        vp = physical_pool(v_pages)
+        n_pages = -(-n_kv // page_size)
+        bt = _table_tensor(block_table[:n_pages], kp.device)
+        return kernels.paged_prefill_attention(q, kp, vp, bt, n_kv, q_start=0, causal=causal,
+                                               impl="tc")
     k, v = gather_paged_kv(k_pages, v_pages, block_table, page_size, n_kv)
     q_t = q.transpose(1, 2)
     k_t = k.transpose(1, 2)

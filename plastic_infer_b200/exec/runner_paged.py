@@ -55,9 +55,17 @@ def _attn_paged(q: torch.Tensor, cache: KVRequestCache, layer_idx: int, store: K
         return paged_attention_v1(q, store.gpu.k_pages, store.gpu.v_pages, block_table,
                                   cfg.page_size, kv_num_tokens=kv_num_tokens, causal=causal)
     # Incremental prefill: Q row i sits at position q_start_pos + i and sees
-    # KV[0 : q_start_pos + i + 1] (runner_paged.py:61-95).
+    # KV[0 : q_start_pos + i + 1] (runner_paged.py:61-95). The tcgen05 prefill kernel
+    # applies that mask itself, reading the pages in place; shapes it does not cover keep
+    # the reference's dense mask over the kernel gather.
     q_len = q.shape[1]
     kv_len = kv_num_tokens or (len(block_table) * cfg.page_size)
+    kp = store.gpu.k_phys
+    if kv_len > 0 and kernels.prefill_supported(q, kp):
+        n_pages = -(-kv_len // cfg.page_size)
+        bt = torch.tensor(block_table[:n_pages], dtype=torch.int32, device=kp.device)
+        return kernels.paged_prefill_attention(q, kp, store.gpu.v_phys, bt, kv_len,
+                                               q_start=q_start_pos, causal=True, impl="tc")
     dev = q.device
     q_pos = torch.arange(q_start_pos, q_start_pos + q_len, device=dev)
     kv_pos = torch.arange(kv_len, device=dev)
