@@ -1080,6 +1080,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     from plastic_infer_b200 import kernels
 
     kernels.set_programmatic_launch(not args.no_pdl)
+    kernels.set_decode_attn_ring(args.attn_ring)
     wl = DecodeWorkload(cfg, rank, world, dev)
     wl.fused = args.fused
     if world > 1 and not args.nccl:
@@ -1172,7 +1173,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                         kv_bytes_per_step=round(wl.attn_bytes() * cfg["layers"] * world / 1e9, 3),
                         l2=f"inputs larger than L2 "
                            f"(~{wl.attn_bytes() * cfg['layers'] / 1e9:.0f} GB KV per step), no flush",
-                        cuda_graph=use_graph, programmatic_launch=not args.no_pdl),
+                        cuda_graph=use_graph, programmatic_launch=not args.no_pdl,
+                        attn_ring=args.attn_ring),
             roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peaks["hbm_gbs"],
                           unit="GB/s", frac=round(achieved / peaks["hbm_gbs"], 4),
                           traffic=traffic, kernel="paged_decode_attn_tma_kernel<bf16,128,16>",
@@ -1367,6 +1369,8 @@ def main() -> None:
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch kernels without programmatic dependent launch (each attention "
                          "then computes its work split only after the previous kernel ends)")
+    ap.add_argument("--attn-ring", choices=["auto", "deep", "shallow"], default="auto",
+                    help="page-ring depth of the decode attention (default: chosen per launch)")
     ap.add_argument("--fused", action="store_true",
                     help="one fused append+attention launch per layer instead of index-copy "
                          "then attention (measured slower: 202.9 vs 197.5 us per layer, 4-stage ring)")

@@ -81,9 +81,9 @@ int pi_set_programmatic_launch(int enable);
 /*
  * Page-ring depth of plain pi_paged_decode_attn launches (no reference counterpart).
  * The TMA kernel keeps a ring of page stages per warp. By default (AUTO) a launch
- * whose bound on the work (batch x bt_stride x num_kv_heads) is large uses a
- * two-stage ring with two CTAs per SM, and every other launch a deep ring (4
- * stages at head_dim <= 128) with one CTA per SM. DEEP and SHALLOW force one of the
+ * whose bound on the work (batch x bt_stride x num_kv_heads x num_q_heads /
+ * num_kv_heads) is large uses a two-stage ring with two CTAs per SM, and every other
+ * launch a deep ring (4 stages at head_dim <= 128) with one CTA per SM. DEEP and SHALLOW force one of the
  * two for every plain launch the fast path takes (SHALLOW only where two CTAs fit on
  * an SM), so either instance can be run and checked at any size. Results agree
  * within the attention tolerance; they are not bit-identical because the work split

@@ -1167,10 +1167,14 @@ int launch_fast_ns(const FastParams& fp, const void* k_pool, const void* v_pool,
 // the deeper ring and one CTA per SM: twice the warps would cut each (request, head)
 // segment into twice the pieces, and on a 1-KV-head shard the extra merges cost 10-15%.
 // The host bounds the work by batch x block-table width x KV heads (the context lengths
-// are on the device); 150 pages per warp at 8 warps per SM separates the two regimes.
+// are on the device), weighted by the query heads per KV head G, since a page's MMA and
+// softmax work grows with G: 600 G-weighted pages per warp at 8 warps per SM separates the
+// two regimes. Measured on B200: the 8B batch (G=4, ~120 pages per warp at 8 warps per SM)
+// and the 30B-A3B batch (G=8, ~60) run faster on the shallow ring (182.2 vs 186.8 and
+// 99.4 vs 103.1 us); KV-head shards of the 8B batch on 2..8 GPUs keep the deep ring.
 // pi_set_decode_attn_ring overrides the choice for plain launches.
 template <int D, int S>
-int ring_stages(int batch, int64_t bt_stride, int hkv, bool plain) {
+int ring_stages(int batch, int64_t bt_stride, int hkv, int group, bool plain) {
   constexpr int NS = stages_for<D, S>();
   if constexpr (2 * fast_smem_bytes<D, S, 2>() <= 227 * 1024 && NS > 2) {
     const double pages_bound = static_cast<double>(batch) * static_cast<double>(bt_stride) *
@@ -1178,7 +1182,7 @@ int ring_stages(int batch, int64_t bt_stride, int hkv, bool plain) {
     const double warps2 = static_cast<double>(device_sm_count()) * 2 * kWarps;
     const int ring = decode_attn_ring();
     const bool shallow = ring == PI_ATTN_RING_SHALLOW ||
-                         (ring == PI_ATTN_RING_AUTO && pages_bound >= 150.0 * warps2);
+                         (ring == PI_ATTN_RING_AUTO && pages_bound * group >= 600.0 * warps2);
     if (plain && shallow) return 2;
   }
   return NS;
@@ -1190,7 +1194,7 @@ int launch_fast(const FastParams& fp, const void* k_pool, const void* v_pool, in
   constexpr int NS = stages_for<D, S>();
   const bool plain = fp.slot_mapping == nullptr && fp.ag.world == 0;
   if constexpr (NS > 2) {
-    if (ring_stages<D, S>(fp.batch, fp.bt_stride, fp.hkv, plain) == 2)
+    if (ring_stages<D, S>(fp.batch, fp.bt_stride, fp.hkv, fp.group, plain) == 2)
       return launch_fast_ns<T, D, S, 2>(fp, k_pool, v_pool, rows, dtype, stream);
   }
   return launch_fast_ns<T, D, S, NS>(fp, k_pool, v_pool, rows, dtype, stream);
@@ -1386,7 +1390,8 @@ extern "C" int pi_paged_decode_attn_ring_stages(int batch, int64_t bt_stride, in
                   num_pages))
     return 0;
 #define PI_RING(D, S) \
-  if (head_dim == D && page_size == S) return ring_stages<D, S>(batch, bt_stride, num_kv_heads, true);
+  if (head_dim == D && page_size == S)                                                        \
+    return ring_stages<D, S>(batch, bt_stride, num_kv_heads, num_q_heads / num_kv_heads, true);
   PI_RING(64, 16)
   PI_RING(128, 16)
   PI_RING(256, 16)

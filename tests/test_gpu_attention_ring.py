@@ -4,7 +4,7 @@ The fast path has two instances per head shape: a deep ring (4 stages per warp a
 head_dim <= 128, one CTA per SM) and a shallow ring (2 stages, two CTAs per SM, whose
 split-KV merge stages its partial records through the smaller ring in different
 batches). By default a plain launch picks the shallow ring when batch x block-table
-width x KV heads is large, which is the case for the 8B-shape decode batch the
+width x KV heads x G is large, which is the case for the 8B-shape decode batch the
 benchmark times (64 requests, contexts uniform in [512, 8192]). These tests run that
 exact batch through the automatic choice and through each forced instance, a
 1-KV-head shard (one rank's share at 8 GPUs) above the shallow threshold, and every
@@ -100,10 +100,11 @@ def test_c3_batch_forced_ring_matches_oracle(c3_batch, mode: str, stages: int) -
 
 def test_c3_one_kv_head_shard_above_the_shallow_threshold() -> None:
     # One rank's share at 8 GPUs (1 KV head, its 4 query heads); a padded block-table
-    # width puts batch x width x heads above the threshold, so the automatic choice is
-    # the shallow ring with ~11 pieces per (request, head) segment to merge.
+    # width puts the launch above the threshold (batch x width x KV heads x G >= 600 x
+    # SMs x 2 CTAs x 4 warps), so the automatic choice is the shallow ring with ~11 pieces
+    # per (request, head) segment to merge.
     sms = torch.cuda.get_device_properties(DEV).multi_processor_count
-    width = -(-150 * sms * 2 * 4 // 64) + 8
+    width = -(-600 * sms * 2 * 4 // (64 * 1 * 4)) + 8
     q, kp, vp, tables, ctx, bt = c3_layer(4, 1, width=width, seed=5)
     kernels.set_decode_attn_ring("auto")
     assert _stages(q, kp, bt) == 2
