@@ -16,6 +16,8 @@ and MLP are outside the path and not run.
              the attention outputs are inside the timed region
   roofline   the attention kernel: algorithmic bytes (context K/V + q + out + block
              table) / its CUDA-event time, against the measured HBM copy bandwidth
+  c4         the C4 (Qwen3-30B-A3B shape) KV path on the same ranks: tok/s and its
+             attention roofline, so every N of a scaling run records both shapes
   index_copy C2 microbench (65536-page pool): GB/s at B = 1, 64, 512, a whole 36-layer
              step in one launch (2304) and a large-B sweep; graphs of back-to-back launches
              with L2 flushed before every timed replay
@@ -1141,6 +1143,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     e2e = None
     if not args.skip_e2e:
         e2e = run_e2e(wl, args, stream, use_graph)
+    # the C4 shape on the same ranks (every N of a scaling run records it)
+    c4 = (measure_c4(args, rank, world, dev, peaks)
+          if args.workload == "c3" and not args.skip_c4 else None)
 
     idx = (bench_index_copy(dev, peaks["hbm_gbs"])
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
@@ -1199,6 +1204,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 per_shape=pro, peak=peaks["hbm_gbs"])
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if c4 is not None:
+            line["c4"] = c4
         line["parity"] = parity if parity is not None else dict(
             status="not checked in this run",
             why=("the check runs in the N=1 CPU baseline leg; the sharded path is checked by "
@@ -1215,6 +1222,63 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         barrier(world)
     if parity is not None and parity["status"] != "ok":
         raise SystemExit("parity check of the timed step failed: " + json.dumps(parity))
+
+
+def measure_c4(args, rank: int, world: int, dev: torch.device, peaks: dict) -> dict:
+    """The C4 (Qwen3-30B-A3B shape) KV path on the same ranks as the C3 line: the same
+    sharding (a KV head per rank is replicated when there are fewer KV heads than ranks),
+    gather and graph capture; device time is the max over ranks."""
+    from plastic_infer_b200 import kernels
+
+    cfg = dict(C4)
+    wl = DecodeWorkload(cfg, rank, world, dev)
+    if world > 1 and not args.nccl:
+        wl.use_peer_gather()
+    stream = torch.cuda.current_stream()
+    for _ in range(max(1, args.warmup)):
+        wl.step()
+    torch.cuda.synchronize()
+    use_graph = not args.no_graph and (world == 1 or wl.exchange is not None)
+    step_fn, g_step, g_attn = wl.step, None, None
+    if use_graph:
+        g_step = graph_of(wl.step)
+        step_fn = g_step.replay
+        for _ in range(args.warmup):
+            step_fn()
+    barrier(world)
+    ms = max_over_ranks(time_region(step_fn, args.steps, stream, world), world)
+    attn_fn = lambda: wl.step(attention=True, copy=False, gather=False)  # noqa: E731
+    if use_graph:
+        g_attn = graph_of(attn_fn)
+        attn_fn = g_attn.replay
+    reps = max(2, args.steps)
+    attn_ms = max_over_ranks(time_region(attn_fn, reps, stream, world) / (reps * cfg["layers"]),
+                             world)
+    achieved = wl.attn_bytes() / (attn_ms * 1e-3) / 1e9
+    D, S = cfg["head_dim"], cfg["page_size"]
+    ring = kernels.decode_attn_ring_stages(cfg["batch"], wl.block_tables.shape[2], wl.hq, wl.hkv,
+                                           D, S, wl.k_pool.shape[0], torch.bfloat16)
+    res = dict(workload=cfg["desc"], metric=cfg["metric"],
+               value=round(cfg["batch"] * args.steps / (ms * 1e-3), 1), unit="tok/s",
+               n_gpus=world, ms_per_step=round(ms / args.steps, 4),
+               parallelism=(f"kv-head shard x{world}" + (" (KV heads replicated)"
+                                                         if world > cfg["hkv"] else "")
+                            if world > 1 else "single gpu"),
+               roofline=dict(bound="hbm", kernel="paged_decode_attn_tma_kernel<bf16,128,16>",
+                             ring_stages=ring, us_per_launch=round(attn_ms * 1e3, 2),
+                             algorithmic_bytes_per_launch=int(wl.attn_bytes()),
+                             achieved=round(achieved, 1), peak=peaks["hbm_gbs"], unit="GB/s",
+                             frac=round(achieved / peaks["hbm_gbs"], 4)))
+    step_fn = attn_fn = None
+    del g_step, g_attn
+    torch.cuda.synchronize()
+    barrier(world)
+    if wl.exchange is not None:
+        wl.exchange.close()
+        barrier(world)
+    del wl
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_e2e(wl: DecodeWorkload, args, stream, use_graph: bool = False) -> dict:
@@ -1343,6 +1407,8 @@ def main() -> None:
     ap.add_argument("--skip-c2", action="store_true", help="skip the index-copy microbench")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the host-buffer e2e run")
+    ap.add_argument("--skip-c4", action="store_true",
+                    help="skip the C4 (Qwen3-30B-A3B shape) line inside the C3 run")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers per step (default: the workload's; fewer only for profiling)")
     ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
