@@ -17,7 +17,10 @@ and MLP are outside the path and not run.
   roofline   the attention kernel: algorithmic bytes (context K/V + q + out + block
              table) / its CUDA-event time, against the measured HBM copy bandwidth
   c4         the C4 (Qwen3-30B-A3B shape) KV path on the same ranks: tok/s and its
-             attention roofline, so every N of a scaling run records both shapes
+             attention roofline
+  c5         the C5 long-context decode through the KV store API on the same ranks (KV
+             heads sharded, each rank streaming its own host chunks): tok/s and the
+             host-link roofline; so every N of a scaling run records C3, C4 and C5
   index_copy C2 microbench (65536-page pool): GB/s at B = 1, 64, 512, a whole 36-layer
              step in one launch (2304) and a large-B sweep; graphs of back-to-back launches
              with L2 flushed before every timed replay
@@ -920,21 +923,22 @@ def run_c2_only(args, dev: torch.device) -> None:
     print(json.dumps(dict(profile=True, c2_batches=list(C2["batches"]))), flush=True)
 
 
-def c5_prefill(cfg: dict, dev: torch.device):
-    """C5 state through the host KV store API: B requests of `ctx` tokens, written chunk
-    by chunk into a device pool that holds `pool_frac` of all pages; every chunk is sunk
-    to the pinned host store as it completes, and the oldest sunk chunks are evicted to
-    make room for the next one. Returns (store, caches, decoder)."""
+def c5_prefill(cfg: dict, dev: torch.device, hkv: int):
+    """C5 state of one rank through the host KV store API: B requests of `ctx` tokens and
+    this rank's `hkv` KV heads, written chunk by chunk into a device pool that holds
+    `pool_frac` of all pages; every chunk is sunk to the pinned host store as it completes,
+    and the oldest sunk chunks are evicted to make room for the next one. Returns
+    (store, caches, decoder)."""
     from plastic_infer_b200 import kernels
     from plastic_infer_b200.decode import HostStoreDecoder
     from plastic_infer_b200.kv.kv_store import KVConfig, KVStore
 
-    L, B, S, D, H = (cfg[x] for x in ("layers", "batch", "page_size", "head_dim", "hkv"))
+    L, B, S, D = (cfg[x] for x in ("layers", "batch", "page_size", "head_dim"))
     ppc = cfg["pages_per_chunk"]
     tpc = S * ppc
     total_pages = L * B * cfg["ctx"] // S
     pool = int(cfg["pool_frac"] * total_pages)
-    kvc = KVConfig(n_layers=L, n_kv_heads=H, head_dim=D, page_size=S, pages_per_chunk=ppc,
+    kvc = KVConfig(n_layers=L, n_kv_heads=hkv, head_dim=D, page_size=S, pages_per_chunk=ppc,
                    max_pages=pool, max_host_chunks=B * (cfg["ctx"] // tpc) + B,
                    dtype=torch.bfloat16, device=dev)
     store = KVStore(kvc)
@@ -942,21 +946,24 @@ def c5_prefill(cfg: dict, dev: torch.device):
     # headroom for one decode step's new pages (a page per layer per request)
     dec = HostStoreDecoder(store, caches, budget_pages=pool - L * B)
     g = torch.Generator(device=dev).manual_seed(cfg["seed"])
-    rows_k = torch.empty((tpc * L, H, D), dtype=torch.bfloat16, device=dev)
+    rows_k = torch.empty((L * tpc, hkv, D), dtype=torch.bfloat16, device=dev)
     rows_v = torch.empty_like(rows_k)
     rng = np.random.default_rng(cfg["seed"])
     chunk_pages = L * ppc
+    offs = np.arange(tpc, dtype=np.int64)
     for c in range(cfg["ctx"] // tpc):
         for cache in caches:
             dec.evict_to(pool - chunk_pages)  # room for this chunk
             start = cache.length
             cache.reserve_tokens(tpc)
-            slots = torch.tensor([cache.block_table.slot(l, start + t)
-                                  for t in range(tpc) for l in range(L)],
-                                 dtype=torch.int64, device=dev)
+            # slots of the chunk's tokens in every layer (layer-major rows)
+            pos = start + offs
+            slots = np.concatenate([np.asarray(cache.block_table.pages[l], dtype=np.int64)[pos // S] * S
+                                    + pos % S for l in range(L)])
             rows_k.normal_(generator=g)
             rows_v.normal_(generator=g)
-            kernels.kv_index_copy(store.gpu.k_phys, store.gpu.v_phys, rows_k, rows_v, slots)
+            kernels.kv_index_copy(store.gpu.k_phys, store.gpu.v_phys, rows_k, rows_v,
+                                  torch.from_numpy(slots).to(dev))
             cache.extend_token_ids([int(x) for x in rng.integers(0, 151936, tpc)])
             store.sink_completed_chunks_async(cache)
     dec.evict_to(dec.budget)
@@ -964,86 +971,129 @@ def c5_prefill(cfg: dict, dev: torch.device):
     return store, caches, dec
 
 
-def run_c5(args, rank: int, world: int, dev: torch.device) -> None:
-    """C5 long-context offload line (rank 0, one GPU), through the KV store API.
-
-    Every request has most of its KV in the pinned host store. Each decode step runs
-    HostStoreDecoder: per layer the new K/V rows are written, and every request is
-    attended by host-stream attention over its evicted chunks (read in place over the
-    host link) plus its device tail; completed chunks are sunk on the store's side
-    stream and evicted to the pool budget. The roofline is the host link: host bytes
-    read per step / step time against a pinned 1 GiB host->device copy measured here.
-    """
-    if rank != 0:
-        return
-    cfg = dict(C5)
-    if args.layers:
-        cfg["layers"] = args.layers
+def host_link_gbs(dev: torch.device) -> float:
+    """Pinned 1 GiB host->device copy rate of this GPU's link (GB/s)."""
     h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
     d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
     d.copy_(h)
     torch.cuda.synchronize()
-    link = 1.0 / (time_region(lambda: d.copy_(h, non_blocking=True), 3,
-                              torch.cuda.current_stream()) / 3 * 1e-3) * (1 << 30) / 1e9
+    ms = time_region(lambda: d.copy_(h, non_blocking=True), 3, torch.cuda.current_stream()) / 3
     del h, d
-    t0 = time.perf_counter()
-    store, caches, dec = c5_prefill(cfg, dev)
-    prefill_s = time.perf_counter() - t0
-    L, B, D, H, Hq = (cfg[x] for x in ("layers", "batch", "head_dim", "hkv", "hq"))
-    g = torch.Generator(device=dev).manual_seed(cfg["seed"] + 1)
-    q = torch.randn((L, B, Hq, D), dtype=torch.bfloat16, device=dev, generator=g)
-    kn = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
-    vn = torch.randn((L, B, H, D), dtype=torch.bfloat16, device=dev, generator=g)
-    out = torch.empty_like(q)
-    rng = np.random.default_rng(cfg["seed"] + 2)
+    return (1 << 30) / (ms * 1e-3) / 1e9
+
+
+def measure_c5(args, rank: int, world: int, dev: torch.device, steps: int, warmup: int) -> dict:
+    """C5 long-context decode through the KV store API on every rank of the job.
+
+    KV heads are split over the ranks (rank r keeps heads [r*8/N, (r+1)*8/N) of every
+    request, its share of the pool, and its own pinned host store), so each rank streams its
+    own host chunks over its own host link; per layer the ranks' attention outputs are
+    all-gathered (NCCL) before o_proj would run. Each step runs HostStoreDecoder: per layer
+    the new K/V rows are written and every request is attended by host-stream attention over
+    its evicted chunks (read in place) plus its device tail; completed chunks are sunk on
+    the store's side stream and evicted to the pool budget. The roofline is the host link:
+    host bytes read per step over the step time, against the sum of the ranks' measured
+    pinned copy rates. A rank that fails to build its state makes every rank skip the
+    timed part (no collective is left waiting).
+    """
+    import torch.distributed as dist
+
+    from plastic_infer_b200.dist import head_shard
+
+    cfg = dict(C5)
+    if args.layers:
+        cfg["layers"] = args.layers
+    L, B, D, Hkv, Hq = (cfg[x] for x in ("layers", "batch", "head_dim", "hkv", "hq"))
     tpc = cfg["page_size"] * cfg["pages_per_chunk"]
-    chunk_layer_bytes = 2 * tpc * H * D * 2          # K + V of one chunk of one layer
+    err = ""
+    try:
+        shard = head_shard(Hq, Hkv, world, rank)
+        link = host_link_gbs(dev)
+        t0 = time.perf_counter()
+        store, caches, dec = c5_prefill(cfg, dev, shard.n_kv)
+        prefill_s = time.perf_counter() - t0
+    except Exception as e:  # noqa: BLE001 - reported in the line, every rank skips
+        err = f"{type(e).__name__}: {e}"[:200]
+    ok = torch.tensor([0.0 if err else 1.0], device=dev)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if ok.item() < 1.0:
+        return dict(skipped=err or "another rank could not build its C5 state")
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"] + 1)
+    q = torch.randn((L, B, shard.n_q, D), dtype=torch.bfloat16, device=dev, generator=g)
+    kn = torch.randn((L, B, shard.n_kv, D), dtype=torch.bfloat16, device=dev, generator=g)
+    vn = torch.randn((L, B, shard.n_kv, D), dtype=torch.bfloat16, device=dev, generator=g)
+    out = torch.empty_like(q)
+    gathered = (torch.empty((L, world * B, shard.n_q, D), dtype=torch.bfloat16, device=dev)
+                if world > 1 else None)
+    rng = np.random.default_rng(cfg["seed"] + 2)
+    chunk_layer_bytes = 2 * tpc * shard.n_kv * D * 2    # K + V of one chunk of one layer
 
     def step():
-        dec.step(q, kn, vn, token_ids=[int(x) for x in rng.integers(0, 151936, B)], out=out)
+        ids = [int(x) for x in rng.integers(0, 151936, B)]
+        dec.begin_step(ids)
+        for layer in range(L):
+            dec.attend(layer, q[layer], kn[layer], vn[layer], out=out[layer])
+            if gathered is not None:
+                dist.all_gather_into_tensor(gathered[layer], out[layer])
+        dec.end_step()
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     host_bytes = 0
-    with ClockSampler([dev.index or 0]) as clk:
+    barrier(world)
+    with ClockSampler(list(range(world)) if rank == 0 else None) as clk:
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.all_reduce(torch.zeros(1, device=dev))
         start.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             host_bytes += sum(c.evicted_chunks for c in caches) * chunk_layer_bytes * L
             step()
         end.record()
         torch.cuda.synchronize()
         ms = start.elapsed_time(end)
-    ms_step = ms / args.steps
-    hb = host_bytes / args.steps
-    link_gbs = hb / (ms_step * 1e-3) / 1e9
-    resident = sum(c.length - c.evicted_chunks * tpc for c in caches)
-    line = dict(
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+    totals = torch.tensor([float(host_bytes), link], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(totals)
+    hb, link_sum = float(totals[0]) / steps, float(totals[1])
+    ms_step = ms / steps
+    res = dict(
         metric="decode tok/s (long-context host offload, Qwen3-8B attention shape)",
-        value=round(B * args.steps / (ms * 1e-3), 2), unit="tok/s", n_gpus=1,
-        steps=args.steps, warmup=args.warmup, ms_per_step=round(ms_step, 2), higher_is_better=True,
-        scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic",
-        config=dict(workload=f"C5 long-context offload through the KV store API: B={B} x "
-                    f"{cfg['ctx']} tokens, {L} layers, {Hq}q/{H}kv heads, head_dim {D}, page "
-                    f"{cfg['page_size']}; device pool = {cfg['pool_frac']:.0%} of all pages; "
-                    "HostStoreDecoder: per layer index-copy + host-stream attention over the "
-                    "evicted chunks (pinned, read in place) and the device tail; async sink + "
-                    "eviction to the budget after every step",
-                    pool_pages=store.gpu.total_pages, budget_pages=dec.budget,
-                    evicted_chunks=sum(c.evicted_chunks for c in caches),
-                    resident_tokens=resident, host_store_gb=round(
-                        store.host_cache_size * 2 * L * chunk_layer_bytes / 2 / 1e9, 1),
-                    prefill_s=round(prefill_s, 1)),
-        roofline=dict(bound="host link", achieved=round(link_gbs, 1), peak=round(link, 1),
-                      unit="GB/s", frac=round(link_gbs / link, 3),
-                      peak_source="pinned 1 GiB host->device copy measured in this run"),
-        host_bytes_read_per_step=int(hb),
-        clocks=clk.summary(),
-    )
-    print(json.dumps(line), flush=True)
+        value=round(B * steps / (ms * 1e-3), 2), unit="tok/s", n_gpus=world, steps=steps,
+        warmup=warmup, ms_per_step=round(ms_step, 2),
+        workload=f"C5 through the KV store API: B={B} x {cfg['ctx']} tokens, {L} layers, "
+                 f"{Hq}q/{Hkv}kv heads (kv-head shard x{world}), head_dim {D}; device pool = "
+                 f"{cfg['pool_frac']:.0%} of all pages; per layer index-copy + host-stream "
+                 "attention over the evicted chunks (pinned, read in place) and the device "
+                 "tail; async sink + eviction to the pool budget after every step",
+        evicted_chunks_per_rank=sum(c.evicted_chunks for c in caches),
+        prefill_s=round(prefill_s, 1),
+        roofline=dict(bound="host link", achieved=round(hb / (ms_step * 1e-3) / 1e9, 1),
+                      peak=round(link_sum, 1), unit="GB/s",
+                      frac=round(hb / (ms_step * 1e-3) / 1e9 / link_sum, 3),
+                      peak_source="sum of the ranks' pinned 1 GiB host->device copies, measured "
+                                  "in this run"),
+        host_bytes_read_per_step=int(hb), clocks=clk.summary())
+    del store, caches, dec, q, kn, vn, out, gathered
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_c5(args, rank: int, world: int, dev: torch.device) -> None:
+    """C5 long-context offload line (`--workload c5`), on every rank of the job."""
+    res = measure_c5(args, rank, world, dev, args.steps, args.warmup)
+    if rank == 0:
+        line = dict(res)
+        workload = line.pop("workload", "C5")
+        line.update(scaling="strong", higher_is_better=True, vs_baseline=None, dtype="bf16",
+                    data="synthetic", config=dict(workload=workload))
+        print(json.dumps(line), flush=True)
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
@@ -1143,9 +1193,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     e2e = None
     if not args.skip_e2e:
         e2e = run_e2e(wl, args, stream, use_graph)
-    # the C4 shape on the same ranks (every N of a scaling run records it)
+    # the C4 and C5 shapes on the same ranks (every N of a scaling run records them); C5
+    # with a few steps (one takes ~0.6 s on one GPU)
     c4 = (measure_c4(args, rank, world, dev, peaks)
           if args.workload == "c3" and not args.skip_c4 else None)
+    c5 = (measure_c5(args, rank, world, dev, steps=min(args.steps, 5), warmup=2)
+          if args.workload == "c3" and not args.skip_c5 else None)
 
     idx = (bench_index_copy(dev, peaks["hbm_gbs"])
            if (world == 1 and not args.skip_c2 and args.workload == "c3") else None)
@@ -1206,6 +1259,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             line["cpu_baseline"] = cpu
         if c4 is not None:
             line["c4"] = c4
+        if c5 is not None:
+            line["c5"] = c5
         line["parity"] = parity if parity is not None else dict(
             status="not checked in this run",
             why=("the check runs in the N=1 CPU baseline leg; the sharded path is checked by "
@@ -1409,6 +1464,8 @@ def main() -> None:
     ap.add_argument("--skip-e2e", action="store_true", help="skip the host-buffer e2e run")
     ap.add_argument("--skip-c4", action="store_true",
                     help="skip the C4 (Qwen3-30B-A3B shape) line inside the C3 run")
+    ap.add_argument("--skip-c5", action="store_true",
+                    help="skip the C5 (long context through the host store) line inside the C3 run")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers per step (default: the workload's; fewer only for profiling)")
     ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",

@@ -138,9 +138,14 @@ class KVRequestCache:
         (src/plastic_infer/exec/runner_paged.py:98-109, 222-226): those zeros are
         always overwritten by _write_kv_layer, so skipping them leaves the same pool.
         """
-        for _ in range(n_tokens):
-            self._ensure_page(self._length)
-            self._length += 1
+        if n_tokens <= 0:
+            return
+        S = self.cfg.page_size
+        # Pages in the order the reference's per-token appends take them: page p of every
+        # layer (layer 0 first), then page p + 1, ...
+        for page_idx in range(self._length // S, (self._length + n_tokens - 1) // S + 1):
+            self._ensure_page(page_idx * S)
+        self._length += n_tokens
 
     def append_token(self, k_token: torch.Tensor, v_token: torch.Tensor) -> None:
         """Append one token's K/V for all layers; k_token, v_token: [n_layers, n_kv_heads, head_dim]."""
