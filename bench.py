@@ -992,9 +992,9 @@ def measure_c5(args, rank: int, world: int, dev: torch.device, steps: int, warmu
     the new K/V rows are written and every request is attended by host-stream attention over
     its evicted chunks (read in place) plus its device tail; completed chunks are sunk on
     the store's side stream and evicted to the pool budget. The roofline is the host link:
-    host bytes read per step over the step time, against the sum of the ranks' measured
-    pinned copy rates. A rank that fails to build its state makes every rank skip the
-    timed part (no collective is left waiting).
+    host bytes read per step over the step time, against the pinned copy rate the ranks
+    reach together (each copying 1 GiB at the same time). A rank that fails to build its
+    state makes every rank skip the timed part (no collective is left waiting).
     """
     import torch.distributed as dist
 
@@ -1008,7 +1008,6 @@ def measure_c5(args, rank: int, world: int, dev: torch.device, steps: int, warmu
     err = ""
     try:
         shard = head_shard(Hq, Hkv, world, rank)
-        link = host_link_gbs(dev)
         t0 = time.perf_counter()
         store, caches, dec = c5_prefill(cfg, dev, shard.n_kv)
         prefill_s = time.perf_counter() - t0
@@ -1019,6 +1018,10 @@ def measure_c5(args, rank: int, world: int, dev: torch.device, steps: int, warmu
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     if ok.item() < 1.0:
         return dict(skipped=err or "another rank could not build its C5 state")
+    # every rank copies at the same time: the host side of the links is shared, so the
+    # peak is what the ranks reach together, not one link alone
+    barrier(world)
+    link = host_link_gbs(dev)
     g = torch.Generator(device=dev).manual_seed(cfg["seed"] + 1)
     q = torch.randn((L, B, shard.n_q, D), dtype=torch.bfloat16, device=dev, generator=g)
     kn = torch.randn((L, B, shard.n_kv, D), dtype=torch.bfloat16, device=dev, generator=g)
@@ -1077,8 +1080,8 @@ def measure_c5(args, rank: int, world: int, dev: torch.device, steps: int, warmu
         roofline=dict(bound="host link", achieved=round(hb / (ms_step * 1e-3) / 1e9, 1),
                       peak=round(link_sum, 1), unit="GB/s",
                       frac=round(hb / (ms_step * 1e-3) / 1e9 / link_sum, 3),
-                      peak_source="sum of the ranks' pinned 1 GiB host->device copies, measured "
-                                  "in this run"),
+                      peak_source="sum over the ranks of a pinned 1 GiB host->device copy, all "
+                                  "ranks copying at once, measured in this run"),
         host_bytes_read_per_step=int(hb), clocks=clk.summary())
     del store, caches, dec, q, kn, vn, out, gathered
     torch.cuda.empty_cache()
