@@ -128,13 +128,16 @@ def test_index_copy_misaligned_falls_back_to_narrow_vectors() -> None:
 
 
 # Geometries that reach every launch shape of the kernel: one chunk per token (a single
-# KV head), a partial last chunk (3 heads x 10 vectors), rows whose vector count is not a
-# power of two (division path), two chunks per warp (whole 36-layer step in one launch)
-# and four chunks per pass with a grid-stride loop (65,536 tokens).
+# KV head, where a pass of two chunks spans two tokens), a partial last chunk (3 heads x
+# 10 vectors), rows whose vector count is not a power of two (division path), one chunk
+# per warp (small launches), two chunks per pass of one token (the whole 36-layer step in
+# one launch) and a grid-stride loop beyond one wave (65,536 tokens).
 GEOMETRIES = [
     # name, pages, kv_heads, page_size, head_dim, dtype, tokens
     ("c4_four_heads", 512, 4, 16, 128, torch.bfloat16, 128),
     ("one_head", 256, 1, 16, 128, torch.bfloat16, 300),
+    ("one_head_two_tokens_per_pass", 256, 1, 16, 128, torch.bfloat16, 3000),
+    ("three_chunks_per_token", 512, 3, 16, 128, torch.bfloat16, 1500),
     ("d96_rows_of_12_vectors", 256, 8, 16, 96, torch.bfloat16, 200),
     ("h3_d80_partial_chunk", 256, 3, 16, 80, torch.float16, 333),
     ("d64_page32", 256, 8, 32, 64, torch.bfloat16, 1000),
