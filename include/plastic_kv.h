@@ -317,10 +317,12 @@ int pi_paged_prefill_attn(void* out, const void* q, const void* k_pool, const vo
 
 /*
  * pi_paged_prefill_attn on the 5th-generation tensor cores (tcgen05): same arguments,
- * semantics, shape coverage and errors, plus q must be 16-byte aligned with
- * q_tok_stride a multiple of 8 elements (PI_ERR_MISALIGNED otherwise). A CTA takes 128
- * query rows of one KV head; S = Q K^T and O = P V accumulate in tensor memory, K/V
- * pages stream through a TMA ring, every wait is bounded (PI_ERR_TIMEOUT through `err`).
+ * semantics, shape coverage and errors, plus q and out must be 16-byte aligned with
+ * q_tok_stride and out_tok_stride multiples of 8 elements (PI_ERR_MISALIGNED otherwise):
+ * both move by TMA. A CTA takes 128 query rows of one KV head; S = Q K^T and O = P V
+ * accumulate in tensor memory, K/V pages stream through a TMA ring, every wait is bounded
+ * (PI_ERR_TIMEOUT through `err`). Only the q_len x num_q_heads x head_dim output rows are
+ * written.
  * Same replaced reference code as pi_paged_prefill_attn
  * (src/plastic_infer/exec/runner_paged.py:36-95).
  */

@@ -9,8 +9,9 @@
 // CTA = (block of 128 / G query tokens, KV head): 128 query rows, row r = token * G + g,
 // one row per TMEM lane. The context streams in tiles of 64 keys (64 / S pages by TMA).
 // Warp-specialized, six warps, synchronized only through mbarriers (full / empty pairs):
-//   - load warp: TMA of K(t) and V(t) into 2-slot rings, each slot reloaded once the MMA
-//     that read it has completed;
+//   - load warp: TMA of the Q tile (a 3-D box of G heads x 128 / G tokens per 64 columns,
+//     zero past q_len), then K(t) and V(t) into 2-slot rings, each slot reloaded once the
+//     MMA that read it has completed;
 //   - MMA warp (one thread): S(t) = Q K(t)^T into one of two TMEM buffers (columns [0, 64)
 //     and [64, 128)) as soon as K(t) has landed and the softmax has read that buffer's
 //     previous S, then O += P(t - 1) V(t - 1) (columns [128, 128 + D)); kind::f16, M = 128,
@@ -23,8 +24,10 @@
 // and O is rescaled on those rare tiles only (the stale maximum cancels in O / l). Tiles a
 // row sees in full skip the per-key mask (one FMA and one exp2 per score). V rows past the
 // context in the last tile are zeroed before P V (an unused slot may hold NaN, and
-// 0 * NaN is NaN). Warp-collective tcgen05 loads and stores run on a path every thread of
-// the warp takes. The CTA needs 113 KB of shared memory at head_dim 128, so two CTAs share
+// 0 * NaN is NaN). At the end each softmax warp writes its 32 rows of O / l into the Q
+// tile's space and stores them with one TMA store per 64 columns (rows of tokens past q_len
+// are dropped by the store). Warp-collective tcgen05 loads and stores run on a path every
+// thread of the warp takes. The CTA needs 113 KB of shared memory at head_dim 128, so two CTAs share
 // an SM. Every wait is bounded: a timeout sets PI_ERR_TIMEOUT, the roles leave their loops,
 // in-flight loads and MMAs complete, TMEM is freed.
 #include <cudaTypedefs.h>
@@ -36,8 +39,10 @@
 
 namespace pi {
 namespace attn {
-// Cached 2-D tensor map over a physical pool [rows = P*Hkv*S, D] (paged_decode_attn.cu).
+// Cached 2-D tensor map over a physical pool [rows = P*Hkv*S, D], and the driver's tensor-map
+// encoder (paged_decode_attn.cu).
 bool pool_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, int D, int S, int dtype);
+PFN_cuTensorMapEncodeTiled_v12000 get_encode();
 }  // namespace attn
 
 namespace prefill_tc {
@@ -65,7 +70,7 @@ struct Cfg {
   static constexpr int kKVBytes = kBoxes * kKVBoxBytes;   // K or V tile [boxes][64 keys][128 B]
   static constexpr int kPBytes = kM * 128;                // P [128 rows][64 keys] bf16: one box
   static constexpr int kPagesPerTile = kN / S;
-  static constexpr int kBarBytes = 128;  // 15 mbarriers + TMEM address
+  static constexpr int kBarBytes = 144;  // 16 mbarriers + TMEM address
   static constexpr int kLayoutBytes = kQBytes + (kKSlots + kVSlots) * kKVBytes + kPBytes + kBarBytes;
   // Slack for aligning the tiles to 1024 bytes (the 128-byte swizzle's period). 768 bytes
   // covers any base aligned to 256 bytes and keeps two head_dim-128 CTAs on one SM (228 KB,
@@ -181,8 +186,30 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int ch) {
   return static_cast<uint32_t>((ch >> 3) * (128 * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
+// 3-D tiled TMA load global -> shared (coordinates innermost first), completion on `bar`.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int x,
+                                            int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// 3-D tiled TMA store shared -> global; elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(tmap), "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+// Commit this thread's bulk stores and wait until their shared-memory sources have been read.
+__device__ __forceinline__ void tma_store_commit_wait_read() {
+  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 // Barrier slots (mbarriers in shared memory): full / empty pairs of the K and V rings and
-// of the two S buffers, P ready, P V done, and a one-phase drain barrier.
+// of the two S buffers, P ready, P V done, a one-phase drain barrier and Q landed.
 enum Bar : int {
   kKFull = 0,    // [2] K(t) landed (TMA bytes)
   kKEmpty = 2,   // [2] S(t) complete: K slot free (MMA commit)
@@ -193,13 +220,16 @@ enum Bar : int {
   kPFull = 12,   // P(t) in shared memory and O rescaled (4 softmax warps)
   kOFree = 13,   // P V(t) complete: P buffer and O free (MMA commit)
   kDrain = 14,   // every MMA issued has completed (one phase, at the end)
-  kNumBars = 15,
+  kQFull = 15,   // the Q tile landed (TMA bytes, one phase)
+  kNumBars = 16,
 };
 
 template <typename T, int D, int S>
 __global__ void __launch_bounds__(kThreads, 2)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
-                            const __grid_constant__ CUtensorMap tmap_v, const Params p) {
+                            const __grid_constant__ CUtensorMap tmap_v,
+                            const __grid_constant__ CUtensorMap tmap_q,
+                            const __grid_constant__ CUtensorMap tmap_o, const Params p) {
   using C = Cfg<D, S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* qs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -237,8 +267,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int b = 0; b < kNumBars; ++b)
       mbar_init(bar(b), (b == kSEmpty || b == kSEmpty + 1 || b == kPFull) ? kSoftmaxWarps : 1);
     fence_mbar_init();
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    prefetch_tmap(&tmap_q);
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
+  } else if (warp < kSoftmaxWarps && lane == 0) {
+    prefetch_tmap(&tmap_o);
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -247,19 +282,6 @@ __global__ void __launch_bounds__(kThreads, 2)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // Q rows into the swizzled K-major tile; rows past q_len are zero
-  for (int c = tid; c < kM * (D / 8); c += kThreads) {
-    const int r = c / (D / 8);
-    const int ch = c - r * (D / 8);
-    const int tok = t0 + r / G;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (tok < p.q_len)
-      v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
-                                          static_cast<int64_t>(tok) * p.q_tok_stride +
-                                          static_cast<int64_t>(h * G + r % G) * D + ch * 8);
-    *reinterpret_cast<uint4*>(qs + sw128_off(r, ch)) = v;
-  }
-  fence_proxy_async_smem();  // the MMA reads Q through the async proxy
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -273,6 +295,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == kLoadWarp) {
     // ---------------- TMA producer: K(t) and V(t) into slot t % 2 ----------------
     int issued[2] = {0, 0};  // K and V loads issued (tiles 0 .. issued - 1)
+    if (lane == 0 && n_tiles > 0) {
+      // Q rows of this CTA: box (64 columns, G heads, 128 / G tokens) per 64 columns, rows
+      // r = token * G + g in the 128-byte-swizzled K-major layout; tokens past q_len are
+      // filled with zeros.
+      mbar_arrive_expect_tx(bar(kQFull), static_cast<uint32_t>(C::kQBytes));
+#pragma unroll
+      for (int b = 0; b < C::kBoxes; ++b)
+        tma_load_3d(smem_u32(qs) + b * C::kQBoxBytes, &tmap_q, bar(kQFull), 64 * b, h * G, t0);
+    }
     if (lane == 0) {
       for (int t = 0; t < n_tiles; ++t) {
         const int sl = t % kKSlots;
@@ -316,6 +347,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     failed = __syncthreads_or(failed) != 0;
     // after a failure, loads still in flight land before the shared memory is released
     if (failed && lane == 0) {
+      if (n_tiles > 0) mbar_wait_bounded(bar(kQFull), 0);
       for (int kind = 0; kind < 2; ++kind) {
         for (int sl = 0; sl < kKSlots && sl < issued[kind]; ++sl) {
           // the last tile loaded into slot sl: its phase completes after the earlier ones
@@ -353,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         umma_commit(bar(kOFree));
         umma_commit(bar(kVEmpty + sl));
       };
+      if (n_tiles > 0 && !mbar_wait_bounded(bar(kQFull), 0)) failed = true;
       for (int t = 0; t < n_tiles && !failed; ++t) {
         const int sl = t % kKSlots;
         const uint32_t parity = static_cast<uint32_t>((t / kKSlots) & 1);
@@ -523,13 +556,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     failed = __syncthreads_or(failed) != 0;
     tc_fence_after();
     if (!failed) {
-      // The TMEM loads are warp-collective (.sync.aligned): every thread of the warp runs
-      // them on the same path, rows past q_len included (a warp can straddle q_len); only
-      // the stores depend on the row.
-      const bool row_valid = tok < p.q_len;
-      T* orow = static_cast<T*>(p.out) +
-                static_cast<int64_t>(row_valid ? tok : 0) * p.out_tok_stride +
-                static_cast<int64_t>(h * G + r % G) * D;
+      // O / l goes through shared memory (the Q tile's space: every MMA that read it has
+      // completed) in the Q tile's layout, and each warp stores its 32 rows with one TMA
+      // store per 64 columns; rows of tokens past q_len fall outside the tensor and are not
+      // written. The TMEM loads are warp-collective (.sync.aligned): every thread of the
+      // warp runs them, rows past q_len included.
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -541,12 +572,23 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] = 0.f;
         }
-        if (row_valid) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 2)
-            *reinterpret_cast<uint32_t*>(orow + 32 * c + e) =
-                MmaOp<T>::pack(ov[e] * inv, ov[e + 1] * inv);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float* o8 = ov + 8 * q4;
+          *reinterpret_cast<uint4*>(qs + sw128_off(r, 4 * c + q4)) =
+              make_uint4(MmaOp<T>::pack(o8[0] * inv, o8[1] * inv), MmaOp<T>::pack(o8[2] * inv, o8[3] * inv),
+                         MmaOp<T>::pack(o8[4] * inv, o8[5] * inv), MmaOp<T>::pack(o8[6] * inv, o8[7] * inv));
         }
+      }
+      fence_proxy_async_smem();  // the TMA store reads these rows through the async proxy
+      __syncwarp();
+      const int w_tok = t0 + warp * (32 / G);  // this warp's first token
+      if (lane == 0 && w_tok < p.q_len) {        // a box that starts past q_len is skipped
+#pragma unroll
+        for (int b = 0; b < C::kBoxes; ++b)
+          tma_store_3d(&tmap_o, smem_u32(qs) + b * C::kQBoxBytes + warp * 32 * 128, 64 * b, h * G,
+                       w_tok);
+        tma_store_commit_wait_read();
       }
     }
   }
@@ -569,9 +611,29 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 bool configured[64][8] = {};
 
+// 3-D tensor map over a [tokens][heads][D] activation with a token stride of `tok_stride`
+// elements (heads contiguous): box = 64 columns x G heads x `box_tokens` tokens, the
+// 128-byte swizzle (one 128-byte row per (token, head) and 64 columns). Loads outside the
+// tensor read zeros, stores outside it are dropped.
+bool token_tensor_map(CUtensorMap* m, const void* base, int tokens, int heads, int D,
+                      int64_t tok_stride, int G, int box_tokens, int dtype) {
+  auto encode = attn::get_encode();
+  if (!encode) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(tokens)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(tok_stride) * 2};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(G), static_cast<cuuint32_t>(box_tokens)};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType dt =
+      dtype == PI_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <typename T, int D, int S>
 int launch(const Params& p, int n_qblocks, const CUtensorMap& tk, const CUtensorMap& tv,
-           cudaStream_t stream) {
+           const CUtensorMap& tq, const CUtensorMap& to, cudaStream_t stream) {
   using C = Cfg<D, S>;
   auto kern = paged_prefill_tc_kernel<T, D, S>;
   int dev = 0;
@@ -584,7 +646,8 @@ int launch(const Params& p, int n_qblocks, const CUtensorMap& tk, const CUtensor
     configured[dev][slot] = true;
   }
   const cudaError_t e =
-      launch_kernel(kern, dim3(n_qblocks, p.hkv), dim3(kThreads), C::kLaunchSmem, stream, tk, tv, p);
+      launch_kernel(kern, dim3(n_qblocks, p.hkv), dim3(kThreads), C::kLaunchSmem, stream, tk, tv, tq,
+                    to, p);
   return e == cudaSuccess ? PI_OK : PI_ERR_CUDA;
 }
 
@@ -615,14 +678,18 @@ extern "C" int pi_paged_prefill_attn_tc(void* out, const void* q, const void* k_
     return PI_ERR_BAD_SHAPE;  // TMA row coordinate is a 32-bit int
   if (q_len == 0) return PI_OK;
   if (!out || !q || !k_pool || !v_pool || (kv_len > 0 && !block_table)) return PI_ERR_NULL_POINTER;
-  // Q rows are read as 16-byte vectors, outputs written as element pairs
-  if (!aligned(q, 16) || (q_tok_stride % 8) || !aligned(out, 4) || (out_tok_stride % 2) ||
+  // Q and the output move by TMA: 16-byte aligned bases and token strides
+  if (!aligned(q, 16) || (q_tok_stride % 8) || !aligned(out, 16) || (out_tok_stride % 8) ||
       !aligned(k_pool, 16) || !aligned(v_pool, 16))
     return PI_ERR_MISALIGNED;
   const uint64_t rows = static_cast<uint64_t>(num_pages) * num_kv_heads * page_size;
-  CUtensorMap tk, tv;
+  CUtensorMap tk, tv, tq, to;
   if (!attn::pool_tensor_map(&tk, k_pool, rows, head_dim, page_size, dtype) ||
-      !attn::pool_tensor_map(&tv, v_pool, rows, head_dim, page_size, dtype))
+      !attn::pool_tensor_map(&tv, v_pool, rows, head_dim, page_size, dtype) ||
+      !prefill_tc::token_tensor_map(&tq, q, q_len, num_q_heads, head_dim, q_tok_stride, G, 128 / G,
+                                    dtype) ||
+      !prefill_tc::token_tensor_map(&to, out, q_len, num_q_heads, head_dim, out_tok_stride, G,
+                                    32 / G, dtype))
     return PI_ERR_CUDA;
   prefill_tc::Params p;
   p.out = out;
@@ -643,7 +710,7 @@ extern "C" int pi_paged_prefill_attn_tc(void* out, const void* q, const void* k_
   const int n_qblocks = (q_len + p.tokens_per_cta - 1) / p.tokens_per_cta;
 #define PI_PREFILL_TC(T, D, S)                                  \
   if (head_dim == D && page_size == S)                          \
-    return prefill_tc::launch<T, D, S>(p, n_qblocks, tk, tv, stream);
+    return prefill_tc::launch<T, D, S>(p, n_qblocks, tk, tv, tq, to, stream);
   if (dtype == PI_DTYPE_BF16) {
     PI_PREFILL_TC(__nv_bfloat16, 64, 16)
     PI_PREFILL_TC(__nv_bfloat16, 128, 16)

@@ -578,15 +578,22 @@ def paged_prefill_attention(
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     block_table = block_table.contiguous()
-    if impl == "tc" and (q3.data_ptr() % 16 or q3.stride(0) % 8):
-        q3 = q3.contiguous()  # the tcgen05 kernel reads q rows as 16-byte vectors
+    dst = out3
+    if impl == "tc":
+        # the tcgen05 kernel moves q and the output by TMA: 16-byte aligned rows
+        if q3.data_ptr() % 16 or q3.stride(0) % 8:
+            q3 = q3.clone(memory_format=torch.contiguous_format)
+        if dst.data_ptr() % 16 or dst.stride(0) % 8:
+            dst = torch.empty((q_len, Hq, D), dtype=k_pool.dtype, device=q3.device)
     _capi.call(
         "pi_paged_prefill_attn_tc" if impl == "tc" else "pi_paged_prefill_attn",
-        out3.data_ptr(), q3.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        dst.data_ptr(), q3.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_table.data_ptr(), block_table.numel(), q_len, int(kv_len), int(q_start),
         1 if causal else 0, Hq, Hkv, D, S, P, float(scale), dtype_code(k_pool.dtype),
-        q3.stride(0), out3.stride(0), _err_ptr(err), _stream(),
+        q3.stride(0), dst.stride(0), _err_ptr(err), _stream(),
     )
+    if dst is not out3:
+        out3.copy_(dst)
     if out is not None:
         return out
     return out3.unsqueeze(0) if batched else out3

@@ -40,8 +40,7 @@ def test_every_declared_symbol_is_exported(lib: ctypes.CDLL) -> None:
 
 
 def test_exports_are_the_declared_symbols(lib: ctypes.CDLL) -> None:
-    # every exported pi_* symbol is declared in the header, except the tcgen05 prefill,
-    # which stays out of the public boundary until it has run against the oracle
+    # every exported pi_* symbol is declared in the header, and nothing else is exported
     import shutil
     import subprocess
 
@@ -114,6 +113,16 @@ def test_host_validation_rejects_before_launch(lib: ctypes.CDLL) -> None:
     assert pf(*args(4, 16, 6, 2, 128, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_ERR_UNSUPPORTED
     assert pf(*args(4, 17, 8, 2, 128, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_ERR_BAD_SHAPE
     assert pf(*args(0, 16, 8, 2, 128, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_OK
+    # tcgen05 prefill: q and out move by TMA, so both need 16-byte aligned bases and token
+    # strides that are multiples of 8 elements
+    tc = lib.pi_paged_prefill_attn_tc
+    assert tc(*args(0, 16, 8, 2, 128, 16, _capi.PI_DTYPE_BF16, 1)) == _capi.PI_OK
+    ok = list(args(4, 16, 8, 2, 128, 16, _capi.PI_DTYPE_BF16, 1))
+    for i, bad in ((0, ctypes.c_void_p(260)), (1, ctypes.c_void_p(264)), (17, 8 * 128 + 4),
+                   (18, 8 * 128 + 2)):
+        a = list(ok)
+        a[i] = bad
+        assert tc(*a) == _capi.PI_ERR_MISALIGNED, i
     # expert-slot copy: too many banks; nothing to do; null pointers
     ec = lib.pi_expert_slot_copy
     assert ec(fake, fake, fake, 33, fake, fake, 4, None, 1, None, None) == _capi.PI_ERR_BAD_SHAPE

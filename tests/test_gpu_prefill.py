@@ -167,6 +167,33 @@ def test_prefill_strided_q_out_param_and_empty_context(impl: str) -> None:
     assert int(torch.count_nonzero(empty)) == 0
 
 
+@pytest.mark.parametrize("G", [1, 4, 16])
+def test_prefill_tc_output_stays_inside_its_rows(G: int) -> None:
+    # The tcgen05 kernel writes its output tile by TMA store, one 32-row box per warp. With
+    # q_len ending inside a CTA's token block, rows of tokens past q_len must be dropped:
+    # the buffer's rows after the output view keep their sentinel.
+    Hkv, D, S = 2, 128, 16
+    Hq = G * Hkv
+    q_len, kv_len, q_start = 45, 300, 255
+    q, kp, vp, bt, lk, lv, table = _setup(q_len, kv_len, Hq, Hkv, D, S, torch.bfloat16, seed=G)
+    buf = torch.full((q_len + 40, Hq, D), 3.0, dtype=torch.bfloat16, device=DEV)
+    out = kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start, True, out=buf[:q_len],
+                                          impl="tc")
+    torch.cuda.synchronize()
+    assert bool((buf[q_len:] == 3.0).all())
+    ref = orc.paged_attention_prefill(q.float().cpu().numpy(), lk, lv, table, kv_len, q_start,
+                                      True, S)
+    _close(out.float().cpu().numpy(), ref)
+    # an output view whose base and token stride are not 16-byte multiples goes through a
+    # temporary: same bits, and the columns around the view untouched
+    wide = torch.full((q_len, Hq * D + 3), 5.0, dtype=torch.bfloat16, device=DEV)
+    view = wide[:, 1:1 + Hq * D].view(q_len, Hq, D)
+    kernels.paged_prefill_attention(q, kp, vp, bt, kv_len, q_start, True, out=view, impl="tc")
+    torch.cuda.synchronize()
+    assert torch.equal(view, out)
+    assert bool((wide[:, 0] == 5.0).all()) and bool((wide[:, -2:] == 5.0).all())
+
+
 @pytest.mark.parametrize("impl", IMPLS)
 def test_prefill_matches_reference_algorithm_on_gpu(impl: str) -> None:
     # the reference's path (gather, repeat_interleave, SDPA with its offset mask) on the GPU

@@ -30,7 +30,7 @@ V_SLOTS = 2
 SLACK = 768
 O_COL = 128
 TMEM_COLS = 256
-BAR_BYTES = 128
+BAR_BYTES = 144
 SM_SMEM = 228 * 1024
 TMEM_PER_SM = 512
 
@@ -79,13 +79,26 @@ def test_shared_memory_and_tmem_bounds(D: int, S: int) -> None:
     v0 = k0 + K_SLOTS * c["kv"]
     p0 = v0 + V_SLOTS * c["kv"]
     bars0 = p0 + c["p"]
-    assert bars0 + 8 * 8 + 4 <= c["layout"]
+    assert bars0 + 16 * 8 + 4 <= c["layout"]  # 16 mbarriers + the TMEM address
     for off in (k0, v0, p0, c["kv"]):
         assert off % 1024 == 0
     # the layout fits after aligning any 256-byte aligned base up to 1024 bytes
     assert all((-base) % 1024 + c["layout"] <= c["smem"] for base in range(0, 4096, 256))
-    # Q writes: rows < 128, 16-byte chunks < D / 8
+    # Q by TMA: box b (64 columns x 128 rows of 128 B) at b * 16 KB, 1024-byte aligned, and
+    # the expect-tx count (the whole tile) equals what the boxes deliver
+    for b in range(c["boxes"]):
+        assert (b * c["q_box"]) % 1024 == 0 and b * c["q_box"] + KM * 128 <= c["q"]
+    assert c["boxes"] * 64 * KM * 2 == c["q"]
+    # the epilogue's O writes into the Q tile's space: rows < 128, 16-byte chunks < D / 8,
+    # and each warp's TMA store source (32 rows of box b) stays inside the tile
     assert max(sw128_off(r, ch) for r in range(KM) for ch in range(D // 8)) + 16 <= c["q"]
+    for w in range(4):
+        for b in range(c["boxes"]):
+            src = b * c["q_box"] + w * 32 * 128
+            assert src % 1024 == 0 and src + 32 * 128 <= c["q"]
+            # the rows a warp's threads write are exactly its store box's rows
+            rows = {(sw128_off(r, 8 * b) - b * c["q_box"]) // 128 for r in range(32 * w, 32 * w + 32)}
+            assert rows == set(range(32 * w, 32 * w + 32))
     # P writes: 64 keys = 8 chunks per row, one box
     assert max(sw128_off(r, ch) for r in range(KM) for ch in range(KN // 8)) + 16 <= c["p"]
     # TMA box destinations of one K or V tile: box b, page pp
@@ -147,6 +160,14 @@ def test_page_reads_tiles_and_expect_tx(D: int, S: int, G: int) -> None:
                     b, rem = divmod(cc, per_box)
                     off = b * c["kv_box"] + (valid + rem // 8) * 128 + (rem & 7) * 16
                     assert off + 16 <= c["kv"]
+            # Q box (64 x G x T) starts inside the tensor; each warp's output box
+            # (64 x G x 32 / G) holds rows r = 32 w .. 32 w + 31, i.e. tokens
+            # t0 + 32 w / G ...; a box that starts at or past q_len is not issued
+            assert t0 < q_len
+            for w in range(4):
+                w_tok = t0 + w * (32 // G)
+                assert [t0 + r // G for r in range(32 * w, 32 * w + 32)] == [
+                    w_tok + i // G for i in range(32)]
             # a row's visible keys never exceed what the CTA loaded
             for r in range(KM):
                 tok = t0 + r // G
@@ -182,14 +203,16 @@ def _simulate(n_tiles: int, seed: int) -> None:
     rnd = random.Random(seed)
     B = {name: _Barrier(4 if name.startswith(("SEmpty", "PFull")) else 1) for name in
          ["KFull0", "KFull1", "KEmpty0", "KEmpty1", "VFull0", "VFull1", "VEmpty0", "VEmpty1",
-          "SFull0", "SFull1", "SEmpty0", "SEmpty1", "PFull", "OFree", "Drain"]}
-    done = {"K": set(), "V": set(), "S": set(), "PV": set()}
+          "SFull0", "SFull1", "SEmpty0", "SEmpty1", "PFull", "OFree", "Drain", "QFull"]}
+    done = {"K": set(), "V": set(), "S": set(), "PV": set(), "Q": set()}
     s_reads = [0] * max(n_tiles, 1)   # softmax warps that have read S(t)
     p_writes = [0] * max(n_tiles, 1)  # softmax warps that have written their rows of P(t)
     pending = []          # async completions: (kind, tile, barriers to arrive on)
     issued_mma = []       # MMAs in issue order (they complete in order)
 
     def load_warp():
+        if n_tiles > 0:
+            pending.append(("Q", 0, ["QFull"]))
         for t in range(n_tiles):
             sl = t % 2
             for kind in ("K", "V"):
@@ -208,6 +231,10 @@ def _simulate(n_tiles: int, seed: int) -> None:
             assert p_writes[u] == 4 and u in done["V"]
             issued_mma.append(("PV", u, ["OFree", "VEmpty" + str(u % 2)]))
 
+        if n_tiles > 0:
+            while not B["QFull"].passed(0):
+                yield
+            assert 0 in done["Q"]
         for t in range(n_tiles):
             sl = t % 2
             while not (B["KFull" + str(sl)].passed((t // 2) & 1) and
@@ -245,6 +272,9 @@ def _simulate(n_tiles: int, seed: int) -> None:
             while not B["Drain"].passed(0):
                 yield
             assert (n_tiles - 1) in done["PV"]
+            # the epilogue writes O into the Q tile's space: Q has landed and no S = Q K^T
+            # is still reading it
+            assert 0 in done["Q"] and done["S"] == set(range(n_tiles))
 
     roles = [load_warp(), mma_thread()] + [softmax_warp(w) for w in range(4)]
     alive = list(roles)
