@@ -249,10 +249,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int G = p.group;
-  const int h = blockIdx.y;
-  // causal: the latest (heaviest) query blocks first
-  const int qblk = p.causal ? static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x)
-                            : static_cast<int>(blockIdx.x);
+  // One CTA per (query block, KV head), KV head fastest. CTAs start in index order, so with
+  // causal masking the latest (heaviest) query blocks of every head go first and the light
+  // ones fill the last wave.
+  const int h = static_cast<int>(blockIdx.x) % p.hkv;
+  const int n_qblocks = static_cast<int>(gridDim.x) / p.hkv;
+  const int qi = static_cast<int>(blockIdx.x) / p.hkv;
+  const int qblk = p.causal ? n_qblocks - 1 - qi : qi;
   const int t0 = qblk * p.tokens_per_cta;
   const int t_end = min(p.q_len, t0 + p.tokens_per_cta);
   // keys any row of this CTA may see
@@ -646,8 +649,8 @@ int launch(const Params& p, int n_qblocks, const CUtensorMap& tk, const CUtensor
     configured[dev][slot] = true;
   }
   const cudaError_t e =
-      launch_kernel(kern, dim3(n_qblocks, p.hkv), dim3(kThreads), C::kLaunchSmem, stream, tk, tv, tq,
-                    to, p);
+      launch_kernel(kern, dim3(n_qblocks * p.hkv), dim3(kThreads), C::kLaunchSmem, stream, tk, tv,
+                    tq, to, p);
   return e == cudaSuccess ? PI_OK : PI_ERR_CUDA;
 }
 

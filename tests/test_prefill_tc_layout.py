@@ -136,9 +136,13 @@ def test_page_reads_tiles_and_expect_tx(D: int, S: int, G: int) -> None:
     ]:
         table_len = -(-kv_len // S)
         n_qblocks = -(-q_len // T)
-        for bx in range(n_qblocks):
-            qb = n_qblocks - 1 - bx if causal else bx   # heaviest block first when causal
-            assert 0 <= qb < n_qblocks
+        hkv = 3
+        seen = set()
+        for lin in range(n_qblocks * hkv):            # 1-D grid, KV head fastest
+            h, qi = lin % hkv, lin // hkv
+            qb = n_qblocks - 1 - qi if causal else qi  # heaviest blocks first when causal
+            assert 0 <= qb < n_qblocks and (qb, h) not in seen
+            seen.add((qb, h))
             t0 = qb * T
             t_end = min(q_len, t0 + T)
             kv_hi = min(kv_len, q_start + t_end) if causal else kv_len
