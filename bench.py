@@ -16,8 +16,8 @@ and MLP are outside the path and not run.
              the attention outputs are inside the timed region
   roofline   the attention kernel: algorithmic bytes (context K/V + q + out + block
              table) / its CUDA-event time, against the measured HBM copy bandwidth
-  c4         the C4 (Qwen3-30B-A3B shape) KV path on the same ranks: tok/s and its
-             attention roofline
+  c4         the C4 (Qwen3-30B-A3B shape) KV path on the same ranks: tok/s, its
+             attention roofline and (N = 1) layer 0 of its timed step against the oracle
   c5         the C5 long-context decode through the KV store API on the same ranks (KV
              heads sharded, each rank streaming its own host chunks): tok/s and the
              host-link roofline; so every N of a scaling run records C3, C4 and C5
@@ -1280,12 +1280,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         barrier(world)
     if parity is not None and parity["status"] != "ok":
         raise SystemExit("parity check of the timed step failed: " + json.dumps(parity))
+    if c4 is not None and c4.get("parity", {}).get("status", "ok") != "ok":
+        raise SystemExit("parity check of the C4 step failed: " + json.dumps(c4["parity"]))
 
 
 def measure_c4(args, rank: int, world: int, dev: torch.device, peaks: dict) -> dict:
     """The C4 (Qwen3-30B-A3B shape) KV path on the same ranks as the C3 line: the same
     sharding (a KV head per rank is replicated when there are fewer KV heads than ranks),
-    gather and graph capture; device time is the max over ranks."""
+    gather and graph capture; device time is the max over ranks. At N = 1 (unless
+    --skip-cpu) layer 0 of the timed step is checked against the oracle, like the C3 line."""
     from plastic_infer_b200 import kernels
 
     cfg = dict(C4)
@@ -1327,6 +1330,10 @@ def measure_c4(args, rank: int, world: int, dev: torch.device, peaks: dict) -> d
                              algorithmic_bytes_per_launch=int(wl.attn_bytes()),
                              achieved=round(achieved, 1), peak=peaks["hbm_gbs"], unit="GB/s",
                              frac=round(achieved / peaks["hbm_gbs"], 4)))
+    if world == 1 and not args.skip_cpu:
+        sample = CpuSample(cfg, LayerSnapshot(wl))
+        res["parity"] = sample.check(sample.layer())
+        del sample
     step_fn = attn_fn = None
     del g_step, g_attn
     torch.cuda.synchronize()
