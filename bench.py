@@ -19,8 +19,10 @@ and MLP are outside the path and not run.
   c4         the C4 (Qwen3-30B-A3B shape) KV path on the same ranks: tok/s, its
              attention roofline and (N = 1) layer 0 of its timed step against the oracle
   c5         the C5 long-context decode through the KV store API on the same ranks (KV
-             heads sharded, each rank streaming its own host chunks): tok/s and the
-             host-link roofline; so every N of a scaling run records C3, C4 and C5
+             heads sharded, each rank streaming its own host chunks): tok/s, the
+             host-link roofline and (rank 0) two (request, layer) outputs of the last step
+             against the oracle over histories rebuilt from the host chunks and device
+             pages; so every N of a scaling run records C3, C4 and C5
   index_copy C2 microbench (65536-page pool): GB/s at B = 1, 64, 512, a whole 36-layer
              step in one launch (2304) and a large-B sweep; graphs of back-to-back launches
              with L2 flushed before every timed replay
@@ -982,6 +984,50 @@ def host_link_gbs(dev: torch.device) -> float:
     return (1 << 30) / (ms * 1e-3) / 1e9
 
 
+def c5_parity(store, caches, q: torch.Tensor, out: torch.Tensor, checks) -> dict:
+    """Outputs of the last C5 step against the oracle, for (request, layer) pairs `checks`:
+    each request's whole K/V history of that layer is rebuilt independently of the decode
+    path, from its evicted chunks in the host store and its device pages, and the oracle
+    attends this rank's query heads over it."""
+    from oracle import paged_kv_oracle as orc
+
+    cfg = store.config
+    S, ppc, tpc = cfg.page_size, cfg.pages_per_chunk, cfg.tokens_per_chunk
+    worst, bad, tokens = 0.0, 0, 0
+    for b, layer in checks:
+        c = caches[b]
+        T = c.length
+        ks, vs = [], []
+        for ci in range(c.evicted_chunks):  # host chunks: logical [L, H, D, tpc]
+            hk, hv = store._host_cache[c.chunk_keys[ci].full_key]
+            ks.append(hk[layer].float().permute(2, 0, 1))
+            vs.append(hv[layer].float().permute(2, 0, 1))
+        pages = c.block_table.pages[layer][c.evicted_chunks * ppc:-(-T // S)]
+        idx = torch.tensor(pages, dtype=torch.int64, device=store.gpu.k_phys.device)
+        for pool, dst in ((store.gpu.k_phys, ks), (store.gpu.v_phys, vs)):  # [P, H, S, D]
+            rows = pool.index_select(0, idx).permute(0, 2, 1, 3).reshape(-1, pool.shape[1], pool.shape[3])
+            dst.append(rows[:T - c.evicted_chunks * tpc].float().cpu())
+        k = torch.cat(ks).numpy()
+        v = torch.cat(vs).numpy()
+        npg = -(-T // S)
+        pad = np.zeros((npg * S - T,) + k.shape[1:], np.float32)
+        kp = np.concatenate([k, pad]).reshape(npg, S, k.shape[1], k.shape[2]).transpose(0, 2, 3, 1)
+        vp = np.concatenate([v, pad]).reshape(npg, S, v.shape[1], v.shape[2]).transpose(0, 2, 3, 1)
+        ref = orc.paged_attention_decode(q[layer, b].float().cpu().numpy()[None], kp, vp,
+                                         [list(range(npg))], [T], S)[0]
+        got = out[layer, b].float().cpu().numpy()
+        err = np.abs(got - ref)
+        worst = max(worst, float(err.max()))
+        bad += int((err > 2e-2 + 1e-2 * np.abs(ref)).sum()) + int((~np.isfinite(got)).sum())
+        tokens += T
+    return dict(status="ok" if bad == 0 else "FAIL",
+                checked=f"last timed step, (request, layer) {list(checks)}: each history "
+                        f"({tokens} tokens in all) rebuilt from the host chunks and device pages, "
+                        "this rank's query heads vs the numpy oracle",
+                tolerance="|out - ref| <= 2e-2 + 1e-2 |ref| (fp32 oracle on the same bf16 inputs)",
+                max_abs_err=worst, violations=bad)
+
+
 def measure_c5(args, rank: int, world: int, dev: torch.device, steps: int, warmup: int) -> dict:
     """C5 long-context decode through the KV store API on every rank of the job.
 
@@ -1083,6 +1129,8 @@ def measure_c5(args, rank: int, world: int, dev: torch.device, steps: int, warmu
                       peak_source="sum over the ranks of a pinned 1 GiB host->device copy, all "
                                   "ranks copying at once, measured in this run"),
         host_bytes_read_per_step=int(hb), clocks=clk.summary())
+    if rank == 0 and not args.skip_cpu:
+        res["parity"] = c5_parity(store, caches, q, out, [(0, 0), (B - 1, L - 1)])
     del store, caches, dec, q, kn, vn, out, gathered
     torch.cuda.empty_cache()
     return res
@@ -1097,6 +1145,8 @@ def run_c5(args, rank: int, world: int, dev: torch.device) -> None:
         line.update(scaling="strong", higher_is_better=True, vs_baseline=None, dtype="bf16",
                     data="synthetic", config=dict(workload=workload))
         print(json.dumps(line), flush=True)
+        if res.get("parity", {}).get("status", "ok") != "ok":
+            raise SystemExit("parity check of the C5 step failed: " + json.dumps(res["parity"]))
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
@@ -1280,8 +1330,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         barrier(world)
     if parity is not None and parity["status"] != "ok":
         raise SystemExit("parity check of the timed step failed: " + json.dumps(parity))
-    if c4 is not None and c4.get("parity", {}).get("status", "ok") != "ok":
-        raise SystemExit("parity check of the C4 step failed: " + json.dumps(c4["parity"]))
+    for name, leg in (("C4", c4), ("C5", c5)):
+        if leg is not None and leg.get("parity", {}).get("status", "ok") != "ok":
+            raise SystemExit(f"parity check of the {name} step failed: " + json.dumps(leg["parity"]))
 
 
 def measure_c4(args, rank: int, world: int, dev: torch.device, peaks: dict) -> dict:
