@@ -13,6 +13,7 @@ batch: `decode_prologue` (QK-norm, RoPE, and the write of the new K/V rows) and
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 
@@ -124,8 +125,10 @@ class HostStoreDecoder:
     attend       per layer: the new K/V rows are written (one index-copy launch), the
                  requests that still hold all their chunks on the device are attended in
                  one paged_decode_attention launch, and every request with evicted chunks
-                 through host_stream_attention_v1 over its host chunks (pinned, read in
-                 place) and its device tail (KVStore.host_stream_chunks).
+                 by host-stream attention (host_stream_attention_v1's kernel) over its host
+                 chunks (pinned, read in place) and its device tail. A host chunk's span
+                 rows are built once, when it is first streamed, and a layer offsets them:
+                 per call the host work is a few array operations, not per-chunk checks.
     end_step     completed chunks are sunk to the host store on the store's side stream
                  without waiting (KVStore.sink_completed_chunks_async), so the copies run
                  under the next step's attention, and chunks are evicted until the pool
@@ -151,6 +154,12 @@ class HostStoreDecoder:
         self.ctx_resident: torch.Tensor | None = None
         self.streamed: list[int] = []
         self.evictions = 0
+        # per request: span-table rows (K address, V address, length, strides) of its
+        # evicted host chunks at layer 0, oldest first; a layer adds layer * _layer_bytes
+        # to both addresses (the chunk buffers are [L, H_kv, T, D])
+        self._host_rows = [np.empty((0, 6), dtype=np.uint64) for _ in caches]
+        elem = torch.tensor([], dtype=cfg.dtype).element_size()
+        self._layer_bytes = cfg.n_kv_heads * cfg.tokens_per_chunk * cfg.head_dim * elem
 
     # -- pool budget -------------------------------------------------------------
 
@@ -200,25 +209,68 @@ class HostStoreDecoder:
         self.slots = torch.tensor([[c.block_table.slot(l, p) for c, p in zip(self.caches, self.positions)]
                                    for l in range(L)], dtype=torch.int64, device=self.device)
         self.streamed = [b for b, c in enumerate(self.caches) if c.evicted_chunks > 0]
+        for b in self.streamed:
+            self._extend_host_rows(b)
         ctx = [0 if b in self.streamed else p + 1 for b, p in enumerate(self.positions)]
         self.ctx_resident = torch.tensor(ctx, dtype=torch.int32, device=self.device)
 
+    def _extend_host_rows(self, b: int) -> None:
+        """Add the span rows of request b's newly evicted chunks (checked once here: page-
+        locked, [L, H_kv, T, D] buffers), after making the current stream wait for their
+        sinks' copies."""
+        cache = self.caches[b]
+        rows = self._host_rows[b]
+        n = cache.evicted_chunks
+        if rows.shape[0] > n:  # evictions are only ever appended; rebuild if that changed
+            rows = np.empty((0, 6), dtype=np.uint64)
+        if rows.shape[0] == n:
+            self._host_rows[b] = rows
+            return
+        cfg = self.store.config
+        T, D, H = cfg.tokens_per_chunk, cfg.head_dim, cfg.n_kv_heads
+        stream = torch.cuda.current_stream(self.device)
+        new = []
+        for ci in range(rows.shape[0], n):
+            k, v, ready = self.store.host_chunk(cache.chunk_keys[ci].full_key)
+            if not (k.is_pinned() and v.is_pinned()):
+                raise RuntimeError("host chunks must be page-locked to be read in place")
+            want = (H * T * D, T * D, 1, D)  # logical [L, H, D, T] over physical [L, H, T, D]
+            if k.stride() != want or v.stride() != want:
+                raise RuntimeError(f"unexpected host chunk layout {tuple(k.stride())}")
+            if ready is not None:
+                stream.wait_event(ready)  # the kernel reads the buffer after its sink's copy
+            new.append((k.data_ptr(), v.data_ptr(), T, T * D, D, 1))
+        self._host_rows[b] = np.concatenate([rows, np.array(new, dtype=np.uint64)])
+
     def attend(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                out: torch.Tensor | None = None) -> torch.Tensor:
-        from .exec.attention import host_stream_attention_v1
-
         gpu = self.store.gpu
+        cfg = self.store.config
         kernels.kv_index_copy(gpu.k_phys, gpu.v_phys, k_new, v_new, self.slots[layer])
         # streamed requests get ctx 0 here (zeros), then their host-stream result
         out = kernels.paged_decode_attention(q, gpu.k_phys, gpu.v_phys, self.tables.tables[layer],
                                              self.ctx_resident, out=out, workspace=self.workspace)
         B, Hq, D = q.shape
+        offset = np.uint64(layer * self._layer_bytes)
         for b in self.streamed:
-            chunks, rk, rv = self.store.host_stream_chunks(self.caches[b], layer,
-                                                           self.tables.tables[layer, b])
-            o = host_stream_attention_v1(q[b].view(1, 1, Hq, D), chunks, rk, rv,
-                                         q_start_pos=self.positions[b], causal=True)
-            out[b].copy_(o.view(Hq, D))
+            cache = self.caches[b]
+            rows = self._host_rows[b]
+            n = rows.shape[0]
+            # the device tail: tokens after the evicted chunks, gathered from the pool
+            start = cache.evicted_chunks * cfg.pages_per_chunk
+            n_tail = cache.length - cache.evicted_chunks * cfg.tokens_per_chunk
+            table = np.empty((n + (1 if n_tail > 0 else 0), 6), dtype=np.uint64)
+            table[:n] = rows
+            table[:n, :2] += offset
+            if n_tail > 0:
+                bt = self.tables.tables[layer, b, start:]
+                rk = kernels.paged_kv_gather(gpu.k_phys, bt, n_tail)  # [R, H_kv, D]
+                rv = kernels.paged_kv_gather(gpu.v_phys, bt, n_tail)
+                table[n] = (rk.data_ptr(), rv.data_ptr(), n_tail, rk.stride(1), rk.stride(0),
+                            rk.stride(2))
+            kernels.host_stream_attention_table(q[b].view(1, Hq, D), out[b].view(1, Hq, D), table,
+                                                cfg.n_kv_heads, q_start=self.positions[b],
+                                                causal=True)
         return out
 
     def end_step(self) -> None:

@@ -698,6 +698,20 @@ def host_stream_attention(
         if out3.shape != (q_len, Hq, D) or out3.dtype != q3.dtype or out3.stride(2) != 1 \
                 or out3.stride(1) != D:
             raise ValueError("out must be [q_len, Hq, D] in q's dtype with contiguous heads")
+    # pi_kv_span_t[]: six 64-bit fields per span (two addresses, length, three strides)
+    table = np.array(rows if rows else [(0, 0, 0, 0, 0, 1)], dtype=np.uint64)
+    _host_stream_launch(q3, out3, table, len(kv_spans), hkv, kv_len, q_start, causal, scale,
+                        workspace, err)
+    _keep_until_done(host)
+    if out is not None:
+        return out
+    return out3.unsqueeze(0) if batched else out3
+
+
+def _host_stream_launch(q3: torch.Tensor, out3: torch.Tensor, table: np.ndarray, n_spans: int,
+                        hkv: int, kv_len: int, q_start: int, causal: bool, scale: float | None,
+                        workspace: Workspace | None, err: torch.Tensor | None) -> None:
+    q_len, Hq, D = q3.shape
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     nbytes = int(_capi.load().pi_host_stream_attn_workspace_size(q_len, Hq, hkv, D, kv_len))
@@ -710,18 +724,48 @@ def host_stream_attention(
                 if workspace is None:
                     workspace = _hs_ws[idx] = Workspace(q3.device)
         ws_ptr = workspace.get(nbytes).data_ptr()
-    # pi_kv_span_t[]: six 64-bit fields per span (two addresses, length, three strides)
-    table = np.array(rows if rows else [(0, 0, 0, 0, 0, 1)], dtype=np.uint64)
     _capi.call(
         "pi_host_stream_attn",
         out3.data_ptr(), q3.data_ptr(), q3.stride(0), out3.stride(0), table.ctypes.data,
-        len(kv_spans), q_len, int(q_start), 1 if causal else 0, Hq, hkv, D, float(scale), code,
-        ws_ptr, nbytes, _capi.HS_SPANS_CHECKED, _err_ptr(err), _stream(),
+        n_spans, q_len, int(q_start), 1 if causal else 0, Hq, hkv, D, float(scale),
+        dtype_code(q3.dtype), ws_ptr, nbytes, _capi.HS_SPANS_CHECKED, _err_ptr(err), _stream(),
     )
-    _keep_until_done(host)
-    if out is not None:
-        return out
-    return out3.unsqueeze(0) if batched else out3
+
+
+def host_stream_attention_table(q: torch.Tensor, out: torch.Tensor, table: np.ndarray,
+                                num_kv_heads: int, q_start: int = 0, causal: bool = True,
+                                scale: float | None = None, workspace: Workspace | None = None,
+                                err: torch.Tensor | None = None) -> torch.Tensor:
+    """host_stream_attention over a span table the caller has already built and checked.
+
+    `table` is a uint64 [n, 6] array, one row per span in sequence order: K address, V
+    address, length T, then the element strides of the [H_kv, T, D] views (head, token,
+    dim). Every span must be device memory on q's GPU or page-locked host memory, in q's
+    dtype with `num_kv_heads` heads and q's head_dim, and stay allocated until the launch
+    has run; nothing here re-checks them. This is the per-step path of a decode loop that
+    keeps its host chunks' rows across steps (decode.HostStoreDecoder): building the table
+    is a few array operations instead of per-span tensor checks. q and out are
+    [q_len, Hq, D] on the GPU with contiguous heads.
+    """
+    if q.dim() != 3 or out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("q and out must both be [q_len, Hq, D] in one dtype")
+    if q.stride(2) != 1 or q.stride(1) != q.shape[2] or out.stride(2) != 1 \
+            or out.stride(1) != q.shape[2]:
+        raise ValueError("q and out need contiguous heads")
+    _require_cuda(q, out)
+    if table.dtype != np.uint64 or table.ndim != 2 or table.shape[1] != 6 or not table.flags.c_contiguous:
+        raise ValueError("table must be a C-contiguous uint64 [n, 6] array")
+    n = table.shape[0]
+    if n > _capi.HS_MAX_SPANS:
+        raise ValueError(f"at most {_capi.HS_MAX_SPANS} spans per call")
+    if q.shape[1] % num_kv_heads:
+        raise ValueError(f"Hq={q.shape[1]} is not a multiple of H_kv={num_kv_heads}")
+    kv_len = int(table[:, 2].sum()) if n else 0
+    if n == 0:
+        table = np.array([(0, 0, 0, 0, 0, 1)], dtype=np.uint64)
+    _host_stream_launch(q, out, table, n, num_kv_heads, kv_len, q_start, causal, scale,
+                        workspace, err)
+    return out
 
 
 # ---------------------------------------------------------------------------

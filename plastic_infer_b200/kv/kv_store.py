@@ -538,6 +538,15 @@ class KVStore:
         """Whether the host store holds (or is being sent) the chunk with this key."""
         return full_key in self._host_cache
 
+    def host_chunk(self, full_key: bytes
+                   ) -> tuple[torch.Tensor, torch.Tensor, Optional[torch.cuda.Event]]:
+        """The host copy of a chunk: (k, v) logical [L, H_kv, D, T] views of its pinned
+        buffers and the event after which they hold the data (None once known complete)."""
+        kv = self._host_cache.get(full_key)
+        if kv is None or kv[0] is None:
+            raise KeyError("no host copy of this chunk")
+        return kv[0], kv[1], self._host_ready.get(full_key)
+
     @property
     def host_cache_size(self) -> int:
         return len(self._host_cache)
