@@ -111,6 +111,18 @@ def decode_step_paged_batched(weights: DenseWeights, config: ModelConfig, store:
     return linear(x[:, -1, :], weights["lm_head.weight"])
 
 
+def host_chunk_span_row(k: torch.Tensor, v: torch.Tensor) -> tuple[int, int, int, int, int, int]:
+    """Span-table row of a host chunk at layer 0, from its K/V logical [L, H_kv, D, T] views
+    over physical [L, H_kv, T, D] buffers: (K address, V address, T, and the element strides
+    of the [H_kv, T, D] span: head, token, dim). Layer l's row adds l * H_kv * T * D *
+    element size to both addresses."""
+    L, H, D, T = k.shape
+    want = (H * T * D, T * D, 1, D)
+    if tuple(k.stride()) != want or tuple(v.stride()) != want or v.shape != k.shape:
+        raise RuntimeError(f"unexpected host chunk layout {tuple(k.stride())}")
+    return (k.data_ptr(), v.data_ptr(), T, T * D, D, 1)
+
+
 class HostStoreDecoder:
     """Decode steps for requests whose KV outgrows the device pool (the host KV store
     wired into the decode loop).
@@ -226,20 +238,15 @@ class HostStoreDecoder:
         if rows.shape[0] == n:
             self._host_rows[b] = rows
             return
-        cfg = self.store.config
-        T, D, H = cfg.tokens_per_chunk, cfg.head_dim, cfg.n_kv_heads
         stream = torch.cuda.current_stream(self.device)
         new = []
         for ci in range(rows.shape[0], n):
             k, v, ready = self.store.host_chunk(cache.chunk_keys[ci].full_key)
             if not (k.is_pinned() and v.is_pinned()):
                 raise RuntimeError("host chunks must be page-locked to be read in place")
-            want = (H * T * D, T * D, 1, D)  # logical [L, H, D, T] over physical [L, H, T, D]
-            if k.stride() != want or v.stride() != want:
-                raise RuntimeError(f"unexpected host chunk layout {tuple(k.stride())}")
             if ready is not None:
                 stream.wait_event(ready)  # the kernel reads the buffer after its sink's copy
-            new.append((k.data_ptr(), v.data_ptr(), T, T * D, D, 1))
+            new.append(host_chunk_span_row(k, v))
         self._host_rows[b] = np.concatenate([rows, np.array(new, dtype=np.uint64)])
 
     def attend(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,

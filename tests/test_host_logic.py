@@ -223,3 +223,30 @@ def test_extend_token_ids_gives_the_keys_of_set_token_ids() -> None:
     assert added == len(whole.chunk_keys) == 7
     assert step.chunk_keys == whole.chunk_keys
     assert step._final_hash == whole._final_hash
+
+
+def test_host_chunk_span_rows_match_the_generic_span_path() -> None:
+    # HostStoreDecoder keeps one row per host chunk (layer 0) and offsets it by the layer;
+    # that must equal the row host_stream_attention builds from the chunk's layer view
+    # (kv[layer] of the logical [L, H, D, T] view, permuted to [H, T, D]).
+    import numpy as np
+
+    from plastic_infer_b200.decode import host_chunk_span_row
+
+    L, H, T, D = 5, 3, 32, 16
+    for dtype in (torch.bfloat16, torch.float32):
+        kp = torch.zeros((L, H, T, D), dtype=dtype)
+        vp = torch.zeros_like(kp)
+        k, v = kp.permute(0, 1, 3, 2), vp.permute(0, 1, 3, 2)   # the store's logical views
+        row = np.array(host_chunk_span_row(k, v), dtype=np.uint64)
+        layer_bytes = H * T * D * kp.element_size()
+        for layer in range(L):
+            ks, vs = k[layer].permute(0, 2, 1), v[layer].permute(0, 2, 1)
+            want = (ks.data_ptr(), vs.data_ptr(), ks.shape[1], ks.stride(0), ks.stride(1),
+                    ks.stride(2))
+            got = row.copy()
+            got[:2] += np.uint64(layer * layer_bytes)
+            assert tuple(int(x) for x in got) == want
+    with pytest.raises(RuntimeError):
+        bad = torch.zeros((L, H, D, T))  # contiguous logical layout: not the store's buffers
+        host_chunk_span_row(bad, bad)
