@@ -14,11 +14,14 @@
 //     MMA that read it has completed;
 //   - MMA warp (one thread): S(t) = Q K(t)^T into one of two TMEM buffers (columns [0, 64)
 //     and [64, 128)) as soon as K(t) has landed and the softmax has read that buffer's
-//     previous S, then O += P(t - 1) V(t - 1) (columns [128, 128 + D)); kind::f16, M = 128,
-//     K-major Q, K and P with the 128-byte swizzle, MN-major V;
+//     previous S, then O += P(t - 1) V(t - 1) (columns [128, 128 + D)) with P read from
+//     TMEM as the A operand; kind::f16, M = 128, K-major Q and K with the 128-byte swizzle,
+//     MN-major V;
 //   - 4 softmax warps (one thread per row): read S(t), release its buffer, run the online
-//     softmax in base 2, wait for the previous P V, store P (bf16/f16, swizzled K-major)
-//     and rescale O where needed, then signal P ready.
+//     softmax in base 2, write P (bf16/f16 pairs) over the first 32 columns of S(t)'s
+//     buffer, rescale O where needed (after the previous P V), then signal P ready.
+// P(t) overwrites S(t) in place: the MMA thread issues S(t + 2) into that buffer only after
+// P(t) V(t), and one thread's tcgen05.mma run in order.
 // So S(t + 1) computes while the softmax of tile t runs, and the softmax never waits on a
 // load. The running maximum of a row moves only when it grows by more than 2^8: P <= 256,
 // and O is rescaled on those rare tiles only (the stale maximum cancels in O / l). Tiles a
@@ -27,9 +30,10 @@
 // 0 * NaN is NaN). At the end each softmax warp writes its 32 rows of O / l into the Q
 // tile's space and stores them with one TMA store per 64 columns (rows of tokens past q_len
 // are dropped by the store). Warp-collective tcgen05 loads and stores run on a path every
-// thread of the warp takes. The CTA needs 113 KB of shared memory at head_dim 128, so two CTAs share
-// an SM. Every wait is bounded: a timeout sets PI_ERR_TIMEOUT, the roles leave their loops,
-// in-flight loads and MMAs complete, TMEM is freed.
+// thread of the warp takes. The CTA needs 97 KB of shared memory and 256 TMEM columns at
+// head_dim 128, so two CTAs share an SM. Every wait is bounded: a timeout sets
+// PI_ERR_TIMEOUT, the roles leave their loops, in-flight loads and MMAs complete, TMEM is
+// freed.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -68,10 +72,9 @@ struct Cfg {
   static constexpr int kKVBoxBytes = kN * 128;
   static constexpr int kQBytes = kBoxes * kQBoxBytes;     // Q tile [boxes][128 rows][128 B]
   static constexpr int kKVBytes = kBoxes * kKVBoxBytes;   // K or V tile [boxes][64 keys][128 B]
-  static constexpr int kPBytes = kM * 128;                // P [128 rows][64 keys] bf16: one box
   static constexpr int kPagesPerTile = kN / S;
-  static constexpr int kBarBytes = 144;  // 16 mbarriers + TMEM address
-  static constexpr int kLayoutBytes = kQBytes + (kKSlots + kVSlots) * kKVBytes + kPBytes + kBarBytes;
+  static constexpr int kBarBytes = 144;  // 17 mbarriers + TMEM address
+  static constexpr int kLayoutBytes = kQBytes + (kKSlots + kVSlots) * kKVBytes + kBarBytes;
   // Slack for aligning the tiles to 1024 bytes (the 128-byte swizzle's period). 768 bytes
   // covers any base aligned to 256 bytes and keeps two head_dim-128 CTAs on one SM (228 KB,
   // 1 KB reserved per CTA); the kernel checks the fit and reports PI_ERR_MISALIGNED if not.
@@ -137,6 +140,16 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16 with an f32 accumulator.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc)
+      : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -217,12 +230,15 @@ enum Bar : int {
   kVEmpty = 6,   // [2] P V(t) complete: V slot free
   kSFull = 8,    // [2] S(t) complete (MMA commit)
   kSEmpty = 10,  // [2] S(t) read by the 4 softmax warps
-  kPFull = 12,   // P(t) in shared memory and O rescaled (4 softmax warps)
-  kOFree = 13,   // P V(t) complete: P buffer and O free (MMA commit)
-  kDrain = 14,   // every MMA issued has completed (one phase, at the end)
-  kQFull = 15,   // the Q tile landed (TMA bytes, one phase)
-  kNumBars = 16,
+  kPFull = 12,   // [2] P(t) in TMEM and O rescaled (4 softmax warps), slot t % 2: a warp
+                 // may run a tile ahead of another (it waits for the previous P V only to
+                 // rescale), and tile t + 1's arrivals must not complete tile t's phase
+  kOFree = 14,   // P V(t) complete: O free (MMA commit)
+  kDrain = 15,   // every MMA issued has completed (one phase, at the end)
+  kQFull = 16,   // the Q tile landed (TMA bytes, one phase)
+  kNumBars = 17,
 };
+static_assert(kNumBars * 8 + 4 <= 144, "the mbarriers and the TMEM address fit kBarBytes");
 
 template <typename T, int D, int S>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -236,8 +252,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                                            ~static_cast<uintptr_t>(1023));
   uint8_t* ks = qs + C::kQBytes;                    // K slot s at s * kKVBytes
   uint8_t* vs = ks + kKSlots * C::kKVBytes;         // V slot s at s * kKVBytes
-  uint8_t* ps = vs + kVSlots * C::kKVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + C::kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kVSlots * C::kKVBytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   if ((qs - smem_raw) + C::kLayoutBytes > C::kSmem) {  // CTA-uniform: the base is too unaligned
     if (threadIdx.x == 0) record_error(p.err, PI_ERR_MISALIGNED);
@@ -268,7 +283,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (tid == 0) {
     for (int b = 0; b < kNumBars; ++b)
-      mbar_init(bar(b), (b == kSEmpty || b == kSEmpty + 1 || b == kPFull) ? kSoftmaxWarps : 1);
+      mbar_init(bar(b), (b == kSEmpty || b == kSEmpty + 1 || b == kPFull || b == kPFull + 1)
+                            ? kSoftmaxWarps : 1);
     fence_mbar_init();
   }
   if (warp == kLoadWarp && lane == 0) {
@@ -367,10 +383,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t id_s = umma::instr_desc_f16(kBf16, kM, kN, false, false);
       const uint32_t id_o = umma::instr_desc_f16(kBf16, kM, D, false, true);
       const uint32_t q_addr = smem_u32(qs);
-      const uint32_t p_addr = smem_u32(ps);
       auto pv = [&](int u) {  // O += P(u) V(u)
         const int sl = u % kVSlots;
-        if (!mbar_wait_bounded(bar(kPFull), static_cast<uint32_t>(u & 1)) ||
+        if (!mbar_wait_bounded(bar(kPFull + u % 2), static_cast<uint32_t>((u / 2) & 1)) ||
             !mbar_wait_bounded(bar(kVFull + sl), static_cast<uint32_t>((u / kVSlots) & 1))) {
           failed = true;
           return;
@@ -378,12 +393,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint64_t a = umma::smem_desc(p_addr + static_cast<uint32_t>(kk * 32), 16, 1024,
-                                             umma::kSwizzle128);
           const uint64_t b = umma::smem_desc(
               v_addr0 + static_cast<uint32_t>(sl * C::kKVBytes + kk * 16 * 128), C::kKVBoxBytes,
               1024, umma::kSwizzle128);
-          umma_f16(tmem + kOCol, a, b, id_o, (u > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + kOCol, tmem + static_cast<uint32_t>(kN * (u % 2) + 8 * kk), b, id_o,
+                      (u > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(bar(kOFree));
         umma_commit(bar(kVEmpty + sl));
@@ -502,22 +516,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float ls = ls_a + ls_b;
       l_run = l_run * alpha + ls;
       m_run = m_new;
-      // P V(j - 1) complete: the P buffer and O are free
-      if (j > 0) {
-        if (!mbar_wait_bounded(bar(kOFree), static_cast<uint32_t>((j - 1) & 1))) failed = true;
-        if (__any_sync(0xffffffffu, failed)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-      }
+      {
+        // P(t) as bf16/f16 pairs over the first 32 columns of S(t)'s buffer (read above),
+        // the layout the P V MMA takes its A operand in
+        float pf[kN / 2];
 #pragma unroll
-      for (int ch = 0; ch < kN / 8; ++ch)
-        *reinterpret_cast<uint4*>(ps + sw128_off(r, ch)) =
-            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-      // O of earlier tiles, rescaled where a row's maximum moved. The TMEM loads are
-      // warp-collective: the whole warp takes the branch.
+        for (int c = 0; c < kN / 2; ++c) pf[c] = __uint_as_float(pk[c]);
+        tmem_st32(t_row + static_cast<uint32_t>(kN * sb), pf);
+        tmem_wait_st();
+      }
+      // O of earlier tiles, rescaled where a row's maximum moved, once P V(j - 1) is done.
+      // The TMEM loads are warp-collective: the whole warp takes the branch.
       if (__any_sync(0xffffffffu, rescale)) {
+        if (j > 0) {
+          if (!mbar_wait_bounded(bar(kOFree), static_cast<uint32_t>((j - 1) & 1))) failed = true;
+          if (__any_sync(0xffffffffu, failed)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+        }
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           float ov[32];
@@ -549,10 +567,10 @@ __global__ void __launch_bounds__(kThreads, 2)
                                     (rem & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
       }
-      fence_proxy_async_smem();  // P and the zeroed V rows are read by the MMA
+      fence_proxy_async_smem();  // the zeroed V rows are read by the MMA
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kPFull));
+      if (lane == 0) mbar_arrive(bar(kPFull + sb));
     }
     // The last P V, and with it every MMA, completes on the drain barrier.
     if (!failed && n_tiles > 0 && !mbar_wait_bounded(bar(kDrain), 0)) failed = true;

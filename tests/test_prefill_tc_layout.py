@@ -2,14 +2,17 @@
 
 This restates the kernel's layout constants and index arithmetic and checks, for every
 instantiated shape (head_dim 64/128, pages of 16/32) and a sweep of launch shapes, that:
-- every shared-memory offset it forms (Q, the K and V rings, TMA box
-  destinations, P, the V zeroing of the last tile, the MMA descriptor start addresses)
+- every shared-memory offset it forms (Q, the K and V rings, TMA box destinations, the V
+  zeroing of the last tile, the MMA descriptor start addresses, the output staging)
   stays inside its region, the regions fit the dynamic allocation it requests, and two
   CTAs of head_dim 128 fit on one SM (228 KB of shared memory, 1 KB reserved per CTA)
   while their TMEM columns fit the SM's 512;
 - each load's expect-tx byte count equals the bytes its TMA boxes deliver;
 - every page id it reads lies inside block_table[0, ceil(kv_len / S));
-- the TMEM columns it uses fit the ones it allocates.
+- the TMEM columns it uses fit the ones it allocates, P(t) lies inside S(t)'s buffer, and
+  the P V MMA's A-operand columns stay inside P;
+- the warp-specialized protocol (load warp, MMA thread, 4 softmax warps over mbarriers)
+  cannot deadlock and never reuses a buffer early, under random completion orders.
 The constants are restated here on purpose: a change on one side fails the check.
 """
 
@@ -41,11 +44,10 @@ def cfg(D: int, S: int) -> dict:
     kv_box = KN * 128
     q_bytes = boxes * q_box
     kv_bytes = boxes * kv_box
-    p_bytes = KM * 128
-    layout = q_bytes + (K_SLOTS + V_SLOTS) * kv_bytes + p_bytes + BAR_BYTES
+    layout = q_bytes + (K_SLOTS + V_SLOTS) * kv_bytes + BAR_BYTES
     smem = SLACK + layout
     launch = max(smem, 80 * 1024)
-    return dict(boxes=boxes, q_box=q_box, kv_box=kv_box, q=q_bytes, kv=kv_bytes, p=p_bytes,
+    return dict(boxes=boxes, q_box=q_box, kv_box=kv_box, q=q_bytes, kv=kv_bytes,
                 pages_per_tile=KN // S, smem=smem, launch=launch, layout=layout)
 
 
@@ -62,7 +64,15 @@ def test_constants_match_the_kernel_source() -> None:
     assert re.search(rf"static constexpr int kSlack = {SLACK};", src)
     assert re.search(rf"static constexpr int kBarBytes = {BAR_BYTES};", src)
     assert "kSmem > 80 * 1024 ? kSmem : 80 * 1024" in src
-    assert "(kKSlots + kVSlots) * kKVBytes + kPBytes + kBarBytes" in src
+    assert "(kKSlots + kVSlots) * kKVBytes + kBarBytes" in src
+    # P V reads P from TMEM: tile t's P over the first 32 columns of S(t)'s buffer, K step kk
+    # at 8 columns (16 bf16/f16 values) per MMA
+    assert "umma_f16_ts(tmem + kOCol, tmem + static_cast<uint32_t>(kN * (u % 2) + 8 * kk)" in src
+    assert "tmem_st32(t_row + static_cast<uint32_t>(kN * sb), pf);" in src
+    # P ready is two barriers by tile parity (the simulation below needs them)
+    assert "mbar_arrive(bar(kPFull + sb));" in src
+    assert "mbar_wait_bounded(bar(kPFull + u % 2), static_cast<uint32_t>((u / 2) & 1))" in src
+    assert "kNumBars = 17," in src
 
 
 @pytest.mark.parametrize("D,S", list(itertools.product((64, 128), (16, 32))))
@@ -77,10 +87,9 @@ def test_shared_memory_and_tmem_bounds(D: int, S: int) -> None:
     q0 = 0
     k0 = q0 + c["q"]
     v0 = k0 + K_SLOTS * c["kv"]
-    p0 = v0 + V_SLOTS * c["kv"]
-    bars0 = p0 + c["p"]
-    assert bars0 + 16 * 8 + 4 <= c["layout"]  # 16 mbarriers + the TMEM address
-    for off in (k0, v0, p0, c["kv"]):
+    bars0 = v0 + V_SLOTS * c["kv"]
+    assert bars0 + 17 * 8 + 4 <= c["layout"]  # 17 mbarriers + the TMEM address
+    for off in (k0, v0, bars0, c["kv"]):
         assert off % 1024 == 0
     # the layout fits after aligning any 256-byte aligned base up to 1024 bytes
     assert all((-base) % 1024 + c["layout"] <= c["smem"] for base in range(0, 4096, 256))
@@ -99,8 +108,6 @@ def test_shared_memory_and_tmem_bounds(D: int, S: int) -> None:
             # the rows a warp's threads write are exactly its store box's rows
             rows = {(sw128_off(r, 8 * b) - b * c["q_box"]) // 128 for r in range(32 * w, 32 * w + 32)}
             assert rows == set(range(32 * w, 32 * w + 32))
-    # P writes: 64 keys = 8 chunks per row, one box
-    assert max(sw128_off(r, ch) for r in range(KM) for ch in range(KN // 8)) + 16 <= c["p"]
     # TMA box destinations of one K or V tile: box b, page pp
     for pp in range(c["pages_per_tile"]):
         for b in range(c["boxes"]):
@@ -120,8 +127,13 @@ def test_shared_memory_and_tmem_bounds(D: int, S: int) -> None:
         assert v_off + (c["boxes"] - 1) * c["kv_box"] + 16 * 128 <= c["kv"]
     # descriptors hold addresses >> 4 in 14 bits: the whole allocation must stay below 256 KB
     assert c["smem"] < (1 << 18)
-    # TMEM: S double-buffered in [0, 64) and [64, 128), O in [128, 128 + D)
+    # TMEM: S double-buffered in [0, 64) and [64, 128), O in [128, 128 + D); P(t) in the
+    # first KN / 2 columns of buffer t % 2 (pairs), the P V MMAs' A operands 8 columns each
     assert 2 * KN <= O_COL and O_COL + D <= TMEM_COLS
+    for sb in range(2):
+        p_cols = range(KN * sb, KN * sb + KN // 2)
+        a_cols = {KN * sb + 8 * kk + c for kk in range(KN // 16) for c in range(8)}
+        assert a_cols == set(p_cols) and max(p_cols) < KN * (sb + 1)
 
 
 @pytest.mark.parametrize("D,S", list(itertools.product((64, 128), (16, 32))))
@@ -197,7 +209,7 @@ class _Barrier:
         return (self.phase & 1) != parity
 
 
-def _simulate(n_tiles: int, seed: int) -> None:
+def _simulate(n_tiles: int, seed: int) -> None:  # noqa: C901
     """The kernel's three roles (load warp, MMA thread, 4 softmax warps) as coroutines over
     mbarriers, with TMA loads and MMAs completing asynchronously in random order. Checks
     that every role finishes (no deadlock) and that no buffer is overwritten before its
@@ -207,7 +219,8 @@ def _simulate(n_tiles: int, seed: int) -> None:
     rnd = random.Random(seed)
     B = {name: _Barrier(4 if name.startswith(("SEmpty", "PFull")) else 1) for name in
          ["KFull0", "KFull1", "KEmpty0", "KEmpty1", "VFull0", "VFull1", "VEmpty0", "VEmpty1",
-          "SFull0", "SFull1", "SEmpty0", "SEmpty1", "PFull", "OFree", "Drain", "QFull"]}
+          "SFull0", "SFull1", "SEmpty0", "SEmpty1", "PFull0", "PFull1", "OFree", "Drain",
+          "QFull"]}
     done = {"K": set(), "V": set(), "S": set(), "PV": set(), "Q": set()}
     s_reads = [0] * max(n_tiles, 1)   # softmax warps that have read S(t)
     p_writes = [0] * max(n_tiles, 1)  # softmax warps that have written their rows of P(t)
@@ -230,7 +243,8 @@ def _simulate(n_tiles: int, seed: int) -> None:
 
     def mma_thread():
         def pv(u):
-            while not (B["PFull"].passed(u & 1) and B["VFull" + str(u % 2)].passed((u // 2) & 1)):
+            while not (B["PFull" + str(u % 2)].passed((u // 2) & 1) and
+                       B["VFull" + str(u % 2)].passed((u // 2) & 1)):
                 yield
             assert p_writes[u] == 4 and u in done["V"]
             issued_mma.append(("PV", u, ["OFree", "VEmpty" + str(u % 2)]))
@@ -262,16 +276,19 @@ def _simulate(n_tiles: int, seed: int) -> None:
             yield  # reading S
             s_reads[j] += 1
             B["SEmpty" + str(j % 2)].arrive()
-            if j > 0:
+            # P(j) goes over S(j) in TMEM buffer j % 2: the P V that read P(j - 2) there
+            # has completed (S(j) was written after it, in issue order)
+            assert j < 2 or (j - 2) in done["PV"]
+            if j > 0 and rnd.random() < 0.3:  # a row's maximum moved: rescale O
                 while not B["OFree"].passed((j - 1) & 1):
                     yield
-                assert (j - 1) in done["PV"]  # P buffer and O free
+                assert (j - 1) in done["PV"]  # O free
             if j == n_tiles - 1:
                 while not B["VFull" + str(j % 2)].passed((j // 2) & 1):
                     yield
                 assert j in done["V"]
             p_writes[j] += 1
-            B["PFull"].arrive()
+            B["PFull" + str(j % 2)].arrive()
         if n_tiles > 0:
             while not B["Drain"].passed(0):
                 yield
